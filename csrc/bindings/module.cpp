@@ -1,0 +1,66 @@
+// module.cpp -- pybind11/torch binding of libgicc (opengda_b200._C).
+// Tensors are validated here; the kernels themselves live in libgicc.so.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "gicc/error.hpp"
+#include "gicc/ops.hpp"
+
+namespace {
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_cuda_bf16(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
+  TORCH_CHECK(t.stride(1) == 1, name, " must be row-major (stride(1) == 1)");
+}
+
+at::Tensor gemm(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tensor> out, double alpha, bool out_f32,
+                int64_t bn) {
+  check_cuda_bf16(A, "A");
+  check_cuda_bf16(B, "B");
+  TORCH_CHECK(A.size(1) == B.size(1), "A[M,K] and B[N,K] must share K");
+  const c10::cuda::CUDAGuard g(A.device());
+  const int64_t M = A.size(0), N = B.size(0), K = A.size(1);
+  at::Tensor C;
+  if (out.has_value()) {
+    C = *out;
+    TORCH_CHECK(C.is_cuda() && C.dim() == 2 && C.size(0) == M && C.size(1) == N && C.stride(1) == 1, "bad out");
+    TORCH_CHECK(C.scalar_type() == (out_f32 ? at::kFloat : at::kBFloat16), "out dtype mismatch");
+  } else {
+    C = at::empty({M, N}, A.options().dtype(out_f32 ? at::kFloat : at::kBFloat16));
+  }
+  gicc::ops::gemm_bf16(A.data_ptr(), B.data_ptr(), C.data_ptr(), (int)M, (int)N, (int)K, A.stride(0), B.stride(0),
+                       C.stride(0), out_f32, (float)alpha, (int)bn, cur_stream());
+  return C;
+}
+
+py::dict read_errors(bool clear) {
+  gicc::ErrorRecord r = gicc::read_error_record(clear);
+  py::dict d;
+  d["code"] = r.code;
+  d["status"] = gicc::status_name(r.code);
+  d["where"] = gicc::where_name(r.where);
+  d["rank"] = r.rank;
+  d["peer"] = r.peer;
+  d["value"] = r.value;
+  d["expected"] = r.expected;
+  d["count"] = r.count;
+  return d;
+}
+
+}  // namespace
+
+void bind_runtime(py::module_& m);  // runtime.cpp
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "opengda_b200 native ops (sm_100a)";
+  m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("out") = py::none(), py::arg("alpha") = 1.0,
+        py::arg("out_f32") = false, py::arg("bn") = 0, "C = alpha * A @ B^T with the tcgen05 GEMM");
+  m.def("read_errors", &read_errors, py::arg("clear") = true, "read (and clear) the device error record");
+  m.def("default_timeout_ns", &gicc::default_timeout_ns);
+  bind_runtime(m);
+}

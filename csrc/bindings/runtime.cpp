@@ -1,0 +1,114 @@
+// runtime.cpp -- binding of the host runtime: Bootstrap (and, below, Runtime/Barrier/AM).
+#include <torch/extension.h>
+
+#include "gicc/bootstrap.hpp"
+
+namespace py = pybind11;
+using gicc::Bootstrap;
+
+namespace {
+
+py::bytes to_bytes(const std::vector<uint8_t>& v) { return py::bytes(reinterpret_cast<const char*>(v.data()), v.size()); }
+
+}  // namespace
+
+void bind_runtime_objects(py::module_& m);  // runtime_objects.cpp
+
+void bind_runtime(py::module_& m) {
+  py::register_exception<gicc::BootstrapError>(m, "BootstrapError", PyExc_RuntimeError);
+
+  py::class_<Bootstrap, std::shared_ptr<Bootstrap>>(m, "Bootstrap")
+      .def(py::init<>(), py::call_guard<py::gil_scoped_release>(), "bootstrap from the environment (blocks for all ranks)")
+      .def(py::init<int, int, const std::string&, double>(), py::arg("rank"), py::arg("size"), py::arg("addr"),
+           py::arg("timeout_s") = -1.0, py::call_guard<py::gil_scoped_release>())
+      .def("setup", &Bootstrap::setup, py::arg("local_rank_hint") = -1, py::arg("local_size_hint") = -1,
+           py::call_guard<py::gil_scoped_release>())
+      .def_property_readonly("rank", &Bootstrap::rank)
+      .def_property_readonly("size", &Bootstrap::size)
+      .def_property_readonly("local_rank", &Bootstrap::local_rank)
+      .def_property_readonly("local_size", &Bootstrap::local_size)
+      .def_property_readonly("server_port", &Bootstrap::server_port)
+      .def_property_readonly("job_id", &Bootstrap::job_id)
+      .def_property_readonly("timeout_s", &Bootstrap::timeout_s)
+      .def("locality_map", &Bootstrap::locality_map)
+      .def("barrier", &Bootstrap::barrier, py::call_guard<py::gil_scoped_release>())
+      .def("allgather",
+           [](Bootstrap& b, py::bytes data) {
+             std::string s = data;
+             std::vector<std::vector<uint8_t>> all;
+             {
+               py::gil_scoped_release rel;
+               all = b.allgather(s.data(), (int)s.size());
+             }
+             py::list out;
+             for (auto& v : all) out.append(to_bytes(v));
+             return out;
+           })
+      .def("broadcast",
+           [](Bootstrap& b, py::object data, int root) {
+             // root passes bytes; every rank receives them (length is broadcast first)
+             std::string s;
+             if (b.rank() == root) s = data.cast<std::string>();
+             uint64_t len = s.size();
+             {
+               py::gil_scoped_release rel;
+               b.broadcast(len, root);
+               s.resize(len);
+               b.broadcast_bytes(&s[0], len, root);
+             }
+             return py::bytes(s);
+           },
+           py::arg("data"), py::arg("root") = 0)
+      .def("send",
+           [](Bootstrap& b, py::bytes data, int dst, int tag) {
+             std::string s = data;
+             py::gil_scoped_release rel;
+             b.send(s.data(), s.size(), dst, tag);
+           },
+           py::arg("data"), py::arg("dst"), py::arg("tag") = 0)
+      .def("recv",
+           [](Bootstrap& b, size_t n, int src, int tag) {
+             std::string s(n, '\0');
+             {
+               py::gil_scoped_release rel;
+               b.recv(&s[0], n, src, tag);
+             }
+             return py::bytes(s);
+           },
+           py::arg("nbytes"), py::arg("src"), py::arg("tag") = 0)
+      .def("sendrecv",
+           [](Bootstrap& b, py::bytes data, int dst, size_t n, int src, int tag) {
+             std::string s = data;
+             std::string r(n, '\0');
+             {
+               py::gil_scoped_release rel;
+               b.sendrecv(s.data(), s.size(), dst, &r[0], n, src, tag);
+             }
+             return py::bytes(r);
+           },
+           py::arg("data"), py::arg("dst"), py::arg("nbytes"), py::arg("src"), py::arg("tag") = 0)
+      .def("wtime", &Bootstrap::wtime)
+      .def("kv_put",
+           [](Bootstrap& b, const std::string& k, py::bytes v) {
+             std::string s = v;
+             py::gil_scoped_release rel;
+             b.kv_put(k, s.data(), s.size());
+           })
+      .def("kv_get",
+           [](Bootstrap& b, const std::string& k, int consume) {
+             std::vector<uint8_t> v;
+             {
+               py::gil_scoped_release rel;
+               v = b.kv_get(k, consume);
+             }
+             return to_bytes(v);
+           },
+           py::arg("key"), py::arg("consume") = 0)
+      .def("check", &Bootstrap::check, py::call_guard<py::gil_scoped_release>())
+      .def("fail_job", &Bootstrap::fail_job, py::call_guard<py::gil_scoped_release>())
+      .def("abort_job", &Bootstrap::abort_job, py::call_guard<py::gil_scoped_release>())
+      .def("send_fds", &Bootstrap::send_fds, py::call_guard<py::gil_scoped_release>())
+      .def("recv_fds", &Bootstrap::recv_fds, py::call_guard<py::gil_scoped_release>());
+
+  bind_runtime_objects(m);
+}

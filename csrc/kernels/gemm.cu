@@ -1,0 +1,131 @@
+// gemm.cu -- single-GPU tcgen05 GEMM (the compute core of every distributed GEMM mode).
+//
+//   C[M,N] = alpha * A[M,K] * B[N,K]^T,  bf16 inputs, f32 accumulation, bf16 or f32 output.
+//
+// Host entry points: gicc::ops::gemm_bf16 (C++, throws) and gicc_gemm_bf16 (C ABI).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "gicc/device/gemm_core.cuh"
+#include "gicc/host_util.hpp"
+#include "gicc/ops.hpp"
+
+namespace gicc {
+namespace gemm {
+
+// Epilogue: row-major bf16/f32 store of alpha * acc.
+struct StoreEpi {
+  static constexpr bool kNeedsTileDone = false;
+  void* C;
+  long long ldc;
+  int M, N;
+  float alpha;
+  int out_f32;
+  __device__ static void fence_before_done() {}
+  __device__ void tile_done(const TileInfo&) {}
+  __device__ void begin_tile(const TileInfo&, int) {}
+  __device__ void end_tile(const TileInfo&, int) {}
+  __device__ __forceinline__ void store(const TileInfo& ti, int row, int c, const uint32_t* r) {
+    const int gm = ti.m0 + row;
+    if (gm >= M) return;
+    const int gn = ti.n0 + c;
+    if (out_f32) {
+      float* p = static_cast<float*>(C) + (size_t)gm * ldc + gn;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (gn + 4 * j + 4 <= N) {
+          uint4 v;
+          v.x = __float_as_uint(alpha * __uint_as_float(r[4 * j + 0]));
+          v.y = __float_as_uint(alpha * __uint_as_float(r[4 * j + 1]));
+          v.z = __float_as_uint(alpha * __uint_as_float(r[4 * j + 2]));
+          v.w = __float_as_uint(alpha * __uint_as_float(r[4 * j + 3]));
+          ptx::st_v4(p + 4 * j, v);
+        }
+      }
+    } else {
+      uint16_t* p = static_cast<uint16_t*>(C) + (size_t)gm * ldc + gn;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (gn + 8 * j + 8 <= N) {
+          uint4 v;
+          v.x = ptx::pack_bf16x2(alpha * __uint_as_float(r[8 * j + 0]), alpha * __uint_as_float(r[8 * j + 1]));
+          v.y = ptx::pack_bf16x2(alpha * __uint_as_float(r[8 * j + 2]), alpha * __uint_as_float(r[8 * j + 3]));
+          v.z = ptx::pack_bf16x2(alpha * __uint_as_float(r[8 * j + 4]), alpha * __uint_as_float(r[8 * j + 5]));
+          v.w = ptx::pack_bf16x2(alpha * __uint_as_float(r[8 * j + 6]), alpha * __uint_as_float(r[8 * j + 7]));
+          ptx::st_v4(p + 8 * j, v);
+        }
+      }
+    }
+  }
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, PlainSched sched,
+                StoreEpi epi, ErrorRecord* err, uint64_t timeout_ns) {
+  gemm_core<BN>(&tmA, &tmB, sched, epi, err, timeout_ns, -1);
+}
+
+template <int BN>
+static void launch_plain(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
+                         long long ldc, bool out_f32, float alpha, cudaStream_t stream) {
+  using Cf = Cfg<BN>;
+  const CUtensorMap tA = make_tmap_2d(A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, lda, BM, BK,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tB = make_tmap_2d(B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldb, BN, BK,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  PlainSched s;
+  s.M = M;
+  s.N = N;
+  s.K = K;
+  s.bn = BN;
+  s.num_m = (M + BM - 1) / BM;
+  s.num_n = (N + BN - 1) / BN;
+  s.group_m = 16;
+  StoreEpi e;
+  e.C = C;
+  e.ldc = ldc;
+  e.M = M;
+  e.N = N;
+  e.alpha = alpha;
+  e.out_f32 = out_f32 ? 1 : 0;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  GICC_CUDA(cudaGetDevice(&dev));
+  if (!attr_set[dev]) {
+    GICC_CUDA(cudaFuncSetAttribute(k_gemm_bf16<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmemBytes));
+    attr_set[dev] = true;
+  }
+  const int tiles = s.num_m * s.num_n;
+  const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
+  k_gemm_bf16<BN><<<grid, kThreads, Cf::kSmemBytes, stream>>>(tA, tB, s, e, device_error_record(),
+                                                               default_timeout_ns());
+  GICC_CUDA(cudaGetLastError());
+}
+
+}  // namespace gemm
+
+namespace ops {
+
+void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
+               long long ldc, bool out_f32, float alpha, int bn, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) throw std::runtime_error("gicc::gemm_bf16: empty shape");
+  if (K % 8 != 0 || lda % 8 != 0 || ldb % 8 != 0)
+    throw std::runtime_error("gicc::gemm_bf16: K and leading dimensions of A/B must be multiples of 8 (16-byte TMA rows)");
+  if (out_f32 ? (N % 4 != 0 || ldc % 4 != 0) : (N % 8 != 0 || ldc % 8 != 0))
+    throw std::runtime_error("gicc::gemm_bf16: N/ldc must allow 16-byte vector stores");
+  if (bn == 0) bn = 256;
+  switch (bn) {
+    case 256: gemm::launch_plain<256>(A, B, C, M, N, K, lda, ldb, ldc, out_f32, alpha, stream); break;
+    case 128: gemm::launch_plain<128>(A, B, C, M, N, K, lda, ldb, ldc, out_f32, alpha, stream); break;
+    default: throw std::runtime_error("gicc::gemm_bf16: bn must be 128 or 256");
+  }
+}
+
+}  // namespace ops
+}  // namespace gicc
+
+GICC_API int gicc_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
+                            long long ldc, int out_f32, float alpha, cudaStream_t stream) {
+  return gicc::guarded([&] { gicc::ops::gemm_bf16(A, B, C, M, N, K, lda, ldb, ldc, out_f32 != 0, alpha, 0, stream); });
+}

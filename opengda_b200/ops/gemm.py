@@ -1,0 +1,25 @@
+"""tcgen05 GEMM: ``C = alpha * A @ B^T`` with A[M,K], B[N,K] bf16 (K-major both)."""
+from __future__ import annotations
+
+import torch
+
+from .. import native
+
+
+def gemm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = None, alpha: float = 1.0,
+         out_dtype: torch.dtype = torch.bfloat16, bn: int = 0) -> torch.Tensor:
+    """Run the persistent warp-specialised tcgen05 GEMM (csrc/kernels/gemm.cu).
+
+    A is [M, K], B is [N, K] (the nn.Linear weight layout); both bf16, row-major.
+    Accumulation is f32 in TMEM; the output is bf16 or f32.
+    """
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("out_dtype must be bfloat16 or float32")
+    return native().gemm(A, B, out, float(alpha), out_dtype == torch.float32, int(bn))
+
+
+def check_errors(clear: bool = True) -> None:
+    """Raise if a kernel of this library recorded a device-side error (timeout, bounds)."""
+    rec = native().read_errors(clear)
+    if rec["code"] != 0:
+        raise RuntimeError(f"gicc device error: {rec}")
