@@ -52,6 +52,25 @@ py::dict read_errors(bool clear) {
   return d;
 }
 
+at::ScalarType dtype_from_name(const std::string& n) {
+  if (n == "bfloat16") return at::kBFloat16;
+  if (n == "float16") return at::kHalf;
+  if (n == "float32") return at::kFloat;
+  if (n == "float64") return at::kDouble;
+  if (n == "int32") return at::kInt;
+  if (n == "int64") return at::kLong;
+  if (n == "uint8") return at::kByte;
+  if (n == "int8") return at::kChar;
+  throw std::runtime_error("tensor_from_ptr: unsupported dtype " + n);
+}
+
+// Zero-copy tensor view of device memory owned elsewhere (symmetric buffers, peer
+// mappings, multicast addresses).  The caller keeps the owner alive.
+at::Tensor tensor_from_ptr(uint64_t ptr, std::vector<int64_t> shape, const std::string& dtype, int device) {
+  auto opts = at::TensorOptions().dtype(dtype_from_name(dtype)).device(at::kCUDA, device);
+  return at::from_blob(reinterpret_cast<void*>(static_cast<uintptr_t>(ptr)), shape, opts);
+}
+
 }  // namespace
 
 void bind_runtime(py::module_& m);  // runtime.cpp
@@ -62,5 +81,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out_f32") = false, py::arg("bn") = 0, "C = alpha * A @ B^T with the tcgen05 GEMM");
   m.def("read_errors", &read_errors, py::arg("clear") = true, "read (and clear) the device error record");
   m.def("default_timeout_ns", &gicc::default_timeout_ns);
+  m.def("tensor_from_ptr", &tensor_from_ptr, py::arg("ptr"), py::arg("shape"), py::arg("dtype"), py::arg("device"));
   bind_runtime(m);
 }

@@ -1,0 +1,136 @@
+// runtime_objects.cpp -- binding of Runtime, Barrier and the communication kernels.
+// Device addresses cross the boundary as Python ints.
+#include <ATen/cuda/CUDAContext.h>
+#include <torch/extension.h>
+
+#include "gicc/barrier.hpp"
+#include "gicc/ops.hpp"
+#include "gicc/runtime.hpp"
+
+namespace py = pybind11;
+using namespace gicc;
+
+namespace {
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+template <class T>
+T* P(uint64_t a) {
+  return reinterpret_cast<T*>(static_cast<uintptr_t>(a));
+}
+uint64_t A(const void* p) { return static_cast<uint64_t>(reinterpret_cast<uintptr_t>(p)); }
+
+py::dict buf_dict(const Buffer& b) {
+  py::dict d;
+  d["ptr"] = A(b.ptr);
+  d["size"] = b.size;
+  d["addr"] = b.addr;
+  d["lkey"] = b.lkey;
+  d["rkey"] = b.rkey;
+  d["index"] = b.index;
+  return d;
+}
+Buffer to_buf(Runtime& rt, int idx) { return rt.buffer(idx); }
+}  // namespace
+
+void bind_runtime_objects(py::module_& m) {
+  py::class_<RuntimeOptions>(m, "RuntimeOptions")
+      .def(py::init<>())
+      .def_readwrite("device", &RuntimeOptions::device)
+      .def_readwrite("signal_heap_bytes", &RuntimeOptions::signal_heap_bytes)
+      .def_readwrite("enable_multicast", &RuntimeOptions::enable_multicast);
+
+  py::class_<Runtime, std::shared_ptr<Runtime>>(m, "Runtime")
+      .def(py::init<>(), py::call_guard<py::gil_scoped_release>())
+      .def(py::init<std::shared_ptr<Bootstrap>, RuntimeOptions>(), py::arg("boot"), py::arg("options") = RuntimeOptions(),
+           py::call_guard<py::gil_scoped_release>())
+      .def("register_buffer",
+           [](Runtime& r, uint64_t ptr, size_t size, bool is_device) {
+             return buf_dict(r.register_buffer(P<void>(ptr), size, is_device));
+           },
+           py::arg("ptr"), py::arg("size"), py::arg("is_device") = true)
+      .def("alloc", [](Runtime& r, size_t n, bool mc) { return buf_dict(r.alloc(n, mc)); }, py::arg("nbytes"),
+           py::arg("multicast") = false)
+      .def("exchange", &Runtime::exchange, py::call_guard<py::gil_scoped_release>())
+      .def("remote_buffer",
+           [](Runtime& r, int rank, int idx) {
+             RemoteBufferInfo i = r.remote_buffer(rank, idx);
+             return py::make_tuple(i.addr, i.rkey);
+           })
+      .def("remote_ptr", [](Runtime& r, int rank, int idx, size_t off) { return A(r.remote_ptr(rank, idx, off)); },
+           py::arg("rank"), py::arg("buf_index"), py::arg("offset") = 0)
+      .def("translate", [](Runtime& r, uint64_t local, int peer) { return A(r.translate(P<void>(local), peer)); })
+      .def("multicast_ptr", [](Runtime& r, int idx) { return A(r.multicast_ptr(idx)); })
+      .def_property_readonly("multicast_supported", &Runtime::multicast_supported)
+      .def("buffer", [](Runtime& r, int idx) { return buf_dict(r.buffer(idx)); })
+      .def_property_readonly("num_buffers", &Runtime::num_buffers)
+      .def("prepare", [](Runtime& r, int peer, int idx) { return A(r.prepare(peer, idx)); }, py::arg("peer") = -1,
+           py::arg("remote_buf_index") = 0)
+      .def("build_context", [](Runtime& r) { return A(r.build_context()); })
+      .def("reset", &Runtime::reset)
+      .def("barrier", &Runtime::barrier, py::call_guard<py::gil_scoped_release>())
+      .def_property_readonly("rank", &Runtime::rank)
+      .def_property_readonly("size", &Runtime::size)
+      .def_property_readonly("gpu_id", &Runtime::gpu_id)
+      .def("clock_rate_khz", &Runtime::clock_rate_khz)
+      .def("gpu_name", [](Runtime& r) { return std::string(r.gpu_name()); })
+      .def("boot", &Runtime::boot_ptr)
+      .def("put_no_db",
+           [](Runtime& r, int src_idx, int dest_rank, int dest_idx, size_t size, size_t src_off, size_t dst_off) {
+             Token t = r.put_no_db(to_buf(r, src_idx), dest_rank, dest_idx, size, src_off, dst_off);
+             return py::make_tuple(t.slot, t.epoch);
+           },
+           py::arg("src_index"), py::arg("dest_rank"), py::arg("dest_index"), py::arg("size"), py::arg("src_off") = 0,
+           py::arg("dst_off") = 0)
+      .def("prepare_trigger", [](Runtime& r, int slot, uint64_t epoch) { return A(r.prepare_trigger(Token{slot, epoch})); })
+      .def("wait", [](Runtime& r, int slot, uint64_t epoch) { r.wait(Token{slot, epoch}); },
+           py::call_guard<py::gil_scoped_release>())
+      .def("signal_alloc", &Runtime::signal_alloc)
+      .def("signal_local", [](Runtime& r, size_t w) { return A(r.signal_local(w)); }, py::arg("word") = 0)
+      .def("signal_peer", [](Runtime& r, int rank, size_t w) { return A(r.signal_peer(rank, w)); }, py::arg("rank"),
+           py::arg("word") = 0)
+      .def("signal_multicast", [](Runtime& r, size_t w) { return A(r.signal_multicast(w)); }, py::arg("word") = 0)
+      .def_property_readonly("timeout_ns", &Runtime::timeout_ns)
+      .def("check_device_errors", &Runtime::check_device_errors, py::arg("clear") = true)
+      .def("finalize", &Runtime::finalize, py::call_guard<py::gil_scoped_release>());
+
+  py::class_<Barrier, std::shared_ptr<Barrier>>(m, "Barrier")
+      .def(py::init<Runtime&, bool>(), py::arg("runtime"), py::arg("nvls") = false, py::keep_alive<1, 2>())
+      .def("init", &Barrier::init)
+      .def("finalize", &Barrier::finalize)
+      .def("setup", &Barrier::setup)
+      .def("wait_completion", &Barrier::wait_completion, py::call_guard<py::gil_scoped_release>())
+      .def("reset", &Barrier::reset)
+      .def("start_continuous", &Barrier::start_continuous)
+      .def("wait_continuous", &Barrier::wait_continuous, py::call_guard<py::gil_scoped_release>())
+      .def("device_ctx", [](Barrier& b) { return A(b.device_ctx()); })
+      .def("count", &Barrier::count)
+      .def_property_readonly("uses_nvls", &Barrier::uses_nvls);
+
+  // ---- communication kernels (enqueued on torch's current stream) ----
+  m.def("k_barrier_single", [](uint64_t ctx, uint64_t flag) { ops::barrier_single(P<BarrierCtx>(ctx), P<uint64_t>(flag), cur_stream()); });
+  m.def("k_barrier_continuous", [](uint64_t ctx, int n, uint64_t counter) {
+    ops::barrier_continuous(P<BarrierCtx>(ctx), n, P<uint64_t>(counter), cur_stream());
+  });
+  m.def("k_copy", [](uint64_t dst, uint64_t src, size_t bytes, int iters, int blocks, int threads) {
+    ops::copy(P<void>(dst), P<const void>(src), bytes, iters, blocks, threads, cur_stream());
+  }, py::arg("dst"), py::arg("src"), py::arg("bytes"), py::arg("iters") = 1, py::arg("blocks") = 0, py::arg("threads") = 0);
+  m.def("k_put_signal", [](uint64_t dst, uint64_t src, size_t bytes, uint64_t sig, int blocks) {
+    ops::put_signal(P<void>(dst), P<const void>(src), bytes, P<uint64_t>(sig), blocks, cur_stream());
+  }, py::arg("dst"), py::arg("src"), py::arg("bytes"), py::arg("sig"), py::arg("blocks") = 0);
+  m.def("k_wait_signal", [](uint64_t sig, int cmp, uint64_t value, uint64_t timeout_ns, uint64_t status) {
+    ops::wait_signal(P<const uint64_t>(sig), cmp, value, timeout_ns, P<int>(status), cur_stream());
+  });
+  m.def("k_signal", [](uint64_t sig, uint64_t value, int op) { ops::signal(P<uint64_t>(sig), value, op, cur_stream()); });
+  m.def("k_pingpong", [](uint64_t rbuf, uint64_t lbuf, size_t bytes, uint64_t rflag, uint64_t lflag, int iters,
+                         bool initiator, uint64_t base, uint64_t out_ns, uint64_t timeout_ns, int rank) {
+    ops::pingpong(P<void>(rbuf), P<const void>(lbuf), bytes, P<uint64_t>(rflag), P<const uint64_t>(lflag), iters,
+                  initiator, base, P<uint64_t>(out_ns), timeout_ns, rank, cur_stream());
+  });
+  m.def("k_quiet_latency", [](uint64_t remote, int iters, uint64_t out_ns) {
+    ops::quiet_latency(P<uint64_t>(remote), iters, P<uint64_t>(out_ns), cur_stream());
+  });
+  m.def("k_flush", [](uint64_t ctx, uint64_t status) { ops::flush_queued(P<DeviceCtx>(ctx), P<int>(status), cur_stream()); });
+  m.def("k_fill_pattern", [](uint64_t buf, size_t n, uint32_t seed) { ops::fill_pattern(P<void>(buf), n, seed, cur_stream()); });
+  m.def("k_check_pattern", [](uint64_t buf, size_t n, uint32_t seed, uint64_t bad) {
+    ops::check_pattern(P<const void>(buf), n, seed, P<unsigned long long>(bad), cur_stream());
+  });
+}

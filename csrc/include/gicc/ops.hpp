@@ -6,6 +6,7 @@
 #include <cstdint>
 
 #include "gicc/host_util.hpp"
+#include "gicc/types.hpp"
 
 namespace gicc {
 namespace ops {
@@ -14,6 +15,24 @@ namespace ops {
 // bn selects the tile width (0 = default 256).
 GICC_EXPORT void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
                            long long ldc, bool out_f32, float alpha, int bn, cudaStream_t stream);
+
+// ---- communication kernels (comm.cu) ------------------------------------------------------
+GICC_EXPORT void barrier_single(BarrierCtx* ctx, uint64_t* flag, cudaStream_t s);
+GICC_EXPORT void barrier_continuous(BarrierCtx* ctx, int n, uint64_t* counter, cudaStream_t s);
+// Grid copy of `bytes`, repeated `iters` times, ending with fence.acq_rel.sys (local or peer memory).
+GICC_EXPORT void copy(void* dst, const void* src, size_t bytes, int iters, int blocks, int threads, cudaStream_t s);
+// Grid put; each block then adds 1 to *sig_remote with release semantics.
+GICC_EXPORT void put_signal(void* dst, const void* src, size_t bytes, uint64_t* sig_remote, int blocks, cudaStream_t s);
+GICC_EXPORT void wait_signal(const uint64_t* sig, int cmp, uint64_t value, uint64_t timeout_ns, int* status,
+                             cudaStream_t s);
+GICC_EXPORT void signal(uint64_t* sig, uint64_t value, int op, cudaStream_t s);
+GICC_EXPORT void pingpong(void* remote_buf, const void* local_buf, size_t bytes, uint64_t* remote_flag,
+                          const uint64_t* local_flag, int iters, bool initiator, uint64_t base, uint64_t* out_ns,
+                          uint64_t timeout_ns, int rank, cudaStream_t s);
+GICC_EXPORT void quiet_latency(uint64_t* remote, int iters, uint64_t* out_ns, cudaStream_t s);
+GICC_EXPORT void flush_queued(DeviceCtx* ctx, int* status, cudaStream_t s);
+GICC_EXPORT void fill_pattern(void* buf, size_t n, uint32_t seed, cudaStream_t s);
+GICC_EXPORT void check_pattern(const void* buf, size_t n, uint32_t seed, unsigned long long* bad, cudaStream_t s);
 
 }  // namespace ops
 }  // namespace gicc

@@ -73,7 +73,7 @@ class GICC_EXPORT Runtime {
   // --- additions ------------------------------------------------------------------------
   // Symmetric allocation, registered under the next index (not collective by itself; all
   // ranks must allocate the same sequence and then call exchange()).
-  Buffer alloc(size_t size, bool multicast = false);
+  Buffer alloc(size_t bytes, bool multicast = false);
   void* remote_ptr(int rank, int buf_index, size_t offset = 0) const;
   void* multicast_ptr(int buf_index) const;  // nullptr when not multicast-bound
   bool multicast_supported() const { return mc_supported_; }

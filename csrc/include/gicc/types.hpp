@@ -88,19 +88,22 @@ struct GiccContext {
 };
 
 // Device barrier context (reference: BarrierCtx, platform/ofi/ofi_barrier_device.cuh:31-45).
-// Signals are monotonically increasing epochs, so nothing is re-armed between barriers.
+// Signals carry monotonically increasing epochs, so nothing is re-armed between barriers.
+// `expected_signal` is the epoch of the next barrier: the host owns it in single mode
+// (Barrier::setup), a continuous-mode kernel owns it and increments it after each
+// barrier() -- the reference's contract (examples/ofi/barrier_test.cpp:32-41).
 struct BarrierCtx {
-  int n_rounds;
+  int n_rounds;                              // ceil(log2(size)); 0 with NVLS or one rank
   int rank;
   int size;
-  int n_signal_slots;                    // 1 (epochs make a second slot unnecessary)
-  uint64_t* signals;                     // [GICC_MAX_ROUNDS] this rank's slots
+  int n_signal_slots;                        // 1 (epochs make a second slot unnecessary)
+  uint64_t* signals;                         // [GICC_MAX_ROUNDS] this rank's slots
   uint64_t* trigger_addrs[GICC_MAX_ROUNDS];  // round k: slot k on rank (rank + 2^k) % size
-  uint64_t* expected_signal;             // device word: epoch of the next barrier
-  uint64_t* done_counter;                // mapped host word: barriers completed
-  uint64_t* ready_counter;               // always-satisfied (no host re-arm on NVLink)
-  uint64_t* mc_counter;                  // NVLS: multicast address of a shared counter (or 0)
-  uint64_t* mc_local;                    // NVLS: this rank's copy of that counter
+  uint64_t expected_signal;                  // epoch of the next barrier
+  uint64_t* done_counter;                    // mapped host word: epoch of the last completed barrier
+  uint64_t* ready_counter;                   // kept for API parity; NVLink needs no host re-arm
+  uint64_t* mc_counter;                      // NVLS: multicast address of a shared arrival counter (or 0)
+  uint64_t* mc_local;                        // NVLS: this rank's copy of that counter
   ErrorRecord* err;
   uint64_t timeout_ns;
 };
