@@ -102,6 +102,7 @@ void bind_runtime_objects(py::module_& m) {
       .def("start_continuous", &Barrier::start_continuous)
       .def("wait_continuous", &Barrier::wait_continuous, py::call_guard<py::gil_scoped_release>())
       .def("device_ctx", [](Barrier& b) { return A(b.device_ctx()); })
+      .def("advance", &Barrier::advance)
       .def("count", &Barrier::count)
       .def_property_readonly("uses_nvls", &Barrier::uses_nvls);
 
@@ -129,6 +130,25 @@ void bind_runtime_objects(py::module_& m) {
     ops::quiet_latency(P<uint64_t>(remote), iters, P<uint64_t>(out_ns), cur_stream());
   });
   m.def("k_flush", [](uint64_t ctx, uint64_t status) { ops::flush_queued(P<DeviceCtx>(ctx), P<int>(status), cur_stream()); });
+  m.def("k_reduce_bf16", [](std::vector<uint64_t> srcs, uint64_t out, size_t count, float scale, bool out_f32) {
+    std::vector<const void*> p;
+    for (auto a : srcs) p.push_back(P<const void>(a));
+    ops::reduce_bf16(p.data(), (int)p.size(), P<void>(out), count, scale, out_f32, cur_stream());
+  });
+  m.def("k_allreduce_bf16", [](int algo, std::vector<uint64_t> in, std::vector<uint64_t> out, uint64_t mc_in,
+                               uint64_t mc_out, int n, int me, size_t count, float scale, bool out_f32,
+                               std::vector<uint64_t> flags, int max_blocks, uint64_t epoch, uint64_t timeout_ns,
+                               int blocks) {
+    std::vector<const void*> ip;
+    std::vector<void*> op;
+    std::vector<uint64_t*> fp;
+    for (auto a : in) ip.push_back(P<const void>(a));
+    for (auto a : out) op.push_back(P<void>(a));
+    for (auto a : flags) fp.push_back(P<uint64_t>(a));
+    ops::allreduce_bf16(algo, ip.empty() ? nullptr : ip.data(), op.empty() ? nullptr : op.data(), P<const void>(mc_in),
+                        P<void>(mc_out), n, me, count, scale, out_f32, fp.data(), max_blocks, epoch, timeout_ns, blocks,
+                        cur_stream());
+  });
   m.def("k_fill_pattern", [](uint64_t buf, size_t n, uint32_t seed) { ops::fill_pattern(P<void>(buf), n, seed, cur_stream()); });
   m.def("k_check_pattern", [](uint64_t buf, size_t n, uint32_t seed, uint64_t bad) {
     ops::check_pattern(P<const void>(buf), n, seed, P<unsigned long long>(bad), cur_stream());

@@ -29,6 +29,9 @@ class GICC_EXPORT Barrier {
   void start_continuous(uint64_t n);   // hand the epoch to a kernel that runs n barriers
   void wait_continuous();              // host wait (bounded) until those n completed
   BarrierCtx* device_ctx() const { return dctx_; }
+  // Record that n barriers were enqueued by stream-ordered kernels that advance the
+  // device epoch themselves (ops::barrier_continuous); no device memory is touched.
+  void advance(uint64_t n);
   uint64_t count() const;              // barriers completed on this rank
   bool uses_nvls() const { return nvls_; }
 

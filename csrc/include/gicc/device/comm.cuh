@@ -269,7 +269,8 @@ __device__ __forceinline__ int barrier(BarrierCtx* ctx) {
     report_error(ctx->err, st, W_BARRIER, ctx->rank, -1, seen, epoch);
     return st;
   }
-  ptx::st_release_sys(ctx->done_counter, epoch);
+  // progress report for the host (plain posted store into mapped host memory)
+  *reinterpret_cast<volatile uint64_t*>(ctx->done_counter) = epoch;
   return GICC_OK;
 }
 

@@ -34,5 +34,17 @@ GICC_EXPORT void flush_queued(DeviceCtx* ctx, int* status, cudaStream_t s);
 GICC_EXPORT void fill_pattern(void* buf, size_t n, uint32_t seed, cudaStream_t s);
 GICC_EXPORT void check_pattern(const void* buf, size_t n, uint32_t seed, unsigned long long* bad, cudaStream_t s);
 
+// ---- collectives (collectives.cu) ---------------------------------------------------------
+enum AllreduceAlgo : int { ALLREDUCE_ONESHOT = 0, ALLREDUCE_TWOSHOT = 1, ALLREDUCE_NVLS = 2 };
+// out = scale * sum_i srcs[i] over `count` bf16 elements (f32 accumulation); srcs may be peer memory.
+GICC_EXPORT void reduce_bf16(const void* const* srcs, int nsrc, void* out, size_t count, float scale, bool out_f32,
+                             cudaStream_t s);
+// Allreduce of `count` bf16 elements held in symmetric memory.  in/out: per-rank addresses
+// (this process's view); mc_in/mc_out: multicast addresses (NVLS only); flag_bases: per-rank
+// base of a [2][max_blocks][n] signal-word area; epoch: call counter (same on all ranks).
+GICC_EXPORT void allreduce_bf16(int algo, const void* const* in, void* const* out, const void* mc_in, void* mc_out,
+                                int n, int me, size_t count, float scale, bool out_f32, uint64_t* const* flag_bases,
+                                int max_blocks, uint64_t epoch, uint64_t timeout_ns, int blocks, cudaStream_t s);
+
 }  // namespace ops
 }  // namespace gicc

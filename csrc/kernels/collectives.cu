@@ -1,0 +1,235 @@
+// collectives.cu -- allreduce (one-shot, two-shot, NVLS) fused with scale/cast, and a
+// multi-source reduction used by GEMM->reduce-scatter.
+//
+// None of these exists in the reference (its only reduction is the host scalar
+// coll::allreduce_sum over MPI, src/gicc/coll.hpp:15-21).  Design:
+//   * inputs live in symmetric memory, so every rank reads its peers' data directly;
+//   * no separate barrier kernel: every CTA does an entry and an exit handshake with
+//     the CTA of the same index on every peer (epoch-valued flags in the signal heap,
+//     release stores / acquire polls, bounded by %globaltimer).  CTA b of every rank
+//     touches the same element range, so the pairwise handshake is all that is needed;
+//   * bf16 data is summed in f32 registers, scaled, and written as bf16 or f32;
+//   * NVLS: multimem.ld_reduce sums all ranks' copies inside the NVSwitch, multimem.st
+//     broadcasts the result -- each GPU moves 1/n of the bytes once in each direction.
+#include <cuda_runtime.h>
+
+#include "gicc/device/comm.cuh"
+#include "gicc/host_util.hpp"
+#include "gicc/ops.hpp"
+
+namespace gicc {
+namespace {
+
+constexpr int kMaxRanks = 16;
+
+struct PeerPtrs {
+  const void* p[kMaxRanks];
+};
+struct PeerOut {
+  void* p[kMaxRanks];
+};
+struct FlagPtrs {
+  uint64_t* p[kMaxRanks];  // each rank's flag area base (this rank's view)
+};
+
+__device__ __forceinline__ void add_bf16x8(float* acc, const uint4& v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    acc[2 * j] += ptx::bf16_lo(w[j]);
+    acc[2 * j + 1] += ptx::bf16_hi(w[j]);
+  }
+}
+
+__device__ __forceinline__ void store8(void* out, size_t vec, const float* acc, float scale, int out_f32) {
+  if (out_f32) {
+    float4* o = reinterpret_cast<float4*>(out) + 2 * vec;
+    o[0] = make_float4(acc[0] * scale, acc[1] * scale, acc[2] * scale, acc[3] * scale);
+    o[1] = make_float4(acc[4] * scale, acc[5] * scale, acc[6] * scale, acc[7] * scale);
+  } else {
+    uint4 r;
+    r.x = ptx::pack_bf16x2(acc[0] * scale, acc[1] * scale);
+    r.y = ptx::pack_bf16x2(acc[2] * scale, acc[3] * scale);
+    r.z = ptx::pack_bf16x2(acc[4] * scale, acc[5] * scale);
+    r.w = ptx::pack_bf16x2(acc[6] * scale, acc[7] * scale);
+    reinterpret_cast<uint4*>(out)[vec] = r;
+  }
+}
+
+// Pairwise handshake of CTA `blockIdx.x` with the same CTA on every peer.
+// flags layout (per rank): [phase][block][src] words.
+__device__ __forceinline__ int cta_handshake(const FlagPtrs& flags, int n, int me, int phase, int max_blocks,
+                                             uint64_t epoch, uint64_t timeout_ns, ErrorRecord* err) {
+  __shared__ int st;
+  ptx::fence_acq_rel_sys();
+  __syncthreads();
+  if (threadIdx.x == 0) st = GICC_OK;
+  __syncthreads();
+  const size_t slot = ((size_t)phase * max_blocks + blockIdx.x) * n;
+  const int t = threadIdx.x;
+  if (t < n && t != me) {
+    ptx::st_release_sys(flags.p[t] + slot + me, epoch);
+    uint64_t seen = 0;
+    if (!proto::wait_until<proto::DevMem>(flags.p[me] + slot + t, proto::CMP_GE, epoch, timeout_ns, &seen)) {
+      report_error(err, GICC_ETIMEDOUT, W_ALLREDUCE, me, t, seen, epoch);
+      st = GICC_ETIMEDOUT;
+    }
+  }
+  __syncthreads();
+  return st;
+}
+
+// One-shot: every rank reads all inputs and writes the whole result locally.
+__global__ void __launch_bounds__(512) k_allreduce_oneshot(PeerPtrs in, void* out, size_t nvec, int n, int me,
+                                                           float scale, int out_f32, FlagPtrs flags, int max_blocks,
+                                                           uint64_t epoch, uint64_t timeout_ns, ErrorRecord* err) {
+  if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) != GICC_OK) return;
+  for (size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += (size_t)gridDim.x * blockDim.x) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    uint4 x[kMaxRanks];
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p)
+      if (p < n) x[p] = reinterpret_cast<const uint4*>(in.p[p])[v];  // fixed order: same sum on every rank
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p)
+      if (p < n) add_bf16x8(acc, x[p]);
+    store8(out, v, acc, scale, out_f32);
+  }
+  cta_handshake(flags, n, me, 1, max_blocks, epoch, timeout_ns, err);
+}
+
+// Two-shot: rank r reduces chunk r from all inputs and pushes it into every rank's output.
+__global__ void __launch_bounds__(512) k_allreduce_twoshot(PeerPtrs in, PeerOut out, size_t nvec, int n, int me,
+                                                           float scale, int out_f32, FlagPtrs flags, int max_blocks,
+                                                           uint64_t epoch, uint64_t timeout_ns, ErrorRecord* err) {
+  if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) != GICC_OK) return;
+  const size_t per = (nvec + n - 1) / n;
+  const size_t lo = per * me, hi = lo + per < nvec ? lo + per : nvec;
+  for (size_t v = lo + (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < hi; v += (size_t)gridDim.x * blockDim.x) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    uint4 x[kMaxRanks];
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p)
+      if (p < n) x[p] = reinterpret_cast<const uint4*>(in.p[p])[v];  // fixed order: same sum on every rank
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p)
+      if (p < n) add_bf16x8(acc, x[p]);
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p)
+      if (p < n) store8(out.p[(me + p) % n], v, acc, scale, out_f32);
+  }
+  cta_handshake(flags, n, me, 1, max_blocks, epoch, timeout_ns, err);
+}
+
+// NVLS: rank r reduces chunk r inside the switch and multicasts the result.
+__global__ void __launch_bounds__(512) k_allreduce_nvls(const void* mc_in, void* mc_out, size_t nvec, int n, int me,
+                                                        float scale, int out_f32, FlagPtrs flags, int max_blocks,
+                                                        uint64_t epoch, uint64_t timeout_ns, ErrorRecord* err) {
+  if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) != GICC_OK) return;
+  const size_t per = (nvec + n - 1) / n;
+  const size_t lo = per * me, hi = lo + per < nvec ? lo + per : nvec;
+  for (size_t v = lo + (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < hi; v += (size_t)gridDim.x * blockDim.x) {
+    const uint4 s = ptx::multimem_ld_reduce_bf16x8(reinterpret_cast<const uint4*>(mc_in) + v);
+    if (out_f32) {
+      float acc[8];
+      const uint32_t w[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] = ptx::bf16_lo(w[j]) * scale;
+        acc[2 * j + 1] = ptx::bf16_hi(w[j]) * scale;
+      }
+      uint4* o = reinterpret_cast<uint4*>(mc_out) + 2 * v;
+      ptx::multimem_st_v4(o, make_uint4(__float_as_uint(acc[0]), __float_as_uint(acc[1]), __float_as_uint(acc[2]),
+                                        __float_as_uint(acc[3])));
+      ptx::multimem_st_v4(o + 1, make_uint4(__float_as_uint(acc[4]), __float_as_uint(acc[5]), __float_as_uint(acc[6]),
+                                            __float_as_uint(acc[7])));
+    } else {
+      uint4 r = s;
+      if (scale != 1.0f) {
+        const uint32_t w[4] = {s.x, s.y, s.z, s.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = ptx::pack_bf16x2(ptx::bf16_lo(w[j]) * scale, ptx::bf16_hi(w[j]) * scale);
+        r = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      ptx::multimem_st_v4(reinterpret_cast<uint4*>(mc_out) + v, r);
+    }
+  }
+  cta_handshake(flags, n, me, 1, max_blocks, epoch, timeout_ns, err);
+}
+
+// Plain multi-source reduction (callers order it with barriers): out = scale * sum(src).
+__global__ void __launch_bounds__(512) k_reduce(PeerPtrs src, int nsrc, void* out, size_t nvec, float scale,
+                                                int out_f32) {
+  for (size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += (size_t)gridDim.x * blockDim.x) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    uint4 x[kMaxRanks];
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p)
+      if (p < nsrc) x[p] = reinterpret_cast<const uint4*>(src.p[p])[v];
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p)
+      if (p < nsrc) add_bf16x8(acc, x[p]);
+    store8(out, v, acc, scale, out_f32);
+  }
+}
+
+}  // namespace
+
+namespace ops {
+
+void reduce_bf16(const void* const* srcs, int nsrc, void* out, size_t count, float scale, bool out_f32,
+                 cudaStream_t s) {
+  if (nsrc < 1 || nsrc > kMaxRanks) throw std::runtime_error("gicc::reduce_bf16: 1..16 sources");
+  if (count % 8) throw std::runtime_error("gicc::reduce_bf16: count must be a multiple of 8");
+  PeerPtrs p{};
+  for (int i = 0; i < nsrc; ++i) {
+    if (reinterpret_cast<uintptr_t>(srcs[i]) & 15) throw std::runtime_error("gicc::reduce_bf16: unaligned source");
+    p.p[i] = srcs[i];
+  }
+  const size_t nvec = count / 8;
+  int blocks = (int)std::min<size_t>((nvec + 511) / 512, 4 * (size_t)num_sms());
+  k_reduce<<<blocks, 512, 0, s>>>(p, nsrc, out, nvec, scale, out_f32 ? 1 : 0);
+  GICC_CUDA(cudaGetLastError());
+}
+
+void allreduce_bf16(int algo, const void* const* in, void* const* out, const void* mc_in, void* mc_out, int n, int me,
+                    size_t count, float scale, bool out_f32, uint64_t* const* flag_bases, int max_blocks,
+                    uint64_t epoch, uint64_t timeout_ns, int blocks, cudaStream_t s) {
+  if (n < 1 || n > kMaxRanks) throw std::runtime_error("gicc::allreduce: 1..16 ranks");
+  if (count % 8) throw std::runtime_error("gicc::allreduce: element count must be a multiple of 8");
+  const size_t nvec = count / 8;
+  PeerPtrs ip{};
+  PeerOut op{};
+  FlagPtrs fp{};
+  for (int i = 0; i < n; ++i) {
+    ip.p[i] = in ? in[i] : nullptr;
+    op.p[i] = out ? out[i] : nullptr;
+    fp.p[i] = flag_bases[i];
+  }
+  const size_t work = algo == ALLREDUCE_ONESHOT ? nvec : (nvec + n - 1) / n;
+  if (blocks <= 0) blocks = (int)std::min<size_t>(std::max<size_t>((work + 511) / 512, 1), 2 * (size_t)num_sms());
+  if (blocks > max_blocks) blocks = max_blocks;
+  ErrorRecord* err = device_error_record();
+  switch (algo) {
+    case ALLREDUCE_ONESHOT:
+      k_allreduce_oneshot<<<blocks, 512, 0, s>>>(ip, op.p[me], nvec, n, me, scale, out_f32, fp, max_blocks, epoch,
+                                                 timeout_ns, err);
+      break;
+    case ALLREDUCE_TWOSHOT:
+      k_allreduce_twoshot<<<blocks, 512, 0, s>>>(ip, op, nvec, n, me, scale, out_f32, fp, max_blocks, epoch,
+                                                 timeout_ns, err);
+      break;
+    case ALLREDUCE_NVLS:
+      if (!mc_in || !mc_out) throw std::runtime_error("gicc::allreduce: NVLS needs multicast-bound buffers");
+      k_allreduce_nvls<<<blocks, 512, 0, s>>>(mc_in, mc_out, nvec, n, me, scale, out_f32, fp, max_blocks, epoch,
+                                              timeout_ns, err);
+      break;
+    default:
+      throw std::runtime_error("gicc::allreduce: unknown algorithm");
+  }
+  GICC_CUDA(cudaGetLastError());
+}
+
+}  // namespace ops
+}  // namespace gicc

@@ -16,7 +16,9 @@ namespace {
 
 __global__ void k_barrier_single(BarrierCtx* ctx, uint64_t* flag) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  if (barrier(ctx) == GICC_OK && flag) *reinterpret_cast<volatile uint64_t*>(flag) = 42;
+  if (barrier(ctx) != GICC_OK) return;
+  ctx->expected_signal++;  // stream-ordered use needs no host re-arm; setup() may still set it
+  if (flag) *reinterpret_cast<volatile uint64_t*>(flag) = 42;
 }
 
 __global__ void k_barrier_continuous(BarrierCtx* ctx, int n, uint64_t* counter) {

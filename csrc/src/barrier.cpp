@@ -31,7 +31,7 @@ Barrier::Barrier(Runtime& rt, bool nvls) : rt_(rt) {
     c.n_rounds = rounds;
     for (int k = 0; k < rounds; ++k) c.trigger_addrs[k] = rt.signal_peer((me + (1 << k)) % n, off + k);
   }
-  c.expected_signal = 0;
+  c.expected_signal = 1;  // epoch of the first barrier
   void* h = nullptr;
   GICC_CUDA(cudaHostAlloc(&h, 2 * sizeof(uint64_t), cudaHostAllocMapped));
   std::memset(h, 0, 2 * sizeof(uint64_t));
@@ -74,6 +74,11 @@ void Barrier::setup() {
 void Barrier::start_continuous(uint64_t n) {
   const uint64_t first = epoch_ + 1;
   GICC_CUDA(cudaMemcpy(&dctx_->expected_signal, &first, sizeof(first), cudaMemcpyHostToDevice));
+  epoch_ += n;
+  target_ = epoch_;
+}
+
+void Barrier::advance(uint64_t n) {
   epoch_ += n;
   target_ = epoch_;
 }

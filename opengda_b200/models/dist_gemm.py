@@ -1,19 +1,131 @@
-"""Distributed GEMM workload (placeholder: single-GPU path; modes added next)."""
+"""Distributed GEMM: bf16 in / f32 accumulate, C = A . B.
+
+Two modes, both over the NVLink symmetric-memory runtime (no NCCL on this path):
+
+* ``ag`` -- all-gather -> GEMM.  A [M, K] is row-sharded (rank r owns rows
+  r*M/w ... (r+1)*M/w), B is column-sharded (rank r owns output columns r*N/w ...),
+  stored as B^T rows [N/w, K] (the weight layout of nn.Linear).  Each rank computes
+  C[:, cols_r] = A_full @ B_r^T.
+* ``rs`` -- GEMM -> reduce-scatter.  K is sharded: rank r owns A[:, k_r] and B[:, k_r];
+  partial products are summed across ranks and rank r keeps rows r*M/w ... of C.
+
+With one GPU both reduce to the single tcgen05 GEMM.  The reference's version of this
+workload is the striped fp32 ring matmul of examples/gicc/mm.cu:116-225 (B stripes
+rotated around the ring while a SIMT kernel accumulates with atomicAdd).
+"""
 from __future__ import annotations
+
+from typing import Optional
 
 import torch
 
+from ..ops.gemm import gemm
+
+
+class DistGemm:
+    def __init__(self, M: int, N: int, K: int, mode: str = "ag", rt=None, device: Optional[torch.device] = None):
+        self.M, self.N, self.K, self.mode = M, N, K, mode
+        self.rt = rt
+        self.world = rt.size if rt is not None else 1
+        self.rank = rt.rank if rt is not None else 0
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        w = self.world
+        if mode not in ("ag", "rs"):
+            raise ValueError("mode must be 'ag' or 'rs'")
+        if M % w or N % w or K % w:
+            raise ValueError("M, N and K must be divisible by the number of ranks")
+        self.launches_per_step = 1
+        if w > 1:
+            from ..ops import collectives
+            from ..parallel import Barrier
+
+            self._coll = collectives
+            self.barrier = Barrier(rt)
+            if mode == "ag":
+                self.A_full = rt.alloc_tensor((M, K), torch.bfloat16)
+                self.C = torch.empty(M, N // w, dtype=torch.bfloat16, device=self.device)
+                self.launches_per_step = 2 + (w - 1) + 1
+            else:
+                self.P = rt.alloc_tensor((M, N), torch.bfloat16)  # bf16 partials, f32 reduction
+                self.C = torch.empty(M // w, N, dtype=torch.bfloat16, device=self.device)
+                self.launches_per_step = 1 + 2 + 1
+
+    # shapes of this rank's operands
+    def a_shape(self):
+        w = self.world
+        return (self.M // w, self.K) if self.mode == "ag" else (self.M, self.K // w)
+
+    def b_shape(self):
+        w = self.world
+        return (self.N // w, self.K) if self.mode == "ag" else (self.N, self.K // w)
+
+    def out_shape(self):
+        w = self.world
+        return (self.M, self.N // w) if self.mode == "ag" else (self.M // w, self.N)
+
+    def a_slot(self) -> torch.Tensor:
+        """Where this rank's A shard must live for the AG mode (zero-copy input)."""
+        Ms = self.M // self.world
+        return self.A_full.local[self.rank * Ms:(self.rank + 1) * Ms]
+
+    def forward(self, A: torch.Tensor, B: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        w, r = self.world, self.rank
+        if w == 1:
+            return gemm(A, B, out=out)
+        if self.mode == "ag":
+            Ms = self.M // w
+            slot = self.a_slot()
+            if A.data_ptr() != slot.data_ptr():
+                slot.copy_(A)
+            self.barrier.device_barrier()  # every shard is in place
+            row_bytes = self.K * 2
+            for k in range(1, w):
+                p = (r + k) % w
+                off = p * Ms * row_bytes
+                self._coll.copy(self.A_full.ptr() + off, self.A_full.ptr(p) + off, Ms * row_bytes)
+            C = gemm(self.A_full.local, B, out=out if out is not None else self.C)
+            self.barrier.device_barrier()  # peers finished reading our shard
+            return C
+        # rs: partial product, then each rank reduces its row block from all peers
+        gemm(A, B, out=self.P.local)
+        self.barrier.device_barrier()
+        Mr = self.M // w
+        C = out if out is not None else self.C
+        srcs = [self.P.ptr(p) + r * Mr * self.N * 2 for p in range(w)]
+        self._coll.reduce_sum(C, srcs, Mr * self.N)
+        self.barrier.device_barrier()
+        return C
+
+    __call__ = forward
+
+
+def make_operands(M: int, N: int, K: int, mode: str, world: int, rank: int, seed: int = 2,
+                  device: Optional[torch.device] = None):
+    """Synthetic A, B ~ N(0, sigma^2) with sigma^2 = 1/sqrt(K) (so C has unit variance),
+    generated identically on every rank from `seed`; returns this rank's shards."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=device).manual_seed(seed)
+    std = K ** -0.25
+    A = (torch.randn(M, K, generator=g, device=device) * std).to(torch.bfloat16)
+    B = (torch.randn(N, K, generator=g, device=device) * std).to(torch.bfloat16)  # B^T layout
+    if mode == "ag":
+        Ms, Ns = M // world, N // world
+        return A[rank * Ms:(rank + 1) * Ms].contiguous(), B[rank * Ns:(rank + 1) * Ns].contiguous(), (A, B)
+    Ks = K // world
+    return A[:, rank * Ks:(rank + 1) * Ks].contiguous(), B[:, rank * Ks:(rank + 1) * Ks].contiguous(), (A, B)
+
 
 def smoke_step(device: torch.device) -> None:
-    from ..ops.gemm import gemm, check_errors
+    """One tiny forward through the flagship path on one GPU, checked against fp32."""
+    from ..ops.gemm import check_errors
 
-    g = torch.Generator(device=device).manual_seed(2)
-    A = torch.randn(256, 512, device=device, generator=g).to(torch.bfloat16)
-    B = torch.randn(256, 512, device=device, generator=g).to(torch.bfloat16)
-    C = gemm(A, B)
+    torch.cuda.set_device(device)
+    model = DistGemm(256, 512, 384, "ag", rt=None, device=device)
+    A, B, (Af, Bf) = make_operands(256, 512, 384, "ag", 1, 0, device=device)
+    C = model(A, B)
     torch.cuda.synchronize(device)
     check_errors()
-    ref = A.float() @ B.float().t()
+    ref = Af.float() @ Bf.float().t()
     err = (C.float() - ref).abs().max().item()
-    if err > 1e-2 * ref.abs().max().item() + 1e-2:
-        raise RuntimeError(f"smoke: GEMM mismatch {err}")
+    if not err <= 2e-2 * ref.abs().max().item() + 1e-2:
+        raise RuntimeError(f"smoke: distributed GEMM mismatch (max abs err {err})")

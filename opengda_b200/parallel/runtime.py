@@ -216,6 +216,12 @@ class Barrier:
         self._b.setup()
         native().k_barrier_single(self._b.device_ctx(), flag_ptr)
 
+    def device_barrier(self, n: int = 1) -> None:
+        """Enqueue n barriers on the current stream; the kernel advances the epoch itself,
+        so no host memory copy is involved (CUDA-graph capturable)."""
+        self._b.advance(n)
+        native().k_barrier_continuous(self._b.device_ctx(), n, 0)
+
     def run_continuous(self, n: int, counter_ptr: int = 0) -> None:
         """start_continuous(n) + one kernel running n barriers (barrier_test.cpp:32-41)."""
         self._b.start_continuous(n)

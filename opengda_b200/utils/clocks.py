@@ -1,0 +1,68 @@
+"""Sample SM clocks / throttle reasons with nvidia-smi while a timed region runs."""
+from __future__ import annotations
+
+import shutil
+import statistics
+import subprocess
+import tempfile
+from typing import List, Optional
+
+QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+
+class ClockSampler:
+    """``with ClockSampler(gpus) as cs: ...`` then ``cs.summary()``."""
+
+    def __init__(self, gpus: Optional[List[int]] = None, period_ms: int = 200):
+        self.gpus = gpus
+        self.period_ms = period_ms
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        if shutil.which("nvidia-smi") is None:
+            return self
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        cmd = ["nvidia-smi", f"--query-gpu={QUERY}", "--format=csv,noheader,nounits", f"-lms={self.period_ms}"]
+        if self.gpus is not None:
+            cmd.insert(1, "-i=" + ",".join(str(g) for g in self.gpus))
+        self.proc = subprocess.Popen(cmd, stdout=self.file, stderr=subprocess.DEVNULL)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self) -> dict:
+        if self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append((int(parts[0]), float(parts[1]), float(parts[2]), parts[3], parts[5:9]))
+                except ValueError:
+                    continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        mx = max(r[2] for r in rows)
+        loaded = [r for r in rows if r[1] > 0.3 * mx] or rows
+        reasons = set()
+        for r in loaded:
+            for name, v in zip(REASONS, r[4]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r[1] for r in loaded), "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(rows)}

@@ -1,0 +1,131 @@
+"""Rank program for the multi-GPU tests (one process per GPU, launched by
+opengda_b200.parallel.launch).  Writes a JSON result per rank."""
+import json
+import os
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+from opengda_b200 import native  # noqa: E402
+from opengda_b200.parallel import Barrier, Bootstrap, Runtime  # noqa: E402
+
+
+def main():
+    out = sys.argv[1]
+    boot = Bootstrap.from_env()
+    rt = Runtime(boot)
+    r, n = rt.rank, rt.size
+    N = native()
+    res = {"rank": r, "gpu": rt.gpu_id, "nvls": rt.multicast_supported}
+    right, left = (r + 1) % n, (r - 1) % n
+
+    # 1. puts into the right neighbour with a per-rank pattern, verified by the receiver
+    buf = rt.alloc_tensor((1 << 22,), torch.uint8)
+    src = torch.empty(1 << 22, dtype=torch.uint8, device="cuda")
+    N.k_fill_pattern(src.data_ptr(), 1 << 22, 100 + r)
+    bar = Barrier(rt)
+    torch.cuda.synchronize()
+    bar.device_barrier()
+    N.k_copy(buf.ptr(right), src.data_ptr(), 1 << 22)
+    bar.device_barrier()
+    bad = torch.zeros(1, dtype=torch.int64, device="cuda")
+    N.k_check_pattern(buf.ptr(), 1 << 22, 100 + left, bad.data_ptr())
+    torch.cuda.synchronize()
+    res["put_bad_bytes"] = int(bad.item())
+
+    # 2. get: read the left neighbour's buffer (it holds left-left's pattern)
+    dst = torch.zeros(1 << 22, dtype=torch.uint8, device="cuda")
+    N.k_copy(dst.data_ptr(), buf.ptr(left), 1 << 22)
+    bad.zero_()
+    N.k_check_pattern(dst.data_ptr(), 1 << 22, 100 + (left - 1) % n, bad.data_ptr())
+    bar.device_barrier()
+    torch.cuda.synchronize()
+    res["get_bad_bytes"] = int(bad.item())
+
+    # 3. host-queued put_no_db to the right neighbour, flushed on the device
+    qsrc = rt.alloc_tensor((1 << 16,), torch.uint8)
+    qdst = rt.alloc_tensor((1 << 16,), torch.uint8)
+    N.k_fill_pattern(qsrc.ptr(), 1 << 16, 7 + r)
+    torch.cuda.synchronize()
+    rt.reset()
+    tok = rt.put_no_db(qsrc.index, right, qdst.index, 1 << 16)
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    N.k_flush(rt.prepare_trigger(tok), st.data_ptr())
+    rt.wait(tok)
+    bar.device_barrier()
+    bad.zero_()
+    N.k_check_pattern(qdst.ptr(), 1 << 16, 7 + left, bad.data_ptr())
+    torch.cuda.synchronize()
+    res["queued_bad_bytes"] = int(bad.item()) + int(st.item())
+
+    # 4. barriers: single (reference-style setup/wait) and continuous 10000
+    flag = torch.zeros(1, dtype=torch.int64, device="cuda")
+    bar.run_single(flag.data_ptr())
+    bar.wait_completion()
+    torch.cuda.synchronize()
+    res["single_flag"] = int(flag.item())
+    cnt = torch.zeros(1, dtype=torch.int64, device="cuda")
+    nb = 10000
+    torch.cuda.synchronize()
+    boot.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    bar.run_continuous(nb, cnt.data_ptr())
+    e.record()
+    bar.wait_continuous()
+    torch.cuda.synchronize()
+    res["continuous_count"] = int(cnt.item())
+    res["barrier_us"] = s.elapsed_time(e) * 1e3 / nb
+    if rt.multicast_supported:
+        bn = Barrier(rt, nvls=True)
+        boot.barrier()
+        s.record()
+        bn.run_continuous(nb, cnt.data_ptr())
+        e.record()
+        bn.wait_continuous()
+        torch.cuda.synchronize()
+        res["nvls_barrier_us"] = s.elapsed_time(e) * 1e3 / nb
+        res["nvls_continuous_count"] = int(cnt.item())
+
+    # 5. allreduce, every algorithm, against a torch fp32 reference
+    from opengda_b200.ops.collectives import Allreduce
+    ar = Allreduce(rt, 1 << 20)
+    errs = {}
+    for algo in (["oneshot", "twoshot"] + (["nvls"] if rt.multicast_supported else [])):
+        for count in (1024, 65536, 1 << 20):
+            g = torch.Generator(device="cuda").manual_seed(1000 + count)
+            allx = [torch.randn(count, generator=g, device="cuda").to(torch.bfloat16) for _ in range(n)]
+            ar.input(count).copy_(allx[r])
+            y = ar(count, algo=algo, scale=0.5)
+            torch.cuda.synchronize()
+            ref = 0.5 * torch.stack([x.float() for x in allx]).sum(0)
+            errs[f"{algo}_{count}"] = float((y.float() - ref).abs().max().item())
+            boot.barrier()
+    res["allreduce_maxerr"] = errs
+
+    # 6. distributed GEMM, both modes, small shape vs fp32
+    from opengda_b200.models.dist_gemm import DistGemm, make_operands
+    for mode in ("ag", "rs"):
+        M = Nn = K = 1024
+        model = DistGemm(M, Nn, K, mode, rt=rt)
+        A, B, (Af, Bf) = make_operands(M, Nn, K, mode, n, r, seed=2)
+        C = model(A, B)
+        torch.cuda.synchronize()
+        full = Af.float() @ Bf.float().t()
+        ref = full[:, r * Nn // n:(r + 1) * Nn // n] if mode == "ag" else full[r * M // n:(r + 1) * M // n]
+        res[f"gemm_{mode}_relerr"] = float(((C.float() - ref).norm() / ref.norm()).item())
+    rt.check_device_errors()
+    torch.cuda.synchronize()
+    boot.barrier()
+    with open(f"{out}.{r}", "w") as f:
+        json.dump(res, f)
+    del ar
+    rt.finalize()
+
+
+if __name__ == "__main__":
+    main()
