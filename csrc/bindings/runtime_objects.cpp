@@ -149,6 +149,31 @@ void bind_runtime_objects(py::module_& m) {
                         P<void>(mc_out), n, me, count, scale, out_f32, fp.data(), max_blocks, epoch, timeout_ns, blocks,
                         cur_stream());
   });
+  m.def("k_jacobi_init", [](uint64_t a, uint64_t b, int nx, int ny, int rows, int g0, uint64_t seed) {
+    ops::jacobi_init(P<float>(a), P<float>(b), nx, ny, rows, g0, seed, cur_stream());
+  });
+  m.def("k_jacobi_step", [](uint64_t a, uint64_t b, int nx, int rows, uint64_t top_dst, uint64_t bot_dst,
+                            uint64_t top_sig_remote, uint64_t bot_sig_remote, uint64_t top_flag, uint64_t bot_flag,
+                            uint64_t wait_top, uint64_t wait_bot, uint64_t norm, uint64_t timeout_ns, int rank) {
+    ops::JacobiStep st;
+    st.a = P<const float>(a);
+    st.b = P<float>(b);
+    st.nx = nx;
+    st.rows = rows;
+    st.top_dst = P<float>(top_dst);
+    st.bot_dst = P<float>(bot_dst);
+    st.top_sig_remote = P<uint64_t>(top_sig_remote);
+    st.bot_sig_remote = P<uint64_t>(bot_sig_remote);
+    st.top_flag = P<const uint64_t>(top_flag);
+    st.bot_flag = P<const uint64_t>(bot_flag);
+    st.wait_top = wait_top;
+    st.wait_bot = wait_bot;
+    st.norm = P<double>(norm);
+    st.timeout_ns = timeout_ns;
+    st.rank = rank;
+    ops::jacobi_step(st, cur_stream());
+  });
+  m.def("jacobi_ctas_per_row", &ops::jacobi_ctas_per_row);
   m.def("k_fill_pattern", [](uint64_t buf, size_t n, uint32_t seed) { ops::fill_pattern(P<void>(buf), n, seed, cur_stream()); });
   m.def("k_check_pattern", [](uint64_t buf, size_t n, uint32_t seed, uint64_t bad) {
     ops::check_pattern(P<const void>(buf), n, seed, P<unsigned long long>(bad), cur_stream());

@@ -46,5 +46,25 @@ GICC_EXPORT void allreduce_bf16(int algo, const void* const* in, void* const* ou
                                 int n, int me, size_t count, float scale, bool out_f32, uint64_t* const* flag_bases,
                                 int max_blocks, uint64_t epoch, uint64_t timeout_ns, int blocks, cudaStream_t s);
 
+// ---- Jacobi (jacobi.cu) ---------------------------------------------------------------------
+struct JacobiStep {
+  const float* a = nullptr;  // [rows+2][nx] read buffer
+  float* b = nullptr;        // [rows+2][nx] write buffer
+  int nx = 0, rows = 0;
+  float* top_dst = nullptr;  // upper neighbour's bottom halo row (its write buffer), or null
+  float* bot_dst = nullptr;  // lower neighbour's top halo row, or null
+  uint64_t* top_sig_remote = nullptr;
+  uint64_t* bot_sig_remote = nullptr;
+  const uint64_t* top_flag = nullptr;
+  const uint64_t* bot_flag = nullptr;
+  uint64_t wait_top = 0, wait_bot = 0;
+  double* norm = nullptr;
+  uint64_t timeout_ns = 0;
+  int rank = 0;
+};
+GICC_EXPORT void jacobi_init(float* a, float* b, int nx, int ny, int rows, int g0, uint64_t seed, cudaStream_t s);
+GICC_EXPORT void jacobi_step(const JacobiStep& st, cudaStream_t s);
+GICC_EXPORT int jacobi_ctas_per_row(int nx);
+
 }  // namespace ops
 }  // namespace gicc

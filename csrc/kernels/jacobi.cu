@@ -1,0 +1,203 @@
+// jacobi.cu -- 2-D 5-point Jacobi (fp32) with halo puts fused into the stencil kernel.
+//
+// Reference: examples/gicc/jacobi.cu:66-162 -- a 32x32-thread SIMT stencil whose *last*
+// finishing block (atomicInc counter) RDMA-writes both halo rows after every block is done,
+// followed by a host MPI barrier per iteration (jacobi.cu:430-471).
+//
+// Here:
+//  * one thread updates 4 adjacent columns (one float4) for RUN consecutive rows, keeping
+//    the rows above/below in registers (every interior value is read from HBM once);
+//    left/right neighbours come from warp shuffles;
+//  * the CTAs that own this rank's first / last row run first (lowest block ids) and
+//    store those rows straight into the neighbour's halo row over NVLink as they are
+//    computed, then bump the neighbour's arrival counter with a release add;
+//  * the next iteration's boundary CTAs wait (bounded) on their own arrival counter
+//    before reading the halo -- no host barrier, no separate copy kernel;
+//  * the update is ((e + w) + (n + s)) * 0.25 with explicit round-to-nearest adds/muls,
+//    bit-identical to the CPU oracle.
+#include <cuda_runtime.h>
+
+#include "gicc/device/comm.cuh"
+#include "gicc/host_util.hpp"
+#include "gicc/ops.hpp"
+
+namespace gicc {
+namespace {
+
+constexpr int kThreads = 256;           // 8 warps x 128 columns = 1024 columns per CTA
+constexpr int kColsPerCta = kThreads * 4;
+constexpr int kRun = 16;                // rows per CTA
+
+struct JacobiArgs {
+  const float* a;  // [rows+2][nx] read buffer (row 0 / rows+1 are halos)
+  float* b;        // [rows+2][nx] write buffer
+  int nx, rows;
+  float* top_dst;                // upper neighbour's bottom halo row in its write buffer (or null)
+  float* bot_dst;                // lower neighbour's top halo row in its write buffer (or null)
+  uint64_t* top_sig_remote;      // upper neighbour's bottom-halo arrival counter
+  uint64_t* bot_sig_remote;      // lower neighbour's top-halo arrival counter
+  const uint64_t* top_flag;      // my top-halo arrival counter
+  const uint64_t* bot_flag;      // my bottom-halo arrival counter
+  uint64_t wait_top, wait_bot;   // counts that make the halos of the previous iteration valid
+  double* norm;                  // optional: sum of (new-old)^2
+  ErrorRecord* err;
+  uint64_t timeout_ns;
+  int rank;
+};
+
+__device__ __forceinline__ float upd(float e, float w, float n, float s) {
+  return __fmul_rn(__fadd_rn(__fadd_rn(e, w), __fadd_rn(n, s)), 0.25f);
+}
+
+__global__ void __launch_bounds__(kThreads) k_jacobi(JacobiArgs p) {
+  const int nbx = (p.nx + kColsPerCta - 1) / kColsPerCta;
+  const int nby = (p.rows + kRun - 1) / kRun;
+  // boundary CTAs first: by = 0, then by = nby-1, then the rest
+  int bid = blockIdx.x, bx, by;
+  if (bid < nbx) {
+    bx = bid;
+    by = 0;
+  } else if (nby > 1 && bid < 2 * nbx) {
+    bx = bid - nbx;
+    by = nby - 1;
+  } else {
+    const int rest = bid - (nby > 1 ? 2 : 1) * nbx;
+    bx = rest % nbx;
+    by = 1 + rest / nbx;
+  }
+  const bool has_top = by == 0, has_bot = by == nby - 1;
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    if (has_top && p.top_flag &&
+        signal_wait_until(p.top_flag, proto::CMP_GE, p.wait_top, p.timeout_ns, p.err, p.rank, p.rank - 1,
+                          W_JACOBI_HALO) != GICC_OK)
+      ok = 0;
+    if (has_bot && p.bot_flag &&
+        signal_wait_until(p.bot_flag, proto::CMP_GE, p.wait_bot, p.timeout_ns, p.err, p.rank, p.rank + 1,
+                          W_JACOBI_HALO) != GICC_OK)
+      ok = 0;
+  }
+  __syncthreads();
+  if (!ok) return;
+
+  const int lane = threadIdx.x & 31;
+  const int j0 = bx * kColsPerCta + threadIdx.x * 4;  // first column of this thread
+  const bool active = j0 < p.nx;
+  const int r0 = 1 + by * kRun;                         // first local row of the run
+  const int r1 = min(r0 + kRun, p.rows + 1);            // one past the last
+  const size_t nx = (size_t)p.nx;
+  const float* A = p.a;
+
+  auto ld4 = [&](int r) -> float4 {
+    return active ? __ldcs(reinterpret_cast<const float4*>(A + (size_t)r * nx + j0)) : make_float4(0, 0, 0, 0);
+  };
+  float4 up = ld4(r0 - 1), mid = ld4(r0);
+  float sq = 0.f;
+  for (int r = r0; r < r1; ++r) {
+    const float4 dn = ld4(r + 1);
+    float left = __shfl_up_sync(0xffffffffu, mid.w, 1);
+    float right = __shfl_down_sync(0xffffffffu, mid.x, 1);
+    if (lane == 0 && active && j0 > 0) left = A[(size_t)r * nx + j0 - 1];
+    if (lane == 31 && active && j0 + 4 < p.nx) right = A[(size_t)r * nx + j0 + 4];
+    float4 o;
+    o.x = upd(mid.y, left, up.x, dn.x);
+    o.y = upd(mid.z, mid.x, up.y, dn.y);
+    o.z = upd(mid.w, mid.y, up.z, dn.z);
+    o.w = upd(right, mid.z, up.w, dn.w);
+    // Dirichlet columns keep their value
+    if (j0 == 0) o.x = mid.x;
+    if (j0 + 4 >= p.nx) o.w = mid.w;
+    if (active) {
+      __stcs(reinterpret_cast<float4*>(p.b + (size_t)r * nx + j0), o);
+      if (r == 1 && p.top_dst) *reinterpret_cast<float4*>(p.top_dst + j0) = o;
+      if (r == p.rows && p.bot_dst) *reinterpret_cast<float4*>(p.bot_dst + j0) = o;
+      if (p.norm) {
+        const float dx = o.x - mid.x, dy = o.y - mid.y, dz = o.z - mid.z, dw = o.w - mid.w;
+        sq += dx * dx + dy * dy + dz * dz + dw * dw;
+      }
+    }
+    up = mid;
+    mid = dn;
+  }
+  if (p.norm) {
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if (lane == 0 && sq != 0.f) atomicAdd(p.norm, (double)sq);
+  }
+  if ((has_top && p.top_dst) || (has_bot && p.bot_dst)) {
+    ptx::fence_acq_rel_sys();  // this thread's halo stores are visible system-wide
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      if (has_top && p.top_dst) ptx::red_release_sys_add(p.top_sig_remote, 1);
+      if (has_bot && p.bot_dst) ptx::red_release_sys_add(p.bot_sig_remote, 1);
+    }
+  }
+}
+
+// splitmix64 of (seed, global index) -> uniform [0,1) with 24 random bits.
+__device__ __forceinline__ float hash_uniform(uint64_t seed, uint64_t idx) {
+  uint64_t z = seed * 0x9E3779B97F4A7C15ull + idx + 1;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (float)(z >> 40) * (1.0f / 16777216.0f);
+}
+
+// Initialise local rows [0, rows+2) = global rows [g0-1, g0+rows]: top edge 1.0, other
+// edges 0, interior U[0,1) from `seed` keyed by the global index.
+__global__ void k_jacobi_init(float* a, float* b, int nx, int ny, int rows, int g0, uint64_t seed) {
+  const size_t total = (size_t)(rows + 2) * nx;
+  for (size_t k = (size_t)blockIdx.x * blockDim.x + threadIdx.x; k < total; k += (size_t)gridDim.x * blockDim.x) {
+    const int lr = (int)(k / nx), j = (int)(k % nx);
+    const int g = g0 - 1 + lr;
+    float v;
+    if (g <= 0)
+      v = 1.0f;
+    else if (g >= ny - 1 || j == 0 || j == nx - 1)
+      v = 0.0f;
+    else
+      v = hash_uniform(seed, (uint64_t)g * (uint64_t)nx + j);
+    a[k] = v;
+    if (b) b[k] = v;
+  }
+}
+
+}  // namespace
+
+namespace ops {
+
+void jacobi_init(float* a, float* b, int nx, int ny, int rows, int g0, uint64_t seed, cudaStream_t s) {
+  k_jacobi_init<<<4 * num_sms(), 256, 0, s>>>(a, b, nx, ny, rows, g0, seed);
+  GICC_CUDA(cudaGetLastError());
+}
+
+void jacobi_step(const JacobiStep& st, cudaStream_t s) {
+  if (st.nx % 4 != 0) throw std::runtime_error("gicc::jacobi: nx must be a multiple of 4");
+  if (st.rows < 1) throw std::runtime_error("gicc::jacobi: a rank needs at least one row");
+  JacobiArgs p;
+  p.a = st.a;
+  p.b = st.b;
+  p.nx = st.nx;
+  p.rows = st.rows;
+  p.top_dst = st.top_dst;
+  p.bot_dst = st.bot_dst;
+  p.top_sig_remote = st.top_sig_remote;
+  p.bot_sig_remote = st.bot_sig_remote;
+  p.top_flag = st.top_flag;
+  p.bot_flag = st.bot_flag;
+  p.wait_top = st.wait_top;
+  p.wait_bot = st.wait_bot;
+  p.norm = st.norm;
+  p.err = device_error_record();
+  p.timeout_ns = st.timeout_ns ? st.timeout_ns : default_timeout_ns();
+  p.rank = st.rank;
+  const int nbx = (st.nx + kColsPerCta - 1) / kColsPerCta;
+  const int nby = (st.rows + kRun - 1) / kRun;
+  k_jacobi<<<nbx * nby, kThreads, 0, s>>>(p);
+  GICC_CUDA(cudaGetLastError());
+}
+
+int jacobi_ctas_per_row(int nx) { return (nx + kColsPerCta - 1) / kColsPerCta; }
+
+}  // namespace ops
+}  // namespace gicc

@@ -26,4 +26,5 @@ def test_multigpu_suite(tmp_path):
         for k, v in r["allreduce_maxerr"].items():
             assert v < 0.05 * n, (k, v)
         assert r["gemm_ag_relerr"] < 1e-2 and r["gemm_rs_relerr"] < 1e-2, r
+        assert r["jacobi_mismatch"] == 0, r
     print(json.dumps(res))

@@ -118,6 +118,17 @@ def main():
         full = Af.float() @ Bf.float().t()
         ref = full[:, r * Nn // n:(r + 1) * Nn // n] if mode == "ag" else full[r * M // n:(r + 1) * M // n]
         res[f"gemm_{mode}_relerr"] = float(((C.float() - ref).norm() / ref.norm()).item())
+    # 7. Jacobi with fused halo puts vs the CPU oracle (gathered field, bit-exact)
+    import numpy as np
+    from opengda_b200.models.jacobi import Jacobi, jacobi_np
+    jnx, jny, jit = 1024, 4 * n + 70, 25
+    jac = Jacobi(jnx, jny, rt=rt)
+    jac.run(jit)
+    torch.cuda.synchronize()
+    parts = boot.allgather_obj(jac.owned().cpu().numpy())
+    field = np.concatenate(parts, axis=0)
+    ref = jacobi_np(jnx, jny, jit)[1:-1]
+    res["jacobi_mismatch"] = int((field != ref).sum())
     rt.check_device_errors()
     torch.cuda.synchronize()
     boot.barrier()
