@@ -93,15 +93,14 @@ def main() -> int:
         got = C[rows].float()
     rel = ((got - ref).norm() / ref.norm()).item()
     del Afull, Bfull
-    if world > 1:
-        slot = model.a_slot() if args.mode == "ag" else None
-        if slot is not None:
-            slot.copy_(A)
-            A = slot  # zero-copy input: the shard lives in the symmetric landing buffer
     torch.cuda.empty_cache()
+    zero_copy = world > 1 and args.mode == "ag"
+    if zero_copy:  # the shard lives in the symmetric landing buffers (both parities)
+        model.a_slot(0).copy_(A)
+        model.a_slot(1).copy_(A)
 
     def step():
-        model(A, B)
+        model(model.a_slot() if zero_copy else A, B)
 
     for _ in range(args.warmup):
         step()

@@ -174,6 +174,38 @@ void bind_runtime_objects(py::module_& m) {
     ops::jacobi_step(st, cur_stream());
   });
   m.def("jacobi_ctas_per_row", &ops::jacobi_ctas_per_row);
+  m.def("k_ag_gemm", [](int n, int r, int M, int Ns, int K, std::vector<uint64_t> a_full, uint64_t B, long long ldb,
+                        uint64_t C, long long ldc, std::vector<uint64_t> arrivals, std::vector<uint64_t> done,
+                        uint64_t epoch, int units_per_band, int grid, uint64_t timeout_ns) {
+    if ((int)a_full.size() != n || (int)arrivals.size() != n || (int)done.size() != n || n > 16)
+      throw std::runtime_error("k_ag_gemm: per-rank pointer lists must have n <= 16 entries");
+    ops::AgGemmArgs a;
+    a.n = n; a.r = r; a.M = M; a.Ns = Ns; a.K = K;
+    for (int i = 0; i < n; ++i) {
+      a.a_full[i] = P<void>(a_full[i]);
+      a.arrivals[i] = P<uint64_t>(arrivals[i]);
+      a.done[i] = P<uint64_t>(done[i]);
+    }
+    a.B = P<const void>(B); a.ldb = ldb; a.C = P<void>(C); a.ldc = ldc;
+    a.epoch = epoch; a.units_per_band = units_per_band; a.grid = grid; a.timeout_ns = timeout_ns;
+    ops::ag_gemm(a, cur_stream());
+  });
+  m.def("k_gemm_rs", [](int n, int r, int M, int N, int K, uint64_t A, long long lda, uint64_t B, long long ldb,
+                        std::vector<uint64_t> slots, std::vector<uint64_t> arrivals, std::vector<uint64_t> done,
+                        uint64_t out, long long ldo, uint64_t epoch, int grid, uint64_t timeout_ns) {
+    if ((int)slots.size() != n || (int)arrivals.size() != n || (int)done.size() != n || n > 16)
+      throw std::runtime_error("k_gemm_rs: per-rank pointer lists must have n <= 16 entries");
+    ops::GemmRsArgs a;
+    a.n = n; a.r = r; a.M = M; a.N = N; a.K = K;
+    a.A = P<const void>(A); a.lda = lda; a.B = P<const void>(B); a.ldb = ldb;
+    for (int i = 0; i < n; ++i) {
+      a.slots[i] = P<void>(slots[i]);
+      a.arrivals[i] = P<uint64_t>(arrivals[i]);
+      a.done[i] = P<uint64_t>(done[i]);
+    }
+    a.out = P<void>(out); a.ldo = ldo; a.epoch = epoch; a.grid = grid; a.timeout_ns = timeout_ns;
+    ops::gemm_rs(a, cur_stream());
+  });
   m.def("k_fill_pattern", [](uint64_t buf, size_t n, uint32_t seed) { ops::fill_pattern(P<void>(buf), n, seed, cur_stream()); });
   m.def("k_check_pattern", [](uint64_t buf, size_t n, uint32_t seed, uint64_t bad) {
     ops::check_pattern(P<const void>(buf), n, seed, P<unsigned long long>(bad), cur_stream());

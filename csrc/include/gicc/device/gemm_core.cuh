@@ -32,8 +32,11 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle row of bf16
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;   // without communication warps
 constexpr int kEpiThreads = 128;
+
+// Threads of a CTA for a schedule with `comm_warps` extra communication warps.
+__host__ __device__ constexpr int cta_threads(int comm_warps) { return kThreads + 32 * comm_warps; }
 
 template <int BN>
 struct Cfg {
@@ -89,12 +92,14 @@ struct PlainSched {
     ti.aux2 = 0;
     return ti;
   }
+  static constexpr int kCommWarps = 0;
   __device__ bool producer_wait(const TileInfo&, uint64_t, volatile int*, ErrorRecord*) const { return true; }
   __device__ void issue_loads(const TileInfo& ti, int kb, void* sA, void* sB, uint64_t* bar, const CUtensorMap* tmA,
                               const CUtensorMap* tmB) const {
     ptx::tma_load_2d(sA, tmA, bar, kb * BK, ti.a_row);
     ptx::tma_load_2d(sB, tmB, bar, kb * BK, ti.b_row);
   }
+  __device__ void comm(int, int, volatile int*, ErrorRecord*, uint64_t) const {}
 };
 
 template <int BN, class Sched, class Epi>
@@ -241,6 +246,9 @@ __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensor
         ptx::mbar_wait(drain, 0, 20000000ull, nullptr);
       }
     }
+  } else if (warp >= 6) {
+    // ---------------- communication warps (schedules that move data) ----------------
+    if constexpr (Sched::kCommWarps > 0) sched.comm((int)warp - 6, (int)lane, abort_flag, err, timeout_ns);
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access

@@ -66,5 +66,39 @@ GICC_EXPORT void jacobi_init(float* a, float* b, int nx, int ny, int rows, int g
 GICC_EXPORT void jacobi_step(const JacobiStep& st, cudaStream_t s);
 GICC_EXPORT int jacobi_ctas_per_row(int nx);
 
+// ---- distributed GEMM with fused NVLink transfers (gemm_dist.cu) ---------------------------
+// Pointer arrays are indexed by rank and hold this process's view of each rank's buffer.
+struct AgGemmArgs {
+  int n = 0, r = 0, M = 0, Ns = 0, K = 0;
+  void* a_full[16] = {};       // [M][K] bf16 landing buffers (current parity)
+  const void* B = nullptr;     // [Ns][K] bf16 local weights (B^T layout)
+  long long ldb = 0;
+  void* C = nullptr;           // [M][Ns] bf16 output
+  long long ldc = 0;
+  uint64_t* arrivals[16] = {}; // [n][M/n/128] arrival counters
+  uint64_t* done[16] = {};     // [n] CTA-done counters
+  uint64_t epoch = 0;          // call number, >= 1, equal on all ranks
+  int units_per_band = 4;
+  int grid = 0;
+  uint64_t timeout_ns = 0;
+};
+struct GemmRsArgs {
+  int n = 0, r = 0, M = 0, N = 0, K = 0;  // K = local K
+  const void* A = nullptr;     // [M][K] bf16 (K-shard)
+  long long lda = 0;
+  const void* B = nullptr;     // [N][K] bf16 (K-shard, B^T layout)
+  long long ldb = 0;
+  void* slots[16] = {};        // [n][M/n][N] bf16 partial landing areas (current parity)
+  uint64_t* arrivals[16] = {}; // [n][M/n/128]
+  uint64_t* done[16] = {};     // [n]
+  void* out = nullptr;         // [M/n][N] bf16
+  long long ldo = 0;
+  uint64_t epoch = 0;
+  int grid = 0;
+  uint64_t timeout_ns = 0;
+};
+GICC_EXPORT void ag_gemm(const AgGemmArgs& a, cudaStream_t s);
+GICC_EXPORT void gemm_rs(const GemmRsArgs& a, cudaStream_t s);
+
 }  // namespace ops
 }  // namespace gicc

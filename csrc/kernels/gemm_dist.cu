@@ -1,0 +1,435 @@
+// gemm_dist.cu -- distributed GEMM with the NVLink transfer fused into the tcgen05 kernel.
+//
+// all-gather -> GEMM (AG):  C[:, cols_r] = A_full[M,K] * B_r[Ns,K]^T
+//   A is row-sharded; rank r's shard already sits in rows [r*Ms, (r+1)*Ms) of its
+//   symmetric A_full buffer.  Four communication warps per CTA push that shard, in
+//   128-row bands, straight into every peer's A_full (16-byte NVLink stores), then bump
+//   the peer's per-(source, band) arrival counter with a release add.  The TMA producer
+//   of each CTA walks the tiles in "local shard first, then shard r+1, r+2, ..." order and
+//   waits (bounded, acquire) on the band's counter before loading it -- so the transfer of
+//   band b+1 overlaps the MMAs on band b.  Pushes go to rank r-1 first, r-2 next, ...
+//   which is exactly the order in which each receiver consumes them.
+//
+// GEMM -> reduce-scatter (RS): rank r owns output rows [r*Mr, (r+1)*Mr)
+//   K is sharded.  Tiles are walked owner by owner (r+1, r+2, ..., own rows last).  The
+//   epilogue stores a remote owner's tile as bf16 into that owner's slot for source r
+//   (peer memory) and releases a per-(source, band) counter; for its own rows it waits for
+//   every source's tiles of the band, adds them (f32) to its TMEM accumulator and writes the
+//   bf16 result.
+//
+// Both use epoch counters (one epoch per call) and double-buffered landing areas; a rank
+// writes into a peer's area of parity p only after that peer reported (per-CTA done
+// counters) that it finished the call that last used parity p.
+//
+// The reference's distributed matmul (examples/gicc/mm.cu:116-225) rotates fp32 B stripes
+// around a ring with one <<<1,1>>> put per step and a SIMT atomicAdd kernel; this is the
+// same all-gather-and-multiply pattern with tensor-core tiles and fine-grained overlap.
+#include <cuda_runtime.h>
+
+#include "gicc/device/comm.cuh"
+#include "gicc/device/gemm_core.cuh"
+#include "gicc/host_util.hpp"
+#include "gicc/ops.hpp"
+
+namespace gicc {
+namespace gemm {
+namespace {
+
+constexpr int kMaxR = 16;
+constexpr int kCommWarpsAG = 4;
+
+struct DoneTable {
+  uint64_t* p[kMaxR];  // each rank's [n] CTA-done counters, mapped here
+};
+
+__device__ __forceinline__ bool wait_counter(const uint64_t* p, uint64_t target, uint64_t timeout_ns,
+                                             volatile int* abort_flag) {
+  if (ptx::ld_acquire_sys(p) >= target) return true;
+  const uint64_t t0 = ptx::globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (ptx::ld_acquire_sys(p) >= target) return true;
+    if ((i & 63) == 0) {
+      if (abort_flag && *abort_flag) return false;
+      if (ptx::globaltimer() - t0 > timeout_ns) return false;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// all-gather -> GEMM
+// ------------------------------------------------------------------------------------------
+struct AgSched {
+  static constexpr int kCommWarps = kCommWarpsAG;
+  int n, r, M, Ns, K, Ms, nb, bn, num_n, Q, G;
+  const uint16_t* a_local;         // my A_full (this parity)
+  uint16_t* a_peer[kMaxR];         // every rank's A_full (this parity), mapped here
+  const uint64_t* arrivals;        // my counters [n][nb]
+  uint64_t* arrivals_peer[kMaxR];  // each rank's counter base
+  const uint64_t* done_local;      // [n] CTA-exit counts received from each rank
+  uint64_t epoch;                  // this call, >= 1
+
+  __device__ int num_tiles() const { return n * nb * num_n; }
+  __device__ TileInfo tile(int t) const {
+    const int seq = t / num_n, nbk = t - seq * num_n;
+    const int k = seq / nb, b = seq - k * nb;
+    const int s = (r + k) % n;
+    TileInfo ti;
+    ti.m0 = s * Ms + b * BM;
+    ti.a_row = ti.m0;
+    ti.n0 = nbk * bn;
+    ti.b_row = ti.n0;
+    ti.kb0 = 0;
+    ti.kb1 = (K + BK - 1) / BK;
+    ti.aux = s;
+    ti.aux2 = b;
+    return ti;
+  }
+  __device__ bool producer_wait(const TileInfo& ti, uint64_t timeout_ns, volatile int* abort_flag,
+                                ErrorRecord* err) const {
+    if (ti.aux == r) return true;
+    const uint64_t* c = arrivals + (size_t)ti.aux * nb + ti.aux2;
+    const uint64_t target = epoch * (uint64_t)Q;
+    if (!wait_counter(c, target, timeout_ns, abort_flag)) {
+      if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_AG_FLAG, r, ti.aux, ptx::ld_relaxed_sys(c), target);
+      return false;
+    }
+    ptx::fence_proxy_async_global();  // peer's generic-proxy stores -> our TMA reads
+    return true;
+  }
+  __device__ void issue_loads(const TileInfo& ti, int kb, void* sA, void* sB, uint64_t* bar, const CUtensorMap* tmA,
+                              const CUtensorMap* tmB) const {
+    ptx::tma_load_2d(sA, tmA, bar, kb * BK, ti.a_row);
+    ptx::tma_load_2d(sB, tmB, bar, kb * BK, ti.b_row);
+  }
+
+  // Push this rank's shard to the peers: unit u = ((k-1)*nb + b)*Q + q goes to rank r-k.
+  __device__ void comm(int cw, int lane, volatile int* abort_flag, ErrorRecord* err, uint64_t timeout_ns) const {
+    __shared__ int comm_stop;
+    const int tid = cw * 32 + lane;
+    constexpr int kT = kCommWarps * 32;
+    const size_t band_bytes = (size_t)BM * K * 2;
+    const size_t unit_bytes = band_bytes / Q;
+    const int U = (n - 1) * nb * Q;
+    int last_d = -1;
+    for (int u = blockIdx.x; u < U; u += G) {
+      const int k = 1 + u / (nb * Q);
+      const int rem = u - (k - 1) * nb * Q;
+      const int b = rem / Q, q = rem - (rem / Q) * Q;
+      const int d = (r - k + n) % n;
+      if (tid == 0) {
+        int stop = *abort_flag;
+        if (!stop && d != last_d && epoch > 2) {
+          const uint64_t target = (epoch - 2) * (uint64_t)G;
+          if (!wait_counter(done_local + d, target, timeout_ns, abort_flag)) {
+            if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_AG_FLAG, r, d, ptx::ld_relaxed_sys(done_local + d), target);
+            *abort_flag = 1;
+            stop = 1;
+          }
+        }
+        comm_stop = stop;
+      }
+      asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
+      if (comm_stop) break;
+      last_d = d;
+      const size_t off = ((size_t)(r * Ms + b * BM) * K * 2) + (size_t)q * unit_bytes;
+      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a_local) + off);
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a_peer[d]) + off);
+      const size_t nv = unit_bytes / 16;
+      size_t i = tid;
+      for (; i + 7 * kT < nv; i += 8 * kT) {
+        uint4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = ptx::ld_v4_nc(src + i + j * kT);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ptx::st_v4_na(dst + i + j * kT, v[j]);
+      }
+      for (; i < nv; i += kT) ptx::st_v4_na(dst + i, ptx::ld_v4_nc(src + i));
+      ptx::fence_acq_rel_sys();
+      asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
+      if (tid == 0) ptx::red_release_sys_add(arrivals_peer[d] + (size_t)r * nb + b, 1);
+    }
+  }
+};
+
+struct PlainStoreEpi {
+  static constexpr bool kNeedsTileDone = false;
+  uint16_t* C;
+  long long ldc;
+  int M, N;
+  __device__ static void fence_before_done() {}
+  __device__ void tile_done(const TileInfo&) {}
+  __device__ void begin_tile(const TileInfo&, int) {}
+  __device__ void end_tile(const TileInfo&, int) {}
+  __device__ __forceinline__ void store(const TileInfo& ti, int row, int c, const uint32_t* r) {
+    const int gm = ti.m0 + row;
+    if (gm >= M) return;
+    const int gn = ti.n0 + c;
+    uint16_t* p = C + (size_t)gm * ldc + gn;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (gn + 8 * j + 8 <= N) {
+        uint4 v;
+        v.x = ptx::pack_bf16x2(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
+        v.y = ptx::pack_bf16x2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
+        v.z = ptx::pack_bf16x2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
+        v.w = ptx::pack_bf16x2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
+        ptx::st_v4(p + 8 * j, v);
+      }
+    }
+  }
+};
+
+// Each CTA tells every rank that it is done with this call (it will not read any landing
+// area of this parity again).
+__device__ __forceinline__ void signal_cta_done(uint64_t* const* done_peer, int n, int r) {
+  __syncthreads();
+  if (threadIdx.x < (unsigned)n) ptx::red_release_sys_add(done_peer[threadIdx.x] + r, 1);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(cta_threads(kCommWarpsAG), 1)
+    k_ag_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, AgSched sched,
+              PlainStoreEpi epi, DoneTable done_peer, ErrorRecord* err, uint64_t timeout_ns) {
+  gemm_core<BN>(&tmA, &tmB, sched, epi, err, timeout_ns, sched.r);
+  signal_cta_done(done_peer.p, sched.n, sched.r);
+}
+
+// ------------------------------------------------------------------------------------------
+// GEMM -> reduce-scatter
+// ------------------------------------------------------------------------------------------
+struct RsSched {
+  static constexpr int kCommWarps = 0;
+  int n, r, M, N, K, Mr, nbo, bn, num_n;
+  __device__ int num_tiles() const { return n * nbo * num_n; }
+  __device__ TileInfo tile(int t) const {
+    const int seq = t / num_n, nbk = t - seq * num_n;
+    const int k = seq / nbo, b = seq - k * nbo;
+    const int o = (r + 1 + k) % n;  // owners r+1, r+2, ..., r (own rows last)
+    TileInfo ti;
+    ti.m0 = o * Mr + b * BM;
+    ti.a_row = ti.m0;
+    ti.n0 = nbk * bn;
+    ti.b_row = ti.n0;
+    ti.kb0 = 0;
+    ti.kb1 = (K + BK - 1) / BK;
+    ti.aux = o;
+    ti.aux2 = b;
+    return ti;
+  }
+  __device__ bool producer_wait(const TileInfo&, uint64_t, volatile int*, ErrorRecord*) const { return true; }
+  __device__ void issue_loads(const TileInfo& ti, int kb, void* sA, void* sB, uint64_t* bar, const CUtensorMap* tmA,
+                              const CUtensorMap* tmB) const {
+    ptx::tma_load_2d(sA, tmA, bar, kb * BK, ti.a_row);
+    ptx::tma_load_2d(sB, tmB, bar, kb * BK, ti.b_row);
+  }
+  __device__ void comm(int, int, volatile int*, ErrorRecord*, uint64_t) const {}
+};
+
+struct RsEpi {
+  static constexpr bool kNeedsTileDone = true;
+  int n, r, Mr, N, nbo, num_n, G;
+  uint16_t* slots_peer[kMaxR];     // owner o's slot area [n][Mr][N] (this parity), mapped here
+  const uint16_t* slots_local;     // my slot area
+  uint64_t* arrivals_peer[kMaxR];  // owner o's counters [n][nbo]
+  const uint64_t* arrivals;        // mine
+  const uint64_t* done_local;      // [n]
+  uint16_t* out;                   // [Mr][N] bf16
+  long long ldo;
+  uint64_t epoch;
+  uint64_t timeout_ns;
+  ErrorRecord* err;
+  volatile int* abort_flag;
+  int checked_owner;  // per-thread cache: owner whose previous-call readers are known done
+  int skip;           // per-thread: current tile aborted
+
+  __device__ static void fence_before_done() { ptx::fence_acq_rel_sys(); }
+  __device__ void begin_tile(const TileInfo& ti, int) {
+    skip = 0;
+    const int o = ti.aux;
+    if (o != r) {
+      if (o != checked_owner && epoch > 2) {
+        const uint64_t target = (epoch - 2) * (uint64_t)G;
+        if (!wait_counter(done_local + o, target, timeout_ns, abort_flag)) {
+          report_error(err, GICC_ETIMEDOUT, W_RS_FLAG, r, o, ptx::ld_relaxed_sys(done_local + o), target);
+          skip = 1;
+          return;
+        }
+      }
+      checked_owner = o;
+    } else {
+      const uint64_t target = epoch * (uint64_t)num_n;
+      for (int s = 0; s < n && !skip; ++s) {
+        if (s == r) continue;
+        const uint64_t* c = arrivals + (size_t)s * nbo + ti.aux2;
+        if (!wait_counter(c, target, timeout_ns, abort_flag)) {
+          report_error(err, GICC_ETIMEDOUT, W_RS_FLAG, r, s, ptx::ld_relaxed_sys(c), target);
+          skip = 1;
+        }
+      }
+    }
+  }
+  __device__ void end_tile(const TileInfo&, int) {}
+  __device__ __forceinline__ void store(const TileInfo& ti, int row, int c, const uint32_t* acc) {
+    if (skip) return;
+    const int o = ti.aux;
+    const int lrow = ti.m0 - o * Mr + row;  // row within the owner's block
+    const int gn = ti.n0 + c;
+    if (o != r) {
+      uint16_t* p = slots_peer[o] + ((size_t)r * Mr + lrow) * N + gn;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 v;
+        v.x = ptx::pack_bf16x2(__uint_as_float(acc[8 * j + 0]), __uint_as_float(acc[8 * j + 1]));
+        v.y = ptx::pack_bf16x2(__uint_as_float(acc[8 * j + 2]), __uint_as_float(acc[8 * j + 3]));
+        v.z = ptx::pack_bf16x2(__uint_as_float(acc[8 * j + 4]), __uint_as_float(acc[8 * j + 5]));
+        v.w = ptx::pack_bf16x2(__uint_as_float(acc[8 * j + 6]), __uint_as_float(acc[8 * j + 7]));
+        ptx::st_v4_na(p + 8 * j, v);
+      }
+      return;
+    }
+    float f[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(acc[i]);
+    for (int s = 0; s < n; ++s) {
+      if (s == r) continue;
+      const uint16_t* p = slots_local + ((size_t)s * Mr + lrow) * N + gn;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 v = ptx::ld_v4(p + 8 * j);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          f[8 * j + 2 * h] += ptx::bf16_lo(w[h]);
+          f[8 * j + 2 * h + 1] += ptx::bf16_hi(w[h]);
+        }
+      }
+    }
+    uint16_t* q = out + (size_t)lrow * ldo + gn;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 v;
+      v.x = ptx::pack_bf16x2(f[8 * j + 0], f[8 * j + 1]);
+      v.y = ptx::pack_bf16x2(f[8 * j + 2], f[8 * j + 3]);
+      v.z = ptx::pack_bf16x2(f[8 * j + 4], f[8 * j + 5]);
+      v.w = ptx::pack_bf16x2(f[8 * j + 6], f[8 * j + 7]);
+      ptx::st_v4(q + 8 * j, v);
+    }
+  }
+  __device__ void tile_done(const TileInfo& ti) {
+    if (ti.aux != r) ptx::red_release_sys_add(arrivals_peer[ti.aux] + (size_t)r * nbo + ti.aux2, 1);
+  }
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_rs(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, RsSched sched, RsEpi epi,
+              DoneTable done_peer, ErrorRecord* err, uint64_t timeout_ns) {
+  epi.checked_owner = -1;
+  epi.skip = 0;
+  gemm_core<BN>(&tmA, &tmB, sched, epi, err, timeout_ns, sched.r);
+  signal_cta_done(done_peer.p, sched.n, sched.r);
+}
+
+}  // namespace
+}  // namespace gemm
+
+namespace ops {
+
+void ag_gemm(const AgGemmArgs& a, cudaStream_t s) {
+  using namespace gemm;
+  constexpr int BN_ = 256;
+  if (a.n < 2 || a.n > kMaxR) throw std::runtime_error("gicc::ag_gemm: 2..16 ranks");
+  if (a.M % (a.n * BM) || a.Ns % BN_ || a.K % BK)
+    throw std::runtime_error("gicc::ag_gemm: need M % (ranks*128) == 0, N/ranks % 256 == 0, K % 64 == 0");
+  const int Ms = a.M / a.n, nb = Ms / BM;
+  const CUtensorMap tA = make_tmap_2d(a.a_full[a.r], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, a.K, BM, BK,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tB = make_tmap_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.Ns, a.K, a.ldb, BN_, BK,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  const int G = a.grid > 0 ? a.grid : num_sms();
+  AgSched sc{};
+  sc.n = a.n;
+  sc.r = a.r;
+  sc.M = a.M;
+  sc.Ns = a.Ns;
+  sc.K = a.K;
+  sc.Ms = Ms;
+  sc.nb = nb;
+  sc.bn = BN_;
+  sc.num_n = a.Ns / BN_;
+  sc.Q = a.units_per_band > 0 ? a.units_per_band : 4;
+  sc.G = G;
+  sc.a_local = static_cast<const uint16_t*>(a.a_full[a.r]);
+  for (int i = 0; i < a.n; ++i) {
+    sc.a_peer[i] = static_cast<uint16_t*>(a.a_full[i]);
+    sc.arrivals_peer[i] = a.arrivals[i];
+  }
+  sc.arrivals = a.arrivals[a.r];
+  sc.done_local = a.done[a.r];
+  sc.epoch = a.epoch;
+  PlainStoreEpi e{static_cast<uint16_t*>(a.C), a.ldc, a.M, a.Ns};
+  DoneTable dt{};
+  for (int i = 0; i < a.n; ++i) dt.p[i] = a.done[i];
+  constexpr uint32_t smem = Cfg<BN_>::kSmemBytes;
+  static bool attr[64] = {false};
+  int dev = 0;
+  GICC_CUDA(cudaGetDevice(&dev));
+  if (!attr[dev]) {
+    GICC_CUDA(cudaFuncSetAttribute(k_ag_gemm<BN_>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr[dev] = true;
+  }
+  k_ag_gemm<BN_><<<G, cta_threads(kCommWarpsAG), smem, s>>>(tA, tB, sc, e, dt, device_error_record(),
+                                                             a.timeout_ns ? a.timeout_ns : default_timeout_ns());
+  GICC_CUDA(cudaGetLastError());
+}
+
+void gemm_rs(const GemmRsArgs& a, cudaStream_t s) {
+  using namespace gemm;
+  constexpr int BN_ = 256;
+  if (a.n < 2 || a.n > kMaxR) throw std::runtime_error("gicc::gemm_rs: 2..16 ranks");
+  if (a.M % (a.n * BM) || a.N % BN_ || a.K % BK)
+    throw std::runtime_error("gicc::gemm_rs: need M % (ranks*128) == 0, N % 256 == 0, K/ranks % 64 == 0");
+  const int Mr = a.M / a.n;
+  const CUtensorMap tA = make_tmap_2d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, a.lda, BM, BK,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tB = make_tmap_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.ldb, BN_, BK,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  const int G = a.grid > 0 ? a.grid : num_sms();
+  RsSched sc{a.n, a.r, a.M, a.N, a.K, Mr, Mr / BM, BN_, a.N / BN_};
+  RsEpi e{};
+  e.n = a.n;
+  e.r = a.r;
+  e.Mr = Mr;
+  e.N = a.N;
+  e.nbo = Mr / BM;
+  e.num_n = a.N / BN_;
+  e.G = G;
+  for (int i = 0; i < a.n; ++i) {
+    e.slots_peer[i] = static_cast<uint16_t*>(a.slots[i]);
+    e.arrivals_peer[i] = a.arrivals[i];
+  }
+  e.slots_local = static_cast<const uint16_t*>(a.slots[a.r]);
+  e.arrivals = a.arrivals[a.r];
+  e.done_local = a.done[a.r];
+  e.out = static_cast<uint16_t*>(a.out);
+  e.ldo = a.ldo;
+  e.epoch = a.epoch;
+  e.timeout_ns = a.timeout_ns ? a.timeout_ns : default_timeout_ns();
+  e.err = device_error_record();
+  e.abort_flag = nullptr;
+  DoneTable dt{};
+  for (int i = 0; i < a.n; ++i) dt.p[i] = a.done[i];
+  constexpr uint32_t smem = Cfg<BN_>::kSmemBytes;
+  static bool attr[64] = {false};
+  int dev = 0;
+  GICC_CUDA(cudaGetDevice(&dev));
+  if (!attr[dev]) {
+    GICC_CUDA(cudaFuncSetAttribute(k_gemm_rs<BN_>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr[dev] = true;
+  }
+  k_gemm_rs<BN_><<<G, kThreads, smem, s>>>(tA, tB, sc, e, dt, e.err, e.timeout_ns);
+  GICC_CUDA(cudaGetLastError());
+}
+
+}  // namespace ops
+}  // namespace gicc

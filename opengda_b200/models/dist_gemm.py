@@ -23,8 +23,10 @@ from ..ops.gemm import gemm
 
 
 class DistGemm:
-    def __init__(self, M: int, N: int, K: int, mode: str = "ag", rt=None, device: Optional[torch.device] = None):
+    def __init__(self, M: int, N: int, K: int, mode: str = "ag", rt=None, device: Optional[torch.device] = None,
+                 fused: bool = True):
         self.M, self.N, self.K, self.mode = M, N, K, mode
+        self.fused = fused
         self.rt = rt
         self.world = rt.size if rt is not None else 1
         self.rank = rt.rank if rt is not None else 0
@@ -35,7 +37,22 @@ class DistGemm:
         if M % w or N % w or K % w:
             raise ValueError("M, N and K must be divisible by the number of ranks")
         self.launches_per_step = 1
-        if w > 1:
+        self.epoch = 0
+        if w > 1 and fused:
+            # fused kernels: double-buffered landing areas + epoch counters in the signal heap
+            if mode == "ag":
+                self.A_bufs = [rt.alloc_tensor((M, K), torch.bfloat16, exchange=False) for _ in range(2)]
+                nbands = (M // w) // 128
+            else:
+                self.slot_bufs = [rt.alloc_tensor((w, M // w, N), torch.bfloat16, exchange=False) for _ in range(2)]
+                nbands = (M // w) // 128
+            rt.exchange()
+            off = rt.signal_alloc(w * nbands + w)
+            self.arrivals = [rt.signal_peer(p, off) for p in range(w)]
+            self.done = [rt.signal_peer(p, off + w * nbands) for p in range(w)]
+            self.C = torch.empty(*self.out_shape(), dtype=torch.bfloat16, device=self.device)
+            self.launches_per_step = 1
+        elif w > 1:
             from ..ops import collectives
             from ..parallel import Barrier
 
@@ -63,15 +80,40 @@ class DistGemm:
         w = self.world
         return (self.M, self.N // w) if self.mode == "ag" else (self.M // w, self.N)
 
-    def a_slot(self) -> torch.Tensor:
-        """Where this rank's A shard must live for the AG mode (zero-copy input)."""
+    def a_slot(self, parity: Optional[int] = None) -> torch.Tensor:
+        """Where this rank's A shard must live for the AG mode (zero-copy input).  Fused
+        mode alternates two landing buffers; by default the slot of the *next* call."""
         Ms = self.M // self.world
+        if self.fused:
+            p = (self.epoch + 1) % 2 if parity is None else parity
+            return self.A_bufs[p].local[self.rank * Ms:(self.rank + 1) * Ms]
         return self.A_full.local[self.rank * Ms:(self.rank + 1) * Ms]
 
     def forward(self, A: torch.Tensor, B: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         w, r = self.world, self.rank
         if w == 1:
             return gemm(A, B, out=out)
+        if self.fused:
+            from .. import native
+
+            self.epoch += 1
+            p = self.epoch % 2
+            C = out if out is not None else self.C
+            n = native()
+            if self.mode == "ag":
+                slot = self.a_slot(p)
+                if A.data_ptr() != slot.data_ptr():
+                    slot.copy_(A)
+                buf = self.A_bufs[p]
+                n.k_ag_gemm(w, r, self.M, self.N // w, self.K, [buf.ptr(q) for q in range(w)], B.data_ptr(),
+                            B.stride(0), C.data_ptr(), C.stride(0), self.arrivals, self.done, self.epoch, 4, 0,
+                            self.rt.timeout_ns)
+            else:
+                buf = self.slot_bufs[p]
+                n.k_gemm_rs(w, r, self.M, self.N, self.K // w, A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0),
+                            [buf.ptr(q) for q in range(w)], self.arrivals, self.done, C.data_ptr(), C.stride(0),
+                            self.epoch, 0, self.rt.timeout_ns)
+            return C
         if self.mode == "ag":
             Ms = self.M // w
             slot = self.a_slot()

@@ -25,6 +25,7 @@ def test_multigpu_suite(tmp_path):
         assert r["single_flag"] == 42 and r["continuous_count"] == 10000, r
         for k, v in r["allreduce_maxerr"].items():
             assert v < 0.05 * n, (k, v)
-        assert r["gemm_ag_relerr"] < 1e-2 and r["gemm_rs_relerr"] < 1e-2, r
+        for k in ("gemm_ag_relerr", "gemm_rs_relerr", "gemm_ag_fused_relerr", "gemm_rs_fused_relerr"):
+            assert r[k] < 1e-2, (k, r)
         assert r["jacobi_mismatch"] == 0, r
     print(json.dumps(res))

@@ -109,15 +109,19 @@ def main():
 
     # 6. distributed GEMM, both modes, small shape vs fp32
     from opengda_b200.models.dist_gemm import DistGemm, make_operands
-    for mode in ("ag", "rs"):
-        M = Nn = K = 1024
-        model = DistGemm(M, Nn, K, mode, rt=rt)
-        A, B, (Af, Bf) = make_operands(M, Nn, K, mode, n, r, seed=2)
-        C = model(A, B)
-        torch.cuda.synchronize()
-        full = Af.float() @ Bf.float().t()
-        ref = full[:, r * Nn // n:(r + 1) * Nn // n] if mode == "ag" else full[r * M // n:(r + 1) * M // n]
-        res[f"gemm_{mode}_relerr"] = float(((C.float() - ref).norm() / ref.norm()).item())
+    for fused in (False, True):
+        for mode in ("ag", "rs"):
+            M = Nn = K = 2048
+            model = DistGemm(M, Nn, K, mode, rt=rt, fused=fused)
+            worst = 0.0
+            for call in range(4):  # several calls: epochs, both buffer parities, done counters
+                A, B, (Af, Bf) = make_operands(M, Nn, K, mode, n, r, seed=2 + call)
+                C = model(A, B)
+                torch.cuda.synchronize()
+                full = Af.float() @ Bf.float().t()
+                ref = full[:, r * Nn // n:(r + 1) * Nn // n] if mode == "ag" else full[r * M // n:(r + 1) * M // n]
+                worst = max(worst, float(((C.float() - ref).norm() / ref.norm()).item()))
+            res[f"gemm_{mode}{'_fused' if fused else ''}_relerr"] = worst
     # 7. Jacobi with fused halo puts vs the CPU oracle (gathered field, bit-exact)
     import numpy as np
     from opengda_b200.models.jacobi import Jacobi, jacobi_np
@@ -134,6 +138,9 @@ def main():
     boot.barrier()
     with open(f"{out}.{r}", "w") as f:
         json.dump(res, f)
+    if os.path.isdir(os.path.join(ROOT, "gpurun_out")):
+        with open(os.path.join(ROOT, "gpurun_out", f"multigpu_rank{r}.json"), "w") as f:
+            json.dump(res, f)
     del ar
     rt.finalize()
 
