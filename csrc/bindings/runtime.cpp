@@ -14,6 +14,16 @@ py::bytes to_bytes(const std::vector<uint8_t>& v) { return py::bytes(reinterpret
 
 void bind_runtime_objects(py::module_& m);  // runtime_objects.cpp
 
+namespace gicc {
+namespace fake {
+int barrier_run(uint64_t* shm, int rank, int size, int iters, int mode, uint64_t timeout_ns, int skip_at, int* fail_iter);
+size_t am_region_bytes(int size, int nslots, uint32_t slot_bytes);
+int am_run(uint8_t* shm, int rank, int size, int nslots, int nmsg, int nreq, uint64_t timeout_ns, uint64_t* out_counter,
+           uint64_t* out_checksum);
+int am_wait_one(uint8_t* shm, int rank, int size, int nslots, int src, uint64_t timeout_ns);
+}  // namespace fake
+}  // namespace gicc
+
 void bind_runtime(py::module_& m) {
   py::register_exception<gicc::BootstrapError>(m, "BootstrapError", PyExc_RuntimeError);
 
@@ -110,5 +120,29 @@ void bind_runtime(py::module_& m) {
       .def("send_fds", &Bootstrap::send_fds, py::call_guard<py::gil_scoped_release>())
       .def("recv_fds", &Bootstrap::recv_fds, py::call_guard<py::gil_scoped_release>());
 
+  // CPU-rank protocol runners over shared memory (the same protocol code as the kernels)
+  m.def("cpu_barrier_run", [](uint64_t shm, int rank, int size, int iters, int mode, uint64_t timeout_ns, int skip_at) {
+    int fail = -1;
+    int st;
+    {
+      py::gil_scoped_release rel;
+      st = gicc::fake::barrier_run(reinterpret_cast<uint64_t*>(shm), rank, size, iters, mode, timeout_ns, skip_at, &fail);
+    }
+    return py::make_tuple(st, fail);
+  });
+  m.def("cpu_am_region_bytes", &gicc::fake::am_region_bytes);
+  m.def("cpu_am_run", [](uint64_t shm, int rank, int size, int nslots, int nmsg, int nreq, uint64_t timeout_ns) {
+    uint64_t c = 0, k = 0;
+    int st;
+    {
+      py::gil_scoped_release rel;
+      st = gicc::fake::am_run(reinterpret_cast<uint8_t*>(shm), rank, size, nslots, nmsg, nreq, timeout_ns, &c, &k);
+    }
+    return py::make_tuple(st, c, k);
+  });
+  m.def("cpu_am_wait_one", [](uint64_t shm, int rank, int size, int nslots, int src, uint64_t timeout_ns) {
+    py::gil_scoped_release rel;
+    return gicc::fake::am_wait_one(reinterpret_cast<uint8_t*>(shm), rank, size, nslots, src, timeout_ns);
+  });
   bind_runtime_objects(m);
 }

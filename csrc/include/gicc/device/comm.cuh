@@ -252,7 +252,9 @@ __device__ __forceinline__ void* remote_ptr(GiccContext* ctx, const void* local,
 // Uses ctx->expected_signal as the epoch; the caller (host setup() or a continuous
 // kernel) advances it.  Returns a status instead of spinning forever.
 // ---------------------------------------------------------------------------------------
-__device__ __forceinline__ int barrier(BarrierCtx* ctx) {
+// report=false skips the progress store into mapped host memory (continuous kernels report
+// once at the end: a pending PCIe write would otherwise stall the next barrier's fence).
+__device__ __forceinline__ int barrier(BarrierCtx* ctx, bool report = true) {
   const uint64_t epoch = *reinterpret_cast<volatile uint64_t*>(&ctx->expected_signal);
   uint64_t seen = 0;
   int st;
@@ -270,7 +272,7 @@ __device__ __forceinline__ int barrier(BarrierCtx* ctx) {
     return st;
   }
   // progress report for the host (plain posted store into mapped host memory)
-  *reinterpret_cast<volatile uint64_t*>(ctx->done_counter) = epoch;
+  if (report) *reinterpret_cast<volatile uint64_t*>(ctx->done_counter) = epoch;
   return GICC_OK;
 }
 

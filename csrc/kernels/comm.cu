@@ -24,9 +24,11 @@ __global__ void k_barrier_single(BarrierCtx* ctx, uint64_t* flag) {
 __global__ void k_barrier_continuous(BarrierCtx* ctx, int n, uint64_t* counter) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   for (int i = 0; i < n; ++i) {
-    if (barrier(ctx) != GICC_OK) return;
+    const uint64_t epoch = ctx->expected_signal;
+    if (barrier(ctx, false) != GICC_OK) return;
     ctx->expected_signal++;
     if (counter) *reinterpret_cast<volatile uint64_t*>(counter) = i + 1;
+    if (i == n - 1 || (i & 1023) == 1023) *reinterpret_cast<volatile uint64_t*>(ctx->done_counter) = epoch;
   }
 }
 

@@ -70,8 +70,11 @@ struct AgSched {
 
   __device__ int num_tiles() const { return n * nb * num_n; }
   __device__ TileInfo tile(int t) const {
-    const int seq = t / num_n, nbk = t - seq * num_n;
-    const int k = seq / nb, b = seq - k * nb;
+    // shard-major (local shard first), grouped rasterisation inside a shard for L2 reuse
+    const int per = nb * num_n;
+    const int k = t / per;
+    int b, nbk;
+    raster(t - k * per, nb, num_n, 16, b, nbk);
     const int s = (r + k) % n;
     TileInfo ti;
     ti.m0 = s * Ms + b * BM;
@@ -202,9 +205,12 @@ struct RsSched {
   int n, r, M, N, K, Mr, nbo, bn, num_n;
   __device__ int num_tiles() const { return n * nbo * num_n; }
   __device__ TileInfo tile(int t) const {
-    const int seq = t / num_n, nbk = t - seq * num_n;
-    const int k = seq / nbo, b = seq - k * nbo;
-    const int o = (r + 1 + k) % n;  // owners r+1, r+2, ..., r (own rows last)
+    // owner-major (owners r+1, r+2, ..., own rows last), grouped rasterisation per owner
+    const int per = nbo * num_n;
+    const int k = t / per;
+    int b, nbk;
+    raster(t - k * per, nbo, num_n, 16, b, nbk);
+    const int o = (r + 1 + k) % n;
     TileInfo ti;
     ti.m0 = o * Mr + b * BM;
     ti.a_row = ti.m0;

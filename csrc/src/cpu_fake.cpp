@@ -1,0 +1,189 @@
+// cpu_fake.cpp -- CPU ranks over shared memory ("fake device") running the exact flag
+// protocols the kernels use (proto/barrier.hpp, proto/am.hpp) with the HostMem policy.
+// Used by the CPU test-suite: forked processes map one shared file and call these.
+#include <cstdint>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "gicc/proto/am.hpp"
+#include "gicc/proto/barrier.hpp"
+#include "gicc/types.hpp"
+#include "gicc/visibility.hpp"
+
+namespace gicc {
+namespace fake {
+
+using proto::HostMem;
+
+// Shared layout for the barrier test: per rank [GICC_MAX_ROUNDS] signal words, one shared
+// counter (NVLS emulation) and a [size] progress array.
+struct BarrierLayout {
+  static size_t words(int size) { return (size_t)size * 16 + 8 + (size_t)size; }
+};
+
+// Runs `iters` barriers.  Before each barrier a rank publishes its progress; after it, every
+// rank checks that nobody's progress is behind its own (the cross-rank counter check of the
+// reference's barrier verifier, legacy/ofi/prototype/barrier-verify.cpp:347-400).
+// mode 0 = dissemination, 1 = shared-counter.  skip_at >= 0: this rank stops participating
+// at that barrier (to test timeouts).  Returns 0 ok, 1 timeout, 2 ordering violation.
+GICC_EXPORT int barrier_run(uint64_t* shm, int rank, int size, int iters, int mode, uint64_t timeout_ns, int skip_at,
+                            int* fail_iter) {
+  uint64_t* sig = shm;                       // [size][16]
+  uint64_t* counter = shm + (size_t)size * 16;
+  uint64_t* progress = counter + 8;          // [size]
+  const int rounds = proto::n_rounds_for(size);
+  uint64_t* trig[GICC_MAX_ROUNDS];
+  for (int k = 0; k < rounds; ++k) trig[k] = sig + (size_t)((rank + (1 << k)) % size) * 16 + k;
+  for (int it = 0; it < iters; ++it) {
+    if (it == skip_at) return 0;
+    const uint64_t epoch = (uint64_t)it + 1;
+    HostMem::store_release(&progress[rank], epoch);
+    int st;
+    uint64_t seen = 0;
+    if (mode == 0) {
+      int round = -1;
+      st = proto::dissemination_barrier<HostMem>(rounds, trig, sig + (size_t)rank * 16, epoch, timeout_ns, &round, &seen);
+    } else {
+      st = proto::counter_barrier<HostMem>([counter] { HostMem::add_release(counter, 1); }, counter, size, epoch,
+                                           timeout_ns, &seen);
+    }
+    if (st != GICC_OK) {
+      if (fail_iter) *fail_iter = it;
+      return 1;
+    }
+    for (int p = 0; p < size; ++p)
+      if (HostMem::load_acquire(&progress[p]) < epoch) {
+        if (fail_iter) *fail_iter = it;
+        return 2;
+      }
+  }
+  return 0;
+}
+
+// ---- active messages over shared memory ------------------------------------------------------
+// Per-rank region: inbox [size][nslots][slot] | head[size] | tail[size] | credit[size] |
+// ack[size] | ack_val[size] | counter | checksum.
+GICC_EXPORT size_t am_region_bytes(int size, int nslots, uint32_t slot_bytes) {
+  return (size_t)size * nslots * slot_bytes + (size_t)5 * size * 8 + 16;
+}
+
+static am::AmView make_view(uint8_t* shm, int rank, int size, int nslots, uint32_t slot_bytes, uint64_t timeout_ns) {
+  const size_t region = am_region_bytes(size, nslots, slot_bytes);
+  auto base = [&](int r) { return shm + (size_t)r * region; };
+  auto words = [&](int r, int which) {
+    return reinterpret_cast<uint64_t*>(base(r) + (size_t)size * nslots * slot_bytes) + (size_t)which * size;
+  };
+  am::AmView v;
+  std::memset(&v, 0, sizeof(v));
+  v.rank = rank;
+  v.size = size;
+  v.nslots = nslots;
+  v.slot_bytes = slot_bytes;
+  v.inbox = base(rank);
+  for (int p = 0; p < size; ++p) {
+    v.peer_inbox[p] = base(p);
+    v.peer_credit[p] = words(p, 2);
+    v.peer_ack[p] = words(p, 3);
+    v.peer_ack_val[p] = words(p, 4);
+  }
+  v.head = words(rank, 0);
+  v.tail = words(rank, 1);
+  v.credit = words(rank, 2);
+  v.ack = words(rank, 3);
+  v.ack_val = words(rank, 4);
+  v.counter = words(rank, 5);
+  v.checksum = v.counter + 1;
+  v.timeout_ns = timeout_ns;
+  return v;
+}
+
+// Every rank sends `nmsg` COUNTER_ADD(src+1) and `nmsg` CHECKSUM payloads to every peer
+// while draining its own inboxes (tiny rings force credit waits and wrap-around), then
+// runs `nreq` ECHO request/reply round trips with its right neighbour.
+// Returns 0 ok, 1 send timeout, 2 wrong counter, 3 wrong checksum, 4 reply timeout, 5 bad echo.
+GICC_EXPORT int am_run(uint8_t* shm, int rank, int size, int nslots, int nmsg, int nreq, uint64_t timeout_ns,
+                       uint64_t* out_counter, uint64_t* out_checksum) {
+  am::AmView v = make_view(shm, rank, size, nslots, am::AM_SHORT_SIZE + 256, timeout_ns);
+  uint8_t payload[256];
+  for (int i = 0; i < 256; ++i) payload[i] = (uint8_t)(i * 7 + rank);
+  int sent = 0;
+  const int total = 2 * nmsg * (size - 1);
+  const uint64_t t_send = HostMem::now_ns();
+  while (sent < total) {
+    const int idx = sent / (size - 1);
+    const int dst = (rank + 1 + sent % (size - 1)) % size;
+    am::am_args_t a;
+    std::memset(&a, 0, sizeof(a));
+    a.data[0] = (uint64_t)rank + 1;
+    uint64_t seq;
+    if (!am::can_send<HostMem>(v, dst)) {
+      am::poll_all_builtin<HostMem>(v, 64);  // drain while we wait for credit
+      if (HostMem::now_ns() - t_send > timeout_ns) return 1;
+      continue;
+    }
+    if (idx < nmsg)
+      seq = am::send<HostMem>(v, dst, am::AM_HANDLER_COUNTER_ADD, a, nullptr, 0, 0);
+    else
+      seq = am::send<HostMem>(v, dst, am::AM_HANDLER_CHECKSUM, a, payload, 256, 0);
+    if (seq == 0) return 1;
+    ++sent;
+    am::poll_all_builtin<HostMem>(v, 4);
+  }
+  // drain until every peer's messages arrived
+  uint64_t want_counter = 0;
+  for (int p = 0; p < size; ++p)
+    if (p != rank) want_counter += (uint64_t)nmsg * (uint64_t)(p + 1);
+  // payload bytes are (i*7 + p) mod 256
+  uint64_t want_checksum = 0;
+  for (int p = 0; p < size; ++p) {
+    if (p == rank) continue;
+    uint64_t s = 0;
+    for (int i = 0; i < 256; ++i) s += (uint8_t)(i * 7 + p);
+    want_checksum += (uint64_t)nmsg * s;
+  }
+  const uint64_t t0 = HostMem::now_ns();
+  while (HostMem::load_acquire(v.counter) < want_counter || HostMem::load_acquire(v.checksum) < want_checksum) {
+    am::poll_all_builtin<HostMem>(v, 64);
+    if (HostMem::now_ns() - t0 > timeout_ns) break;
+  }
+  if (out_counter) *out_counter = HostMem::load_acquire(v.counter);
+  if (out_checksum) *out_checksum = HostMem::load_acquire(v.checksum);
+  if (HostMem::load_acquire(v.counter) != want_counter) return 2;
+  if (HostMem::load_acquire(v.checksum) != want_checksum) return 3;
+  // request/reply with the right neighbour; serve the left neighbour's requests meanwhile
+  const int right = (rank + 1) % size;
+  for (int i = 0; i < nreq && size > 1; ++i) {
+    am::am_args_t a;
+    std::memset(&a, 0, sizeof(a));
+    a.data[0] = 1000u * (uint64_t)rank + (uint64_t)i;
+    const uint64_t seq = am::send<HostMem>(v, right, am::AM_HANDLER_ECHO, a, nullptr, 0, am::AM_FLAG_REQUEST);
+    if (seq == 0) return 4;
+    uint64_t val = 0;
+    const uint64_t t1 = HostMem::now_ns();
+    while (HostMem::load_acquire(&v.ack[right]) < seq) {
+      am::poll_all_builtin<HostMem>(v, 8);
+      if (HostMem::now_ns() - t1 > timeout_ns) return 4;
+    }
+    val = HostMem::load_acquire(&v.ack_val[right]);
+    if (val != a.data[0]) return 5;
+  }
+  // keep serving until the left neighbour finished its requests
+  const int left = (rank - 1 + size) % size;
+  const uint64_t t2 = HostMem::now_ns();
+  while (size > 1 && HostMem::load_acquire(&v.tail[left]) < (uint64_t)(2 * nmsg + nreq)) {
+    am::poll_all_builtin<HostMem>(v, 8);
+    if (HostMem::now_ns() - t2 > timeout_ns) return 4;
+  }
+  return 0;
+}
+
+// A receiver waiting for a message that is never sent must time out (returns 0 on timeout).
+GICC_EXPORT int am_wait_one(uint8_t* shm, int rank, int size, int nslots, int src, uint64_t timeout_ns) {
+  am::AmView v = make_view(shm, rank, size, nslots, am::AM_SHORT_SIZE + 256, timeout_ns);
+  return am::wait_one<HostMem>(v, src);
+}
+
+}  // namespace fake
+}  // namespace gicc

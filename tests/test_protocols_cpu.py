@@ -1,0 +1,58 @@
+"""The device flag protocols (dissemination / counter barrier, active-message rings with
+credits and request/reply) run on CPU ranks over shared memory -- the same C++ code as the
+kernels, instantiated with host atomics.  Also checks that a dropped message or a missing
+rank ends in a timeout, not a hang."""
+import os
+import sys
+
+import pytest
+
+from opengda_b200.parallel.launch import launch
+
+WORKER = os.path.join(os.path.dirname(__file__), "workers", "proto_worker.py")
+
+
+def _shm(tmp_path, nbytes):
+    p = tmp_path / "shm.bin"
+    with open(p, "wb") as f:
+        f.truncate(nbytes)
+    return str(p)
+
+
+def _run(n, path, what, args, tmp_path):
+    out = str(tmp_path / what)
+    rc = launch(n, [sys.executable, WORKER, path, what, out] + [str(a) for a in args], timeout=120)
+    return rc, [open(f"{out}.{r}").read() for r in range(n)]
+
+
+@pytest.mark.parametrize("n,mode", [(2, 0), (3, 0), (5, 0), (4, 1), (3, 1)])
+def test_barrier_protocol_orders_ranks(n, mode, tmp_path):
+    path = _shm(tmp_path, (n * 16 + 8 + n) * 8 + 4096)
+    rc, res = _run(n, path, "barrier", [2000, mode, -1], tmp_path)
+    assert rc == 0 and all(r == "0 -1" for r in res), res
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_barrier_protocol_missing_rank_times_out(mode, tmp_path):
+    n = 3
+    path = _shm(tmp_path, (n * 16 + 8 + n) * 8 + 4096)
+    rc, res = _run(n, path, "barrier", [200, mode, 1], tmp_path)
+    # rank 1 leaves at barrier 100; the others report a timeout at that barrier
+    for r in (0, 2):
+        st, it = res[r].split()
+        assert st == "1" and int(it) == 100, res
+
+
+@pytest.mark.parametrize("n,nslots", [(2, 4), (3, 2), (4, 8)])
+def test_active_messages_credit_flow_and_replies(n, nslots, tmp_path):
+    from opengda_b200 import native
+    path = _shm(tmp_path, n * native().cpu_am_region_bytes(n, nslots, 64 + 256) + 4096)
+    rc, res = _run(n, path, "am", [nslots, 50, 20], tmp_path)
+    assert rc == 0 and all(r.split()[0] == "0" for r in res), res
+
+
+def test_active_message_drop_times_out(tmp_path):
+    from opengda_b200 import native
+    path = _shm(tmp_path, 2 * native().cpu_am_region_bytes(2, 4, 64 + 256) + 4096)
+    rc, res = _run(2, path, "am_drop", [], tmp_path)
+    assert res[0] == "0", res  # 0 messages handled: the wait ended by timeout
