@@ -47,6 +47,7 @@ def main() -> int:
     ap.add_argument("--mode", default="ag", choices=["ag", "rs"])
     ap.add_argument("--size", type=int, default=16384)
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--unfused", action="store_true", help="decomposed path: copy kernels + GEMM (A/B only)")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_unavailable(args)
@@ -77,7 +78,7 @@ def main() -> int:
     from opengda_b200.utils.clocks import ClockSampler
 
     M = N = K = args.size
-    model = DistGemm(M, N, K, args.mode, rt=rt, device=dev)
+    model = DistGemm(M, N, K, args.mode, rt=rt, device=dev, fused=not args.unfused)
     A, B, (Afull, Bfull) = make_operands(M, N, K, args.mode, world, rank, seed=2, device=dev)
     # numerics spot check (one row block) before timing
     C = model(A, B)

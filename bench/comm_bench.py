@@ -80,9 +80,9 @@ def main():
     put, get, nccl_p2p = [], [], []
     for size in sizes:
         reps = max(1, min(1000, (64 << 20) // size))
-        ms = timed(lambda: N.k_copy(buf.ptr(right), src.data_ptr(), size, reps), 5 if args.quick else 10)
+        ms = timed(lambda: N.k_copy(buf.ptr(right), src.data_ptr(), size, reps, 0, 0, maxb), 5 if args.quick else 10)
         put.append({"bytes": size, "GBps": size * reps / (ms * 1e-3) / 1e9, "us_per_put": ms * 1e3 / reps})
-        ms = timed(lambda: N.k_copy(recvb.data_ptr(), buf.ptr(left), size, reps), 5 if args.quick else 10)
+        ms = timed(lambda: N.k_copy(recvb.data_ptr(), buf.ptr(left), size, reps, 0, 0, maxb), 5 if args.quick else 10)
         get.append({"bytes": size, "GBps": size * reps / (ms * 1e-3) / 1e9, "us_per_get": ms * 1e3 / reps})
 
         def nccl_ring():
@@ -92,7 +92,10 @@ def main():
         nreps = max(1, min(100, (64 << 20) // size))
         ms = timed(lambda: [nccl_ring() for _ in range(nreps)], 3 if args.quick else 5)
         nccl_p2p.append({"bytes": size, "GBps": size * nreps / (ms * 1e-3) / 1e9, "us_per_op": ms * 1e3 / nreps})
-    # verify the last put delivered the pattern
+    # verify: one full-size put of the seeded pattern lands intact on the right neighbour
+    torch.cuda.synchronize()
+    dist.barrier()
+    N.k_copy(buf.ptr(right), src.data_ptr(), maxb)
     torch.cuda.synchronize()
     dist.barrier()
     bad = torch.zeros(1, dtype=torch.int64, device="cuda")

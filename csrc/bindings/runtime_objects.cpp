@@ -111,9 +111,10 @@ void bind_runtime_objects(py::module_& m) {
   m.def("k_barrier_continuous", [](uint64_t ctx, int n, uint64_t counter) {
     ops::barrier_continuous(P<BarrierCtx>(ctx), n, P<uint64_t>(counter), cur_stream());
   });
-  m.def("k_copy", [](uint64_t dst, uint64_t src, size_t bytes, int iters, int blocks, int threads) {
-    ops::copy(P<void>(dst), P<const void>(src), bytes, iters, blocks, threads, cur_stream());
-  }, py::arg("dst"), py::arg("src"), py::arg("bytes"), py::arg("iters") = 1, py::arg("blocks") = 0, py::arg("threads") = 0);
+  m.def("k_copy", [](uint64_t dst, uint64_t src, size_t bytes, int iters, int blocks, int threads, size_t window) {
+    ops::copy(P<void>(dst), P<const void>(src), bytes, iters, blocks, threads, cur_stream(), window);
+  }, py::arg("dst"), py::arg("src"), py::arg("bytes"), py::arg("iters") = 1, py::arg("blocks") = 0, py::arg("threads") = 0,
+     py::arg("window") = 0);
   m.def("k_put_signal", [](uint64_t dst, uint64_t src, size_t bytes, uint64_t sig, int blocks) {
     ops::put_signal(P<void>(dst), P<const void>(src), bytes, P<uint64_t>(sig), blocks, cur_stream());
   }, py::arg("dst"), py::arg("src"), py::arg("bytes"), py::arg("sig"), py::arg("blocks") = 0);

@@ -20,7 +20,9 @@ GICC_EXPORT void gemm_bf16(const void* A, const void* B, void* C, int M, int N, 
 GICC_EXPORT void barrier_single(BarrierCtx* ctx, uint64_t* flag, cudaStream_t s);
 GICC_EXPORT void barrier_continuous(BarrierCtx* ctx, int n, uint64_t* counter, cudaStream_t s);
 // Grid copy of `bytes`, repeated `iters` times, ending with fence.acq_rel.sys (local or peer memory).
-GICC_EXPORT void copy(void* dst, const void* src, size_t bytes, int iters, int blocks, int threads, cudaStream_t s);
+// window > bytes: repetition i copies at offset (i*bytes) mod (window-bytes) on both sides.
+GICC_EXPORT void copy(void* dst, const void* src, size_t bytes, int iters, int blocks, int threads, cudaStream_t s,
+                      size_t window = 0);
 // Grid put; each block then adds 1 to *sig_remote with release semantics.
 GICC_EXPORT void put_signal(void* dst, const void* src, size_t bytes, uint64_t* sig_remote, int blocks, cudaStream_t s);
 GICC_EXPORT void wait_signal(const uint64_t* sig, int cmp, uint64_t value, uint64_t timeout_ns, int* status,

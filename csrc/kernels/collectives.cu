@@ -8,7 +8,10 @@
 //     the CTA of the same index on every peer (epoch-valued flags in the signal heap,
 //     release stores / acquire polls, bounded by %globaltimer).  CTA b of every rank
 //     touches the same element range, so the pairwise handshake is all that is needed;
-//   * bf16 data is summed in f32 registers, scaled, and written as bf16 or f32;
+//   * bf16 data is summed in f32 registers (fixed source order, so every rank gets the
+//     same bits), scaled, and written as bf16 or f32;
+//   * every thread keeps kU 16-byte vectors (x up to 8 sources) in flight per step, so
+//     NVLink latency is covered by memory-level parallelism;
 //   * NVLS: multimem.ld_reduce sums all ranks' copies inside the NVSwitch, multimem.st
 //     broadcasts the result -- each GPU moves 1/n of the bytes once in each direction.
 #include <cuda_runtime.h>
@@ -20,7 +23,8 @@
 namespace gicc {
 namespace {
 
-constexpr int kMaxRanks = 16;
+constexpr int kMaxRanks = 8;  // one NVSwitch node
+constexpr int kU = 4;         // vectors per thread per step
 
 struct PeerPtrs {
   const void* p[kMaxRanks];
@@ -79,46 +83,85 @@ __device__ __forceinline__ int cta_handshake(const FlagPtrs& flags, int n, int m
   return st;
 }
 
+// Reduce vectors [lo, hi) of the n inputs; hand each finished vector to `emit(vec, acc)`.
+template <class Emit>
+__device__ __forceinline__ void reduce_range(const PeerPtrs& in, int n, size_t lo, size_t hi, Emit emit) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t v = lo + (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; v + (kU - 1) * stride < hi; v += kU * stride) {
+    uint4 x[kU][kMaxRanks];
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p)
+        if (p < n) x[u][p] = reinterpret_cast<const uint4*>(in.p[p])[v + u * stride];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p)
+        if (p < n) add_bf16x8(acc, x[u][p]);
+      emit(v + u * stride, acc);
+    }
+  }
+  for (; v < hi; v += stride) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p)
+      if (p < n) add_bf16x8(acc, reinterpret_cast<const uint4*>(in.p[p])[v]);
+    emit(v, acc);
+  }
+}
+
 // One-shot: every rank reads all inputs and writes the whole result locally.
-__global__ void __launch_bounds__(512) k_allreduce_oneshot(PeerPtrs in, void* out, size_t nvec, int n, int me,
+__global__ void __launch_bounds__(256) k_allreduce_oneshot(PeerPtrs in, void* out, size_t nvec, int n, int me,
                                                            float scale, int out_f32, FlagPtrs flags, int max_blocks,
                                                            uint64_t epoch, uint64_t timeout_ns, ErrorRecord* err) {
   if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) != GICC_OK) return;
-  for (size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += (size_t)gridDim.x * blockDim.x) {
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    uint4 x[kMaxRanks];
-#pragma unroll
-    for (int p = 0; p < kMaxRanks; ++p)
-      if (p < n) x[p] = reinterpret_cast<const uint4*>(in.p[p])[v];  // fixed order: same sum on every rank
-#pragma unroll
-    for (int p = 0; p < kMaxRanks; ++p)
-      if (p < n) add_bf16x8(acc, x[p]);
-    store8(out, v, acc, scale, out_f32);
-  }
+  reduce_range(in, n, 0, nvec, [&](size_t v, const float* acc) { store8(out, v, acc, scale, out_f32); });
   cta_handshake(flags, n, me, 1, max_blocks, epoch, timeout_ns, err);
 }
 
 // Two-shot: rank r reduces chunk r from all inputs and pushes it into every rank's output.
-__global__ void __launch_bounds__(512) k_allreduce_twoshot(PeerPtrs in, PeerOut out, size_t nvec, int n, int me,
+__global__ void __launch_bounds__(256) k_allreduce_twoshot(PeerPtrs in, PeerOut out, size_t nvec, int n, int me,
                                                            float scale, int out_f32, FlagPtrs flags, int max_blocks,
                                                            uint64_t epoch, uint64_t timeout_ns, ErrorRecord* err) {
   if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) != GICC_OK) return;
   const size_t per = (nvec + n - 1) / n;
   const size_t lo = per * me, hi = lo + per < nvec ? lo + per : nvec;
-  for (size_t v = lo + (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < hi; v += (size_t)gridDim.x * blockDim.x) {
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    uint4 x[kMaxRanks];
-#pragma unroll
-    for (int p = 0; p < kMaxRanks; ++p)
-      if (p < n) x[p] = reinterpret_cast<const uint4*>(in.p[p])[v];  // fixed order: same sum on every rank
-#pragma unroll
-    for (int p = 0; p < kMaxRanks; ++p)
-      if (p < n) add_bf16x8(acc, x[p]);
+  reduce_range(in, n, lo, hi, [&](size_t v, const float* acc) {
 #pragma unroll
     for (int p = 0; p < kMaxRanks; ++p)
       if (p < n) store8(out.p[(me + p) % n], v, acc, scale, out_f32);
-  }
+  });
   cta_handshake(flags, n, me, 1, max_blocks, epoch, timeout_ns, err);
+}
+
+__device__ __forceinline__ void nvls_emit(void* mc_out, size_t v, uint4 s, float scale, int out_f32) {
+  if (out_f32) {
+    float acc[8];
+    const uint32_t w[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      acc[2 * j] = ptx::bf16_lo(w[j]) * scale;
+      acc[2 * j + 1] = ptx::bf16_hi(w[j]) * scale;
+    }
+    uint4* o = reinterpret_cast<uint4*>(mc_out) + 2 * v;
+    ptx::multimem_st_v4(o, make_uint4(__float_as_uint(acc[0]), __float_as_uint(acc[1]), __float_as_uint(acc[2]),
+                                      __float_as_uint(acc[3])));
+    ptx::multimem_st_v4(o + 1, make_uint4(__float_as_uint(acc[4]), __float_as_uint(acc[5]), __float_as_uint(acc[6]),
+                                          __float_as_uint(acc[7])));
+  } else {
+    uint4 r = s;
+    if (scale != 1.0f) {
+      const uint32_t w[4] = {s.x, s.y, s.z, s.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = ptx::pack_bf16x2(ptx::bf16_lo(w[j]) * scale, ptx::bf16_hi(w[j]) * scale);
+      r = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    ptx::multimem_st_v4(reinterpret_cast<uint4*>(mc_out) + v, r);
+  }
 }
 
 // NVLS: rank r reduces chunk r inside the switch and multicasts the result.
@@ -128,50 +171,25 @@ __global__ void __launch_bounds__(512) k_allreduce_nvls(const void* mc_in, void*
   if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) != GICC_OK) return;
   const size_t per = (nvec + n - 1) / n;
   const size_t lo = per * me, hi = lo + per < nvec ? lo + per : nvec;
-  for (size_t v = lo + (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < hi; v += (size_t)gridDim.x * blockDim.x) {
-    const uint4 s = ptx::multimem_ld_reduce_bf16x8(reinterpret_cast<const uint4*>(mc_in) + v);
-    if (out_f32) {
-      float acc[8];
-      const uint32_t w[4] = {s.x, s.y, s.z, s.w};
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  const uint4* src = reinterpret_cast<const uint4*>(mc_in);
+  size_t v = lo + (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  constexpr int U = 2 * kU;
+  for (; v + (U - 1) * stride < hi; v += U * stride) {
+    uint4 s[U];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        acc[2 * j] = ptx::bf16_lo(w[j]) * scale;
-        acc[2 * j + 1] = ptx::bf16_hi(w[j]) * scale;
-      }
-      uint4* o = reinterpret_cast<uint4*>(mc_out) + 2 * v;
-      ptx::multimem_st_v4(o, make_uint4(__float_as_uint(acc[0]), __float_as_uint(acc[1]), __float_as_uint(acc[2]),
-                                        __float_as_uint(acc[3])));
-      ptx::multimem_st_v4(o + 1, make_uint4(__float_as_uint(acc[4]), __float_as_uint(acc[5]), __float_as_uint(acc[6]),
-                                            __float_as_uint(acc[7])));
-    } else {
-      uint4 r = s;
-      if (scale != 1.0f) {
-        const uint32_t w[4] = {s.x, s.y, s.z, s.w};
-        uint32_t o[4];
+    for (int u = 0; u < U; ++u) s[u] = ptx::multimem_ld_reduce_bf16x8(src + v + u * stride);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) o[j] = ptx::pack_bf16x2(ptx::bf16_lo(w[j]) * scale, ptx::bf16_hi(w[j]) * scale);
-        r = make_uint4(o[0], o[1], o[2], o[3]);
-      }
-      ptx::multimem_st_v4(reinterpret_cast<uint4*>(mc_out) + v, r);
-    }
+    for (int u = 0; u < U; ++u) nvls_emit(mc_out, v + u * stride, s[u], scale, out_f32);
   }
+  for (; v < hi; v += stride) nvls_emit(mc_out, v, ptx::multimem_ld_reduce_bf16x8(src + v), scale, out_f32);
   cta_handshake(flags, n, me, 1, max_blocks, epoch, timeout_ns, err);
 }
 
 // Plain multi-source reduction (callers order it with barriers): out = scale * sum(src).
-__global__ void __launch_bounds__(512) k_reduce(PeerPtrs src, int nsrc, void* out, size_t nvec, float scale,
+__global__ void __launch_bounds__(256) k_reduce(PeerPtrs src, int nsrc, void* out, size_t nvec, float scale,
                                                 int out_f32) {
-  for (size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += (size_t)gridDim.x * blockDim.x) {
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    uint4 x[kMaxRanks];
-#pragma unroll
-    for (int p = 0; p < kMaxRanks; ++p)
-      if (p < nsrc) x[p] = reinterpret_cast<const uint4*>(src.p[p])[v];
-#pragma unroll
-    for (int p = 0; p < kMaxRanks; ++p)
-      if (p < nsrc) add_bf16x8(acc, x[p]);
-    store8(out, v, acc, scale, out_f32);
-  }
+  reduce_range(src, nsrc, 0, nvec, [&](size_t v, const float* acc) { store8(out, v, acc, scale, out_f32); });
 }
 
 }  // namespace
@@ -180,7 +198,7 @@ namespace ops {
 
 void reduce_bf16(const void* const* srcs, int nsrc, void* out, size_t count, float scale, bool out_f32,
                  cudaStream_t s) {
-  if (nsrc < 1 || nsrc > kMaxRanks) throw std::runtime_error("gicc::reduce_bf16: 1..16 sources");
+  if (nsrc < 1 || nsrc > kMaxRanks) throw std::runtime_error("gicc::reduce_bf16: 1..8 sources");
   if (count % 8) throw std::runtime_error("gicc::reduce_bf16: count must be a multiple of 8");
   PeerPtrs p{};
   for (int i = 0; i < nsrc; ++i) {
@@ -188,15 +206,15 @@ void reduce_bf16(const void* const* srcs, int nsrc, void* out, size_t count, flo
     p.p[i] = srcs[i];
   }
   const size_t nvec = count / 8;
-  int blocks = (int)std::min<size_t>((nvec + 511) / 512, 4 * (size_t)num_sms());
-  k_reduce<<<blocks, 512, 0, s>>>(p, nsrc, out, nvec, scale, out_f32 ? 1 : 0);
+  int blocks = (int)std::min<size_t>(std::max<size_t>((nvec + 256 * kU - 1) / (256 * kU), 1), 4 * (size_t)num_sms());
+  k_reduce<<<blocks, 256, 0, s>>>(p, nsrc, out, nvec, scale, out_f32 ? 1 : 0);
   GICC_CUDA(cudaGetLastError());
 }
 
 void allreduce_bf16(int algo, const void* const* in, void* const* out, const void* mc_in, void* mc_out, int n, int me,
                     size_t count, float scale, bool out_f32, uint64_t* const* flag_bases, int max_blocks,
                     uint64_t epoch, uint64_t timeout_ns, int blocks, cudaStream_t s) {
-  if (n < 1 || n > kMaxRanks) throw std::runtime_error("gicc::allreduce: 1..16 ranks");
+  if (n < 1 || n > kMaxRanks) throw std::runtime_error("gicc::allreduce: 1..8 ranks (one NVSwitch node)");
   if (count % 8) throw std::runtime_error("gicc::allreduce: element count must be a multiple of 8");
   const size_t nvec = count / 8;
   PeerPtrs ip{};
@@ -208,16 +226,17 @@ void allreduce_bf16(int algo, const void* const* in, void* const* out, const voi
     fp.p[i] = flag_bases[i];
   }
   const size_t work = algo == ALLREDUCE_ONESHOT ? nvec : (nvec + n - 1) / n;
-  if (blocks <= 0) blocks = (int)std::min<size_t>(std::max<size_t>((work + 511) / 512, 1), 2 * (size_t)num_sms());
+  if (blocks <= 0)
+    blocks = (int)std::min<size_t>(std::max<size_t>((work + 256 * kU - 1) / (256 * kU), 1), 4 * (size_t)num_sms());
   if (blocks > max_blocks) blocks = max_blocks;
   ErrorRecord* err = device_error_record();
   switch (algo) {
     case ALLREDUCE_ONESHOT:
-      k_allreduce_oneshot<<<blocks, 512, 0, s>>>(ip, op.p[me], nvec, n, me, scale, out_f32, fp, max_blocks, epoch,
+      k_allreduce_oneshot<<<blocks, 256, 0, s>>>(ip, op.p[me], nvec, n, me, scale, out_f32, fp, max_blocks, epoch,
                                                  timeout_ns, err);
       break;
     case ALLREDUCE_TWOSHOT:
-      k_allreduce_twoshot<<<blocks, 512, 0, s>>>(ip, op, nvec, n, me, scale, out_f32, fp, max_blocks, epoch,
+      k_allreduce_twoshot<<<blocks, 256, 0, s>>>(ip, op, nvec, n, me, scale, out_f32, fp, max_blocks, epoch,
                                                  timeout_ns, err);
       break;
     case ALLREDUCE_NVLS:

@@ -34,10 +34,17 @@ __global__ void k_barrier_continuous(BarrierCtx* ctx, int n, uint64_t* counter) 
 
 // Grid-wide copy repeated `iters` times; the final fence makes every store performed at
 // system scope before the kernel ends, so kernel time == delivery time.
-__global__ void __launch_bounds__(512) k_copy(uint4* dst, const uint4* src, size_t nvec, int iters) {
+// window_vec > nvec: repetition `it` works on a different part of a window of window_vec
+// vectors (both sides), so repeated small copies do not just hit cached lines.
+__global__ void __launch_bounds__(512) k_copy(uint4* dst_base, const uint4* src_base, size_t nvec, int iters,
+                                              size_t window_vec) {
   const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
+  const size_t span = window_vec > nvec ? window_vec - nvec + 1 : 1;
   for (int it = 0; it < iters; ++it) {
+    const size_t off = ((size_t)it * nvec) % span;
+    uint4* dst = dst_base + off;
+    const uint4* src = src_base + off;
     size_t i = tid;
     for (; i + 3 * stride < nvec; i += 4 * stride) {
       const uint4 a = src[i], b = src[i + stride], c = src[i + 2 * stride], d = src[i + 3 * stride];
@@ -111,6 +118,26 @@ __global__ void k_pingpong(char* remote_buf, const char* local_buf, size_t bytes
   if (lane == 0 && out_ns) *out_ns = ptx::globaltimer() - t0;
 }
 
+// Same protocol with a whole CTA moving the message (large sizes).
+__global__ void __launch_bounds__(1024) k_pingpong_block(char* remote_buf, const char* local_buf, size_t bytes,
+                                                         uint64_t* remote_flag, const uint64_t* local_flag, int iters,
+                                                         int initiator, uint64_t base, uint64_t* out_ns,
+                                                         ErrorRecord* err, uint64_t timeout_ns, int rank) {
+  __shared__ int st;
+  uint64_t t0 = 0;
+  if (threadIdx.x == 0) t0 = ptx::globaltimer();
+  for (int i = 0; i < iters; ++i) {
+    const uint64_t ping = base + 2 * (uint64_t)i + 1, pong = ping + 1;
+    if (initiator) put_signal<Scope::Block>(remote_buf, local_buf, bytes, remote_flag, ping);
+    if (threadIdx.x == 0)
+      st = signal_wait_until(local_flag, proto::CMP_GE, initiator ? pong : ping, timeout_ns, err, rank, -1, W_PINGPONG);
+    __syncthreads();
+    if (st != GICC_OK) return;
+    if (!initiator) put_signal<Scope::Block>(remote_buf, local_buf, bytes, remote_flag, pong);
+  }
+  if (threadIdx.x == 0 && out_ns) *out_ns = ptx::globaltimer() - t0;
+}
+
 // put(8 B) + quiet() per iteration, timed on the device.
 __global__ void k_quiet_latency(uint64_t* remote, int iters, uint64_t* out_ns) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
@@ -157,7 +184,8 @@ void barrier_continuous(BarrierCtx* ctx, int n, uint64_t* counter, cudaStream_t 
   k_barrier_continuous<<<1, 32, 0, s>>>(ctx, n, counter);
   GICC_CUDA(cudaGetLastError());
 }
-void copy(void* dst, const void* src, size_t bytes, int iters, int blocks, int threads, cudaStream_t s) {
+void copy(void* dst, const void* src, size_t bytes, int iters, int blocks, int threads, cudaStream_t s,
+          size_t window) {
   if (bytes == 0) return;
   if (blocks <= 0) blocks = 2 * num_sms();
   if (threads <= 0) threads = 512;
@@ -165,7 +193,8 @@ void copy(void* dst, const void* src, size_t bytes, int iters, int blocks, int t
     const size_t nvec = bytes / 16;
     const size_t need = (nvec + threads - 1) / threads;
     if ((size_t)blocks > need) blocks = (int)need;
-    k_copy<<<blocks, threads, 0, s>>>(static_cast<uint4*>(dst), static_cast<const uint4*>(src), nvec, iters);
+    k_copy<<<blocks, threads, 0, s>>>(static_cast<uint4*>(dst), static_cast<const uint4*>(src), nvec, iters,
+                                      window / 16);
   } else {
     const size_t need = (bytes + threads - 1) / threads;
     if ((size_t)blocks > need) blocks = (int)need;
@@ -189,9 +218,14 @@ void signal(uint64_t* sig, uint64_t value, int op, cudaStream_t s) {
 void pingpong(void* remote_buf, const void* local_buf, size_t bytes, uint64_t* remote_flag, const uint64_t* local_flag,
               int iters, bool initiator, uint64_t base, uint64_t* out_ns, uint64_t timeout_ns, int rank,
               cudaStream_t s) {
-  k_pingpong<<<1, 32, 0, s>>>(static_cast<char*>(remote_buf), static_cast<const char*>(local_buf), bytes, remote_flag,
-                              local_flag, iters, initiator ? 1 : 0, base, out_ns, device_error_record(), timeout_ns,
-                              rank);
+  if (bytes >= 16384)
+    k_pingpong_block<<<1, 1024, 0, s>>>(static_cast<char*>(remote_buf), static_cast<const char*>(local_buf), bytes,
+                                        remote_flag, local_flag, iters, initiator ? 1 : 0, base, out_ns,
+                                        device_error_record(), timeout_ns, rank);
+  else
+    k_pingpong<<<1, 32, 0, s>>>(static_cast<char*>(remote_buf), static_cast<const char*>(local_buf), bytes,
+                                remote_flag, local_flag, iters, initiator ? 1 : 0, base, out_ns, device_error_record(),
+                                timeout_ns, rank);
   GICC_CUDA(cudaGetLastError());
 }
 void quiet_latency(uint64_t* remote, int iters, uint64_t* out_ns, cudaStream_t s) {

@@ -89,17 +89,31 @@ __global__ void __launch_bounds__(kThreads) k_jacobi(JacobiArgs p) {
   const size_t nx = (size_t)p.nx;
   const float* A = p.a;
 
-  auto ld4 = [&](int r) -> float4 {
-    return active ? __ldcs(reinterpret_cast<const float4*>(A + (size_t)r * nx + j0)) : make_float4(0, 0, 0, 0);
-  };
-  float4 up = ld4(r0 - 1), mid = ld4(r0);
+  // Issue every load of the run up front (kRun + 2 rows, plus the warp-edge columns) so
+  // ~20 independent 16-byte loads per thread are in flight: HBM latency is hidden by
+  // memory-level parallelism instead of occupancy.
+  float4 rows[kRun + 2];
+  float edge[kRun];
+#pragma unroll
+  for (int i = 0; i < kRun + 2; ++i) {
+    const int r = r0 - 1 + i;
+    rows[i] = (active && r <= r1) ? __ldcs(reinterpret_cast<const float4*>(A + (size_t)r * nx + j0))
+                                  : make_float4(0, 0, 0, 0);
+  }
+  const bool edge_lane = (lane == 0 && active && j0 > 0) || (lane == 31 && active && j0 + 4 < p.nx);
+  const int ecol = lane == 0 ? j0 - 1 : j0 + 4;
+#pragma unroll
+  for (int i = 0; i < kRun; ++i) edge[i] = (edge_lane && r0 + i < r1) ? A[(size_t)(r0 + i) * nx + ecol] : 0.f;
   float sq = 0.f;
-  for (int r = r0; r < r1; ++r) {
-    const float4 dn = ld4(r + 1);
+#pragma unroll
+  for (int i = 0; i < kRun; ++i) {
+    const int r = r0 + i;
+    if (r >= r1) break;
+    const float4 up = rows[i], mid = rows[i + 1], dn = rows[i + 2];
     float left = __shfl_up_sync(0xffffffffu, mid.w, 1);
     float right = __shfl_down_sync(0xffffffffu, mid.x, 1);
-    if (lane == 0 && active && j0 > 0) left = A[(size_t)r * nx + j0 - 1];
-    if (lane == 31 && active && j0 + 4 < p.nx) right = A[(size_t)r * nx + j0 + 4];
+    if (lane == 0 && active && j0 > 0) left = edge[i];
+    if (lane == 31 && active && j0 + 4 < p.nx) right = edge[i];
     float4 o;
     o.x = upd(mid.y, left, up.x, dn.x);
     o.y = upd(mid.z, mid.x, up.y, dn.y);
@@ -117,8 +131,6 @@ __global__ void __launch_bounds__(kThreads) k_jacobi(JacobiArgs p) {
         sq += dx * dx + dy * dy + dz * dz + dw * dw;
       }
     }
-    up = mid;
-    mid = dn;
   }
   if (p.norm) {
     for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
