@@ -1,0 +1,97 @@
+"""MoE expert-parallel layer benchmark: 4096 tokens per GPU, hidden
+7168, 256 experts (E/n per GPU), top-8 softmax routing (router logits N(0,1), seed 4),
+SwiGLU experts with intermediate 2048, weights N(0, 0.02).
+
+    python bench/moe_bench.py [--tokens 4096 ...]
+    torchrun --nproc-per-node N bench/moe_bench.py
+
+Reports the layer time (device, max over ranks) of this framework's fused path and of the
+NCCL all_to_all + cuBLAS per-expert arm, plus a numerics check of ours against the arm.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--tokens", type=int, default=4096)
+    ap.add_argument("--hidden", type=int, default=7168)
+    ap.add_argument("--experts", type=int, default=256)
+    ap.add_argument("--topk", type=int, default=8)
+    ap.add_argument("--inter", type=int, default=2048)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--no-baseline", action="store_true")
+    ap.add_argument("--out", default=None)
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    rt = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+        from opengda_b200.parallel import Runtime
+        rt = Runtime()
+    rank = rt.rank if rt else 0
+    from opengda_b200.models.moe import MoELayer, make_inputs
+    from opengda_b200.utils.timing import max_over_ranks
+
+    layer = MoELayer(args.tokens, args.hidden, args.experts, args.topk, args.inter, rt=rt)
+    x, logits = make_inputs(args.tokens, args.hidden, args.experts, rank, seed=4)
+
+    def timeit(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(s.elapsed_time(e) / steps)
+
+    ms = timeit(lambda: layer(x, logits), args.steps, args.warmup)
+    if rt:
+        rt.check_device_errors()
+    tflops = layer.flops() * world / (ms * 1e-3) / 1e12
+    res = {"metric": "moe_layer_us", "impl": "ours-fused", "n_gpus": world, "tokens_per_gpu": args.tokens,
+           "hidden": args.hidden, "experts": args.experts, "topk": args.topk, "inter": args.inter,
+           "layer_us": ms * 1e3, "tflops_total": tflops}
+    if not args.no_baseline:
+        from opengda_b200.baselines.moe_nccl import NcclMoE
+        base = NcclMoE(layer)
+        ours = layer(x, logits).float().clone()
+        ref = base(x, logits).float()
+        res["rel_err_vs_baseline"] = float(((ours - ref).norm() / ref.norm()).item())
+        ms_b = timeit(lambda: base(x, logits), max(2, args.steps // 2), 1)
+        res["nccl_torch"] = {"layer_us": ms_b * 1e3, "tflops_total": layer.flops() * world / (ms_b * 1e-3) / 1e12}
+    if rank == 0:
+        js = json.dumps(res)
+        print(js)
+        if args.out:
+            with open(args.out, "w") as f:
+                f.write(js + "\n")
+    if world > 1:
+        del layer
+        torch.cuda.synchronize()
+        rt.finalize()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

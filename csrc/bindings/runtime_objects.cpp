@@ -207,6 +207,56 @@ void bind_runtime_objects(py::module_& m) {
     a.out = P<void>(out); a.ldo = ldo; a.epoch = epoch; a.grid = grid; a.timeout_ns = timeout_ns;
     ops::gemm_rs(a, cur_stream());
   });
+  m.def("k_moe_route", [](uint64_t logits, int T, int E, int topk, uint64_t idx, uint64_t w, uint64_t counts) {
+    ops::moe_route(P<const float>(logits), T, E, topk, P<int>(idx), P<float>(w), P<int>(counts), cur_stream());
+  });
+  m.def("k_moe_forward", [](py::dict d) {
+    ops::MoeArgs a;
+    a.n = d["n"].cast<int>();
+    a.r = d["r"].cast<int>();
+    a.T = d["T"].cast<int>();
+    a.H = d["H"].cast<int>();
+    a.I = d["I"].cast<int>();
+    a.E = d["E"].cast<int>();
+    a.topk = d["topk"].cast<int>();
+    a.logits = P<const float>(d["logits"].cast<uint64_t>());
+    a.x = P<const void>(d["x"].cast<uint64_t>());
+    a.w1 = P<const void>(d["w1"].cast<uint64_t>());
+    a.w2 = P<const void>(d["w2"].cast<uint64_t>());
+    a.topk_idx = P<int>(d["topk_idx"].cast<uint64_t>());
+    a.topk_w = P<float>(d["topk_w"].cast<uint64_t>());
+    a.counts = P<int>(d["counts"].cast<uint64_t>());
+    auto vec = [&](const char* k) { return d[k].cast<std::vector<uint64_t>>(); };
+    auto ct = vec("count_tab"), pf = vec("plan_flags"), rv = vec("recv"), mt = vec("meta"), ar = vec("arrivals"),
+         cb = vec("comb"), ca = vec("comb_arrivals");
+    if ((int)ct.size() != a.n || a.n > 8) throw std::runtime_error("k_moe_forward: per-rank lists need n <= 8 entries");
+    for (int i = 0; i < a.n; ++i) {
+      a.count_tab[i] = P<void>(ct[i]);
+      a.plan_flags[i] = P<uint64_t>(pf[i]);
+      a.recv[i] = P<void>(rv[i]);
+      a.meta[i] = P<void>(mt[i]);
+      a.arrivals[i] = P<uint64_t>(ar[i]);
+      a.comb[i] = P<void>(cb[i]);
+      a.comb_arrivals[i] = P<uint64_t>(ca[i]);
+    }
+    a.h = P<void>(d["h"].cast<uint64_t>());
+    a.out = P<void>(d["out"].cast<uint64_t>());
+    a.cap_rows = d["cap_rows"].cast<int>();
+    a.epoch = d["epoch"].cast<uint64_t>();
+    a.timeout_ns = d["timeout_ns"].cast<uint64_t>();
+    py::dict w = d["ws"];
+    a.ws.dest_row_base = P<int>(w["dest_row_base"].cast<uint64_t>());
+    a.ws.key_base = P<int>(w["key_base"].cast<uint64_t>());
+    a.ws.key_cursor = P<int>(w["key_cursor"].cast<uint64_t>());
+    a.ws.expert_base = P<int>(w["expert_base"].cast<uint64_t>());
+    a.ws.expert_rows = P<int>(w["expert_rows"].cast<uint64_t>());
+    a.ws.mblk_prefix = P<int>(w["mblk_prefix"].cast<uint64_t>());
+    a.ws.cum_rows = P<uint64_t>(w["cum_rows"].cast<uint64_t>());
+    a.ws.cum_pairs = P<uint64_t>(w["cum_pairs"].cast<uint64_t>());
+    a.ws.send_pair = P<int>(w["send_pair"].cast<uint64_t>());
+    a.ws.send_row = P<int>(w["send_row"].cast<uint64_t>());
+    ops::moe_forward(a, cur_stream());
+  });
   m.def("k_fill_pattern", [](uint64_t buf, size_t n, uint32_t seed) { ops::fill_pattern(P<void>(buf), n, seed, cur_stream()); });
   m.def("k_check_pattern", [](uint64_t buf, size_t n, uint32_t seed, uint64_t bad) {
     ops::check_pattern(P<const void>(buf), n, seed, P<unsigned long long>(bad), cur_stream());

@@ -265,28 +265,46 @@ __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensor
       ptx::tc_fence_after();
       const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
       epi.begin_tile(ti, row);
+      if constexpr (Epi::kPairHalves) {
+        // columns c and c + BN/2 together (e.g. gate | up halves of a SwiGLU tile)
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        ptx::tmem_ld32(tbase + c, r);
-        ptx::tmem_ld_wait();
-        if constexpr (!Epi::kNeedsTileDone) {
-          if (c + 32 >= BN) {
-            // all TMEM reads of this accumulator are done: hand it back to the MMA warp
-            ptx::tc_fence_before();
-            ptx::mbar_arrive(&tempty[acc]);
+        for (int c = 0; c < BN / 2; c += 32) {
+          uint32_t lo[32], hi[32];
+          ptx::tmem_ld32(tbase + c, lo);
+          ptx::tmem_ld32(tbase + c + BN / 2, hi);
+          ptx::tmem_ld_wait();
+          if constexpr (!Epi::kNeedsTileDone) {
+            if (c + 32 >= BN / 2) {
+              ptx::tc_fence_before();
+              ptx::mbar_arrive(&tempty[acc]);
+            }
           }
+          epi.store_pair(ti, row, c, lo, hi);
         }
-        epi.store(ti, row, c, r);
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          ptx::tmem_ld32(tbase + c, r);
+          ptx::tmem_ld_wait();
+          if constexpr (!Epi::kNeedsTileDone) {
+            if (c + 32 >= BN) {
+              // all TMEM reads of this accumulator are done: hand it back to the MMA warp
+              ptx::tc_fence_before();
+              ptx::mbar_arrive(&tempty[acc]);
+            }
+          }
+          epi.store(ti, row, c, r);
+        }
       }
       epi.end_tile(ti, row);
       if constexpr (Epi::kNeedsTileDone) {
         // The last of the 4 epilogue warps to finish publishes the tile (e.g. releases a
         // flag on the owner GPU).  The accumulator is handed back only afterwards, so the
         // counter cannot mix two tiles.
+        Epi::fence_before_done();  // every thread: its own (possibly remote) stores first
         __syncwarp();
         if (lane == 0) {
-          Epi::fence_before_done();
           const uint32_t old = atomicAdd(epi_cnt, 1u);
           if (old == 3) {
             *epi_cnt = 0;

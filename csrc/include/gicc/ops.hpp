@@ -102,5 +102,45 @@ struct GemmRsArgs {
 GICC_EXPORT void ag_gemm(const AgGemmArgs& a, cudaStream_t s);
 GICC_EXPORT void gemm_rs(const GemmRsArgs& a, cudaStream_t s);
 
+// ---- MoE expert-parallel layer (moe.cu) -----------------------------------------------------
+struct MoeWorkspace {          // local device arrays
+  int* dest_row_base = nullptr;  // [E]
+  int* key_base = nullptr;       // [El*n + 1]
+  int* key_cursor = nullptr;     // [El*n]
+  int* expert_base = nullptr;    // [El]
+  int* expert_rows = nullptr;    // [El]
+  int* mblk_prefix = nullptr;    // [El+1]
+  uint64_t* cum_rows = nullptr;  // [n][El], zero-initialised once
+  uint64_t* cum_pairs = nullptr; // [1], zero-initialised once
+  int* send_pair = nullptr;      // [T*topk]
+  int* send_row = nullptr;       // [T*topk]
+};
+struct MoeArgs {
+  int n = 1, r = 0, T = 0, H = 0, I = 0, E = 0, topk = 8;
+  const float* logits = nullptr;  // [T][E] router logits
+  const void* x = nullptr;        // [T][H] bf16 tokens
+  const void* w1 = nullptr;       // [El][2I][H] bf16, rows interleaved per 128: gate blk, up blk
+  const void* w2 = nullptr;       // [El][H][I] bf16
+  int* topk_idx = nullptr;        // [T*topk]
+  float* topk_w = nullptr;        // [T*topk]
+  int* counts = nullptr;          // [E]
+  void* count_tab[8] = {};        // per rank: [n][E] int32 (parity of this call)
+  uint64_t* plan_flags[8] = {};   // per rank: [n] words
+  void* recv[8] = {};             // per rank: [cap][H] bf16 (parity of this call)
+  void* meta[8] = {};             // per rank: [cap] int4 (parity of this call)
+  uint64_t* arrivals[8] = {};     // per rank: [n][El] words
+  void* h = nullptr;              // [cap][I] bf16 local
+  void* comb[8] = {};             // per rank: [T*topk][H] bf16
+  uint64_t* comb_arrivals[8] = {};// per rank: [1] word
+  void* out = nullptr;            // [T][H] bf16
+  int cap_rows = 0;
+  uint64_t epoch = 0;             // call number >= 1
+  uint64_t timeout_ns = 0;
+  MoeWorkspace ws;
+};
+GICC_EXPORT void moe_route(const float* logits, int T, int E, int topk, int* topk_idx, float* topk_w, int* counts,
+                           cudaStream_t s);
+GICC_EXPORT void moe_forward(const MoeArgs& a, cudaStream_t s);
+
 }  // namespace ops
 }  // namespace gicc

@@ -226,8 +226,18 @@ void allreduce_bf16(int algo, const void* const* in, void* const* out, const voi
     fp.p[i] = flag_bases[i];
   }
   const size_t work = algo == ALLREDUCE_ONESHOT ? nvec : (nvec + n - 1) / n;
-  if (blocks <= 0)
-    blocks = (int)std::min<size_t>(std::max<size_t>((work + 256 * kU - 1) / (256 * kU), 1), 4 * (size_t)num_sms());
+  if (blocks <= 0) {
+    // Never more CTAs than can be resident at once: every CTA handshakes with its peers'
+    // CTA of the same index, so a second wave would run in lock-step across GPUs.
+    int per_sm = 1;
+    const void* fn = algo == ALLREDUCE_ONESHOT   ? (const void*)k_allreduce_oneshot
+                     : algo == ALLREDUCE_TWOSHOT ? (const void*)k_allreduce_twoshot
+                                                 : (const void*)k_allreduce_nvls;
+    const int threads = algo == ALLREDUCE_NVLS ? 512 : 256;
+    GICC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0));
+    const size_t resident = (size_t)std::max(per_sm, 1) * num_sms();
+    blocks = (int)std::min<size_t>(std::max<size_t>((work + threads * kU - 1) / (threads * kU), 1), resident);
+  }
   if (blocks > max_blocks) blocks = max_blocks;
   ErrorRecord* err = device_error_record();
   switch (algo) {

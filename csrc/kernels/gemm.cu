@@ -16,6 +16,7 @@ namespace gemm {
 // Epilogue: row-major bf16/f32 store of alpha * acc.
 struct StoreEpi {
   static constexpr bool kNeedsTileDone = false;
+  static constexpr bool kPairHalves = false;
   void* C;
   long long ldc;
   int M, N;

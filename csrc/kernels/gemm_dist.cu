@@ -156,6 +156,7 @@ struct AgSched {
 
 struct PlainStoreEpi {
   static constexpr bool kNeedsTileDone = false;
+  static constexpr bool kPairHalves = false;
   uint16_t* C;
   long long ldc;
   int M, N;
@@ -233,6 +234,7 @@ struct RsSched {
 
 struct RsEpi {
   static constexpr bool kNeedsTileDone = true;
+  static constexpr bool kPairHalves = false;
   int n, r, Mr, N, nbo, num_n, G;
   uint16_t* slots_peer[kMaxR];     // owner o's slot area [n][Mr][N] (this parity), mapped here
   const uint16_t* slots_local;     // my slot area

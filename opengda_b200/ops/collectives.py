@@ -59,7 +59,8 @@ class Allreduce:
         nbytes = count * 2
         if nbytes <= 256 * 1024 or self.n == 1:
             return ONESHOT
-        return NVLS if self.rt.multicast_supported else TWOSHOT
+        # NVLS moves 1/n of the data per GPU; with two ranks it saves nothing over two-shot
+        return NVLS if (self.rt.multicast_supported and self.n > 2) else TWOSHOT
 
     def __call__(self, count: int, algo: str = "auto", scale: float = 1.0, blocks: int = 0) -> torch.Tensor:
         if count % 8 or count > self.max_count:

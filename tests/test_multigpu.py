@@ -28,4 +28,5 @@ def test_multigpu_suite(tmp_path):
         for k in ("gemm_ag_relerr", "gemm_rs_relerr", "gemm_ag_fused_relerr", "gemm_rs_fused_relerr"):
             assert r[k] < 1e-2, (k, r)
         assert r["jacobi_mismatch"] == 0, r
+        assert r["moe_relerr"] < 2e-2, r
     print(json.dumps(res))

@@ -133,6 +133,21 @@ def main():
     field = np.concatenate(parts, axis=0)
     ref = jacobi_np(jnx, jny, jit)[1:-1]
     res["jacobi_mismatch"] = int((field != ref).sum())
+    # 8. MoE expert-parallel layer vs an fp32 reference (all experts' weights gathered)
+    from opengda_b200.models.moe import MoELayer, make_inputs, reference_moe
+    T, H, E, k, I = 256, 512, 8 * n, 4, 256
+    layer = MoELayer(T, H, E, k, I, rt=rt, weight_std=0.05)
+    cat = lambda t: torch.cat([q.cuda() for q in boot.allgather_obj(t.cpu())])  # noqa: E731
+    wg, wu, w2 = cat(layer.w_gate), cat(layer.w_up), cat(layer.w2)
+    worst = 0.0
+    for call in range(3):
+        x, logits = make_inputs(T, H, E, r, seed=20 + call)
+        y = layer(x, logits)
+        torch.cuda.synchronize()
+        rows = torch.arange(0, T, 16, device="cuda")
+        ref = reference_moe(x, logits, k, wg, wu, w2, rows)
+        worst = max(worst, float(((y[rows].float() - ref).norm() / ref.norm()).item()))
+    res["moe_relerr"] = worst
     rt.check_device_errors()
     torch.cuda.synchronize()
     boot.barrier()
