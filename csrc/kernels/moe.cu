@@ -69,19 +69,18 @@ __global__ void k_route(const float* logits, int T, int E, int topk, int* topk_i
   const float* l = logits + (size_t)warp * E;
   constexpr int kMaxPer = 32;
   float v[kMaxPer];
-  const int per = E / 32;
+  const int per = (E + 31) / 32;
   float mx = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < kMaxPer; ++i)
-    if (i < per) {
-      v[i] = l[i * 32 + lane];
-      mx = fmaxf(mx, v[i]);
-    }
+  for (int i = 0; i < kMaxPer; ++i) {
+    v[i] = (i < per && i * 32 + lane < E) ? l[i * 32 + lane] : -INFINITY;
+    mx = fmaxf(mx, v[i]);
+  }
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   float sum = 0.f;
 #pragma unroll
   for (int i = 0; i < kMaxPer; ++i)
-    if (i < per) sum += expf(v[i] - mx);
+    if (i < per && i * 32 + lane < E) sum += expf(v[i] - mx);
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   for (int k = 0; k < topk; ++k) {
     // lane-local best (lowest index on ties), then warp argmax
@@ -513,7 +512,7 @@ __global__ void k_combine(const uint16_t* comb, uint16_t* out, int T, int H, int
 namespace ops {
 
 void moe_route(const float* logits, int T, int E, int topk, int* topk_idx, float* topk_w, int* counts, cudaStream_t s) {
-  if (E % 32 || E > 1024 || topk < 1 || topk > 8) throw std::runtime_error("gicc::moe_route: E % 32 == 0, E <= 1024, k <= 8");
+  if (E < topk || E > 1024 || topk < 1 || topk > 8) throw std::runtime_error("gicc::moe_route: topk <= E <= 1024, k <= 8");
   GICC_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * E, s));
   const int warps_per_block = 8;
   moe::k_route<<<(T + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, s>>>(logits, T, E, topk,
