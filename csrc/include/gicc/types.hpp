@@ -12,7 +12,7 @@
 
 namespace gicc {
 
-constexpr int GICC_MAX_BUFS = 16;   // registered buffers per rank (reference: gicc_context.cuh:27-30)
+constexpr int GICC_MAX_BUFS = 64;   // registered buffers per rank (reference: 16, gicc_context.cuh:27-30)
 constexpr int GICC_MAX_PEERS = 64;  // ranks (reference: gicc_context.cuh:27-30, types.hpp:14)
 constexpr int GICC_POOL_SIZE = 32;  // host-queued ops per batch (reference: ofi_runtime.hpp:57)
 constexpr int GICC_MAX_ROUNDS = 12; // dissemination rounds, 4096 ranks (reference: gicc_barrier.hpp:55)

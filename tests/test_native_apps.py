@@ -1,0 +1,42 @@
+"""The native C++ programs (opengda_b200/bin/*) run under the local launcher."""
+import os
+import subprocess
+import sys
+
+import pytest
+
+from opengda_b200.parallel.launch import free_port
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+BIN = os.path.join(ROOT, "opengda_b200", "bin")
+
+pytestmark = pytest.mark.gpu
+
+
+def _launch(n, prog, *args):
+    cmd = [sys.executable, "-m", "opengda_b200.parallel.launch", "-n", str(n), "--port", str(free_port()),
+           "--timeout", "120", os.path.join(BIN, prog)] + [str(a) for a in args]
+    return subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=180,
+                          env=dict(os.environ, GICC_TIMEOUT_MS="5000"))
+
+
+def test_barrier_test_single_rank():
+    p = _launch(1, "gicc_barrier_test", 1000)
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert "PASS" in p.stdout
+
+
+@pytest.mark.multigpu
+def test_barrier_test_all_gpus():
+    import torch
+    n = min(torch.cuda.device_count(), 8)
+    p = _launch(n, "gicc_barrier_test", 10000)
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert p.stdout.count("PASS") == n
+
+
+@pytest.mark.multigpu
+def test_pingpong_two_ranks():
+    p = _launch(2, "gicc_pingpong", 200)
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert "PASS" in p.stdout
