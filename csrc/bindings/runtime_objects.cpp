@@ -3,6 +3,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <torch/extension.h>
 
+#include "gicc/am.hpp"
 #include "gicc/barrier.hpp"
 #include "gicc/ops.hpp"
 #include "gicc/runtime.hpp"
@@ -105,6 +106,36 @@ void bind_runtime_objects(py::module_& m) {
       .def("advance", &Barrier::advance)
       .def("count", &Barrier::count)
       .def_property_readonly("uses_nvls", &Barrier::uses_nvls);
+
+  py::class_<am::Am, std::shared_ptr<am::Am>>(m, "Am")
+      .def(py::init<Runtime&, int, uint32_t>(), py::arg("runtime"), py::arg("nslots") = am::AM_DEFAULT_RING_SLOTS,
+           py::arg("max_payload") = am::AM_MAX_PAYLOAD_SIZE, py::keep_alive<1, 2>())
+      .def("device_view", [](am::Am& a) { return A(a.device_view()); })
+      .def_property_readonly("nslots", &am::Am::nslots)
+      .def("send_handle",
+           [](am::Am& a, int dst, int handler, std::vector<uint64_t> args, bool request) {
+             am::am_args_t v{};
+             for (size_t i = 0; i < args.size() && i < 6; ++i) v.data[i] = args[i];
+             return a.send_handle(dst, (uint16_t)handler, v, request);
+           },
+           py::arg("dst"), py::arg("handler"), py::arg("args"), py::arg("request") = false)
+      .def("send_payload",
+           [](am::Am& a, int dst, int handler, std::vector<uint64_t> args, py::bytes payload) {
+             am::am_args_t v{};
+             for (size_t i = 0; i < args.size() && i < 6; ++i) v.data[i] = args[i];
+             std::string p = payload;
+             return a.send_payload(dst, (uint16_t)handler, v, p.data(), (uint32_t)p.size());
+           })
+      .def("check_can_send", &am::Am::check_can_send)
+      .def("poll_once", &am::Am::poll_once, py::arg("max_per_peer") = 64)
+      .def("reply", &am::Am::reply)
+      .def("wait_reply", &am::Am::wait_reply, py::call_guard<py::gil_scoped_release>())
+      .def("trigger_and_wait", &am::Am::trigger_and_wait)
+      .def("counter", &am::Am::counter)
+      .def("checksum", &am::Am::checksum);
+  m.def("k_am_pingpong", [](uint64_t view, int peer, int iters, int mode, bool initiator, uint64_t out_ns) {
+    ops::am_pingpong(P<am::AmView>(view), peer, iters, mode, initiator, P<unsigned long long>(out_ns), cur_stream());
+  });
 
   // ---- communication kernels (enqueued on torch's current stream) ----
   m.def("k_barrier_single", [](uint64_t ctx, uint64_t flag) { ops::barrier_single(P<BarrierCtx>(ctx), P<uint64_t>(flag), cur_stream()); });

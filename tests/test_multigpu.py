@@ -29,4 +29,5 @@ def test_multigpu_suite(tmp_path):
             assert r[k] < 1e-2, (k, r)
         assert r["jacobi_mismatch"] == 0, r
         assert r["moe_relerr"] < 2e-2, r
+        assert r["am_counter_ok"] and r["am_checksum_ok"], r
     print(json.dumps(res))

@@ -112,3 +112,17 @@ def test_nvshmem_style_api(rt):
     assert api.remote_ptr(p, 0) == p and api.my_pe() == 0 and api.n_pes() == 1
     assert api.context() != 0
     api.barrier()
+
+
+def test_active_messages_to_self(rt):
+    from opengda_b200.parallel.am import Am, CHECKSUM, COUNTER_ADD, ECHO
+    am = Am(rt, nslots=4, max_payload=512)
+    for i in range(10):  # more messages than slots: the poll returns credit
+        assert am.send_handle(0, COUNTER_ADD, [i + 1]) > 0
+        assert am.poll_once() == 1
+    assert am.counter() == sum(range(1, 11))
+    am.send_payload(0, CHECKSUM, [0], bytes(range(200)))
+    assert am.poll_once() == 1 and am.checksum() == sum(range(200))
+    seq = am.send_handle(0, ECHO, [1234], request=True)
+    assert am.poll_once() == 1
+    assert am.wait_reply(0, seq) == 1234

@@ -148,6 +148,29 @@ def main():
         ref = reference_moe(x, logits, k, wg, wu, w2, rows)
         worst = max(worst, float(((y[rows].float() - ref).norm() / ref.norm()).item()))
     res["moe_relerr"] = worst
+
+    # 9. active messages: host sends + device poll, device request/reply ping-pong
+    from opengda_b200.parallel.am import Am, CHECKSUM, COUNTER_ADD
+    am = Am(rt, nslots=8, max_payload=1024)
+    for i in range(20):  # more than the ring: exercises credits (receiver drains in between)
+        while not am.check_can_send(right):
+            am.poll_once()
+        am.send_handle(right, COUNTER_ADD, [r + 1])
+        am.poll_once()
+    payload = bytes((i * 7 + r) % 256 for i in range(1000))
+    am.send_payload(right, CHECKSUM, [0], payload)
+    import time as _t
+    t0 = _t.time()
+    while (am.counter() < 20 * (left + 1) or am.checksum() == 0) and _t.time() - t0 < 10:
+        am.poll_once()
+    res["am_counter_ok"] = am.counter() == 20 * (left + 1)
+    res["am_checksum_ok"] = am.checksum() == sum((i * 7 + left) % 256 for i in range(1000))
+    boot.barrier()
+    out = torch.zeros(1, dtype=torch.int64, device="cuda")
+    if r < 2:
+        am.pingpong(1 - r, 1000, "reqrep", r == 0, out.data_ptr())
+    torch.cuda.synchronize()
+    res["am_reqrep_rtt_us"] = out.item() / 1000 / 1e3 if r == 0 else None
     rt.check_device_errors()
     torch.cuda.synchronize()
     boot.barrier()
