@@ -71,6 +71,9 @@ def main():
     res = {"metric": "moe_layer_us", "impl": "ours-fused", "n_gpus": world, "tokens_per_gpu": args.tokens,
            "hidden": args.hidden, "experts": args.experts, "topk": args.topk, "inter": args.inter,
            "layer_us": ms * 1e3, "tflops_total": tflops}
+    # per-stage breakdown of one extra call (device events between the kernels)
+    layer(x, logits, stage_times=True)
+    res["stage_us_rank0"] = {k: round(v * 1e3, 1) for k, v in layer.last_stage_ms.items()}
     if not args.no_baseline:
         from opengda_b200.baselines.moe_nccl import NcclMoE
         base = NcclMoE(layer)

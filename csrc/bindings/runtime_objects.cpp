@@ -286,7 +286,14 @@ void bind_runtime_objects(py::module_& m) {
     a.ws.cum_pairs = P<uint64_t>(w["cum_pairs"].cast<uint64_t>());
     a.ws.send_pair = P<int>(w["send_pair"].cast<uint64_t>());
     a.ws.send_row = P<int>(w["send_row"].cast<uint64_t>());
+    std::vector<float> stage(6, 0.f);
+    const bool timed = d.contains("stage_times") && d["stage_times"].cast<bool>();
+    if (timed) a.stage_ms = stage.data();
     ops::moe_forward(a, cur_stream());
+    py::list out;
+    if (timed)
+      for (float v : stage) out.append(v);
+    return out;
   });
   m.def("k_fill_pattern", [](uint64_t buf, size_t n, uint32_t seed) { ops::fill_pattern(P<void>(buf), n, seed, cur_stream()); });
   m.def("k_check_pattern", [](uint64_t buf, size_t n, uint32_t seed, uint64_t bad) {

@@ -137,6 +137,7 @@ struct MoeArgs {
   uint64_t epoch = 0;             // call number >= 1
   uint64_t timeout_ns = 0;
   MoeWorkspace ws;
+  float* stage_ms = nullptr;      // optional host [6]: per-stage device time (synchronises)
 };
 GICC_EXPORT void moe_route(const float* logits, int T, int E, int topk, int* topk_idx, float* topk_w, int* counts,
                            cudaStream_t s);

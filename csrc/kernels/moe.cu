@@ -529,8 +529,17 @@ void moe_forward(const MoeArgs& a, cudaStream_t s) {
   const int pairs = a.T * a.topk;
   ErrorRecord* err = device_error_record();
   const uint64_t tmo = a.timeout_ns ? a.timeout_ns : default_timeout_ns();
+  // optional per-stage timing (profiling only: synchronises at the end)
+  cudaEvent_t ev[7] = {};
+  auto mark = [&](int i) {
+    if (a.stage_ms) GICC_CUDA(cudaEventRecord(ev[i], s));
+  };
+  if (a.stage_ms)
+    for (auto& e : ev) GICC_CUDA(cudaEventCreate(&e));
+  mark(0);
   // 1. route
   moe_route(a.logits, a.T, a.E, a.topk, a.topk_idx, a.topk_w, a.counts, s);
+  mark(1);
   // 2. plan
   moe::PlanArgs p{};
   p.n = n;
@@ -556,10 +565,12 @@ void moe_forward(const MoeArgs& a, cudaStream_t s) {
   p.timeout_ns = tmo;
   moe::k_plan<<<1, 256, 0, s>>>(p);
   GICC_CUDA(cudaGetLastError());
+  mark(2);
   // 3. sort
   moe::k_sort<<<(pairs + 255) / 256, 256, 0, s>>>(a.topk_idx, pairs, n, r, El, a.ws.key_base, a.ws.key_cursor,
                                                   a.ws.dest_row_base, a.ws.send_pair, a.ws.send_row);
   GICC_CUDA(cudaGetLastError());
+  mark(3);
   // 4. GEMM 1 (+ dispatch)
   const int G = num_sms();
   const CUtensorMap tA1 = make_tmap_2d(a.recv[r], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.cap_rows, a.H, a.H, BM, BK,
@@ -602,6 +613,7 @@ void moe_forward(const MoeArgs& a, cudaStream_t s) {
   }
   moe::k_moe_gemm1<<<G, cta_threads(moe::kCommWarps), smem, s>>>(tA1, tB1, g1, e1, err, tmo);
   GICC_CUDA(cudaGetLastError());
+  mark(4);
   // 5. GEMM 2 (+ combine push)
   const CUtensorMap tA2 = make_tmap_2d(a.h, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.cap_rows, a.I, a.I, BM, BK,
                                        CU_TENSOR_MAP_SWIZZLE_128B);
@@ -619,11 +631,18 @@ void moe_forward(const MoeArgs& a, cudaStream_t s) {
   }
   moe::k_moe_gemm2<<<G, kThreads, smem, s>>>(tA2, tB2, g2, e2, err, tmo, r);
   GICC_CUDA(cudaGetLastError());
+  mark(5);
   // 6. combine
   const uint64_t target = a.epoch * (uint64_t)pairs * (uint64_t)(a.H / 256);
   moe::k_combine<<<4 * G, 256, 0, s>>>(static_cast<const uint16_t*>(a.comb[r]), static_cast<uint16_t*>(a.out), a.T, a.H,
                                         a.topk, a.comb_arrivals[r], target, err, tmo, r);
   GICC_CUDA(cudaGetLastError());
+  mark(6);
+  if (a.stage_ms) {
+    GICC_CUDA(cudaEventSynchronize(ev[6]));
+    for (int i = 0; i < 6; ++i) GICC_CUDA(cudaEventElapsedTime(&a.stage_ms[i], ev[i], ev[i + 1]));
+    for (auto& e : ev) cudaEventDestroy(e);
+  }
 }
 
 }  // namespace ops

@@ -96,8 +96,12 @@ class MoELayer:
         self.epoch = 0
         self.launches_per_step = 7  # memset + route + plan + sort + gemm1 + gemm2 + combine
 
-    def forward(self, x: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
-        """x [T, H] bf16, logits [T, E] fp32 -> y [T, H] bf16 (this rank's tokens)."""
+    STAGES = ("route", "plan", "sort", "gemm1+dispatch", "gemm2+combine_push", "combine")
+
+    def forward(self, x: torch.Tensor, logits: torch.Tensor, stage_times: bool = False) -> torch.Tensor:
+        """x [T, H] bf16, logits [T, E] fp32 -> y [T, H] bf16 (this rank's tokens).
+        stage_times=True also records per-kernel device times into ``self.last_stage_ms``
+        (synchronises; profiling only)."""
         assert x.shape == (self.T, self.H) and x.dtype == torch.bfloat16 and x.is_contiguous()
         assert logits.shape == (self.T, self.E) and logits.dtype == torch.float32 and logits.is_contiguous()
         self.epoch += 1
@@ -119,8 +123,11 @@ class MoELayer:
             "out": self.out.data_ptr(), "cap_rows": self.cap, "epoch": self.epoch,
             "timeout_ns": self.rt.timeout_ns if self.rt is not None else 0,
             "ws": {k: v.data_ptr() for k, v in self.ws_t.items()},
+            "stage_times": stage_times,
         }
-        native().k_moe_forward(d)
+        st = native().k_moe_forward(d)
+        if stage_times:
+            self.last_stage_ms = dict(zip(self.STAGES, st))
         return self.out
 
     __call__ = forward
