@@ -84,6 +84,14 @@ void bind_runtime_objects(py::module_& m) {
       .def("prepare_trigger", [](Runtime& r, int slot, uint64_t epoch) { return A(r.prepare_trigger(Token{slot, epoch})); })
       .def("wait", [](Runtime& r, int slot, uint64_t epoch) { r.wait(Token{slot, epoch}); },
            py::call_guard<py::gil_scoped_release>())
+      .def("host_put",
+           [](Runtime& r, uint64_t src, int dest_rank, int dest_buf, size_t dst_off, size_t size) {
+             r.host_put(P<const void>(src), dest_rank, dest_buf, dst_off, size, cur_stream());
+           })
+      .def("host_get",
+           [](Runtime& r, uint64_t dst, int src_rank, int src_buf, size_t src_off, size_t size) {
+             r.host_get(P<void>(dst), src_rank, src_buf, src_off, size, cur_stream());
+           })
       .def("signal_alloc", &Runtime::signal_alloc)
       .def("signal_local", [](Runtime& r, size_t w) { return A(r.signal_local(w)); }, py::arg("word") = 0)
       .def("signal_peer", [](Runtime& r, int rank, size_t w) { return A(r.signal_peer(rank, w)); }, py::arg("rank"),
@@ -161,7 +169,10 @@ void bind_runtime_objects(py::module_& m) {
   m.def("k_quiet_latency", [](uint64_t remote, int iters, uint64_t out_ns) {
     ops::quiet_latency(P<uint64_t>(remote), iters, P<uint64_t>(out_ns), cur_stream());
   });
-  m.def("k_flush", [](uint64_t ctx, uint64_t status) { ops::flush_queued(P<DeviceCtx>(ctx), P<int>(status), cur_stream()); });
+  m.def("k_ctx_put", [](uint64_t ctx, uint64_t laddr, uint32_t lkey, uint64_t raddr, uint32_t rkey, uint32_t size) {
+    ops::ctx_put(P<DeviceCtx>(ctx), laddr, lkey, raddr, rkey, size, cur_stream());
+  });
+  m.def("k_flush",[](uint64_t ctx, uint64_t status) { ops::flush_queued(P<DeviceCtx>(ctx), P<int>(status), cur_stream()); });
   m.def("k_reduce_bf16", [](std::vector<uint64_t> srcs, uint64_t out, size_t count, float scale, bool out_f32) {
     std::vector<const void*> p;
     for (auto a : srcs) p.push_back(P<const void>(a));

@@ -126,7 +126,12 @@ __device__ __forceinline__ int signal_wait_until(const uint64_t* sig, int cmp, u
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ bool range_ok(const DeviceCtx* ctx, uint64_t laddr, uint32_t lkey, uint64_t raddr,
                                          uint32_t rkey, uint64_t size) {
-#if defined(GICC_CHECKS)
+  // Bounds checks: on when the context was prepared with GICC_CHECKS=1 in the environment
+  // (or the library was built with -DGICC_CHECKS).  A violation records GICC_ERANGE and the
+  // access is skipped -- never a trap.
+#if !defined(GICC_CHECKS)
+  if (!ctx->checks) return true;
+#endif
   const bool lok = lkey < (uint32_t)ctx->n_bufs && laddr >= ctx->local_base[lkey] &&
                    laddr + size <= ctx->local_base[lkey] + ctx->local_size[lkey];
   const bool rok = rkey < (uint32_t)ctx->n_bufs && raddr >= ctx->remote_base[rkey] &&
@@ -135,9 +140,6 @@ __device__ __forceinline__ bool range_ok(const DeviceCtx* ctx, uint64_t laddr, u
     report_error(ctx->err, GICC_ERANGE, W_BOUNDS, ctx->my_rank, ctx->peer, raddr, size);
     return false;
   }
-#else
-  (void)ctx; (void)laddr; (void)lkey; (void)raddr; (void)rkey; (void)size;
-#endif
   return true;
 }
 
@@ -208,20 +210,20 @@ template <Scope S = Scope::Thread>
 __device__ __forceinline__ void put(GiccContext* ctx, void* dst, const void* src, uint32_t size, int peer,
                                     bool signaled = true) {
   (void)signaled;
-#if defined(GICC_CHECKS)
-  bool ok = false;
-  const uint64_t d = (uint64_t)(uintptr_t)dst;
-  if (peer >= 0 && peer < ctx->n_ranks)
-    for (int b = 0; b < ctx->n_bufs; ++b)
-      ok |= d >= ctx->peer_base[peer][b] && d + size <= ctx->peer_base[peer][b] + ctx->size[b];
-  if (!ok) {
-    report_error(ctx->err, GICC_ERANGE, W_BOUNDS, ctx->my_rank, peer, d, size);
-    return;
-  }
-#else
-  (void)ctx;
-  (void)peer;
+#if !defined(GICC_CHECKS)
+  if (ctx->checks)
 #endif
+  {
+    bool ok = false;
+    const uint64_t d = (uint64_t)(uintptr_t)dst;
+    if (peer >= 0 && peer < ctx->n_ranks)
+      for (int b = 0; b < ctx->n_bufs; ++b)
+        ok |= d >= ctx->peer_base[peer][b] && d + size <= ctx->peer_base[peer][b] + ctx->size[b];
+    if (!ok) {
+      report_error(ctx->err, GICC_ERANGE, W_BOUNDS, ctx->my_rank, peer, d, size);
+      return;
+    }
+  }
   copy_bytes<S>(dst, src, size);
 }
 template <Scope S = Scope::Thread>

@@ -33,6 +33,8 @@ GICC_EXPORT void pingpong(void* remote_buf, const void* local_buf, size_t bytes,
                           uint64_t timeout_ns, int rank, cudaStream_t s);
 GICC_EXPORT void quiet_latency(uint64_t* remote, int iters, uint64_t* out_ns, cudaStream_t s);
 GICC_EXPORT void flush_queued(DeviceCtx* ctx, int* status, cudaStream_t s);
+GICC_EXPORT void ctx_put(DeviceCtx* ctx, uint64_t laddr, uint32_t lkey, uint64_t raddr, uint32_t rkey, uint32_t size,
+                         cudaStream_t s);
 GICC_EXPORT void fill_pattern(void* buf, size_t n, uint32_t seed, cudaStream_t s);
 GICC_EXPORT void check_pattern(const void* buf, size_t n, uint32_t seed, unsigned long long* bad, cudaStream_t s);
 

@@ -172,8 +172,7 @@ GICC_HD int poll_peer_builtin(AmView& v, int src, int max_msgs) {
 template <class Mem>
 GICC_HD int poll_all_builtin(AmView& v, int max_per_peer) {
   int n = 0;
-  for (int p = 0; p < v.size; ++p)
-    if (p != v.rank) n += poll_peer_builtin<Mem>(v, p, max_per_peer);
+  for (int p = 0; p < v.size; ++p) n += poll_peer_builtin<Mem>(v, p, max_per_peer);  // self included
   return n;
 }
 

@@ -70,6 +70,11 @@ class GICC_EXPORT Runtime {
   DeviceCtx* prepare_trigger(Token t);  // ctx whose flush() runs the queued ops
   void wait(Token t);                   // host wait (bounded) for the op's completion
 
+  // --- host-driven transfers (copy engine; reference host verbs path, mlx5/comm.hpp:170-255)
+  void host_put(const void* src_local, int dest_rank, int dest_buf, size_t dst_off, size_t size, cudaStream_t s);
+  void host_get(void* dst_local, int src_rank, int src_buf, size_t src_off, size_t size, cudaStream_t s);
+  bool checks_enabled() const;  // GICC_CHECKS=1: device contexts bounds-check every put
+
   // --- additions ------------------------------------------------------------------------
   // Symmetric allocation, registered under the next index (not collective by itself; all
   // ranks must allocate the same sequence and then call exchange()).

@@ -57,7 +57,7 @@ struct DeviceCtx {
   int n_bufs;
   uint64_t remote_addr;  // default destination (peer buffer chosen at prepare)
   uint32_t remote_rkey;
-  uint32_t pad0;
+  uint32_t checks;      // 1: bounds-check every put (GICC_CHECKS=1 at prepare time)
   uint64_t local_base[GICC_MAX_BUFS];
   uint64_t local_size[GICC_MAX_BUFS];
   uint64_t remote_base[GICC_MAX_BUFS];  // peer's buffers, mapped here
@@ -74,7 +74,7 @@ struct GiccContext {
   int my_rank;
   int n_ranks;
   int n_bufs;
-  int pad0;
+  int checks;  // 1: bounds-check every put (GICC_CHECKS=1 at build_context time)
   uint64_t local_base[GICC_MAX_BUFS];
   uint64_t size[GICC_MAX_BUFS];
   uint64_t peer_base[GICC_MAX_PEERS][GICC_MAX_BUFS];  // [rank][buf]; [my_rank] = local

@@ -138,6 +138,13 @@ __global__ void __launch_bounds__(1024) k_pingpong_block(char* remote_buf, const
   if (threadIdx.x == 0 && out_ns) *out_ns = ptx::globaltimer() - t0;
 }
 
+// Reference-signature put through a DeviceCtx (one warp), then quiet.
+__global__ void k_ctx_put(DeviceCtx* ctx, uint64_t laddr, uint32_t lkey, uint64_t raddr, uint32_t rkey,
+                          uint32_t size) {
+  put<Scope::Warp>(ctx, laddr, lkey, raddr, rkey, size);
+  quiet();
+}
+
 // put(8 B) + quiet() per iteration, timed on the device.
 __global__ void k_quiet_latency(uint64_t* remote, int iters, uint64_t* out_ns) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
@@ -230,6 +237,11 @@ void pingpong(void* remote_buf, const void* local_buf, size_t bytes, uint64_t* r
 }
 void quiet_latency(uint64_t* remote, int iters, uint64_t* out_ns, cudaStream_t s) {
   k_quiet_latency<<<1, 32, 0, s>>>(remote, iters, out_ns);
+  GICC_CUDA(cudaGetLastError());
+}
+void ctx_put(DeviceCtx* ctx, uint64_t laddr, uint32_t lkey, uint64_t raddr, uint32_t rkey, uint32_t size,
+             cudaStream_t s) {
+  k_ctx_put<<<1, 32, 0, s>>>(ctx, laddr, lkey, raddr, rkey, size);
   GICC_CUDA(cudaGetLastError());
 }
 void flush_queued(DeviceCtx* ctx, int* status, cudaStream_t s) {

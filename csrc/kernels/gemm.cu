@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include "gicc/device/gemm_core.cuh"
+#include "gicc/device/gemm_core2.cuh"
 #include "gicc/host_util.hpp"
 #include "gicc/ops.hpp"
 
@@ -104,6 +105,70 @@ static void launch_plain(const void* A, const void* B, void* C, int M, int N, in
   GICC_CUDA(cudaGetLastError());
 }
 
+// ---- CTA-pair (cta_group::2) variant: 256 x 256 tiles per cluster of two CTAs ----
+struct PairPlainSched {
+  int M, N, K;
+  int num_m, num_n, group_m;
+  static constexpr int kCommWarps = 0;
+  __device__ int num_tiles() const { return num_m * num_n; }
+  __device__ TileInfo tile(int t) const {
+    int mb, nb;
+    raster(t, num_m, num_n, group_m, mb, nb);
+    TileInfo ti;
+    ti.m0 = mb * 2 * BM;
+    ti.n0 = nb * pair::BN2;
+    ti.a_row = ti.m0;
+    ti.b_row = ti.n0;
+    ti.kb0 = 0;
+    ti.kb1 = (K + BK - 1) / BK;
+    ti.aux = 0;
+    ti.aux2 = 0;
+    return ti;
+  }
+  __device__ bool producer_wait(const TileInfo&, uint64_t, volatile int*, ErrorRecord*) const { return true; }
+};
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    k_gemm_bf16_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     PairPlainSched sched, StoreEpi epi, ErrorRecord* err, uint64_t timeout_ns) {
+  pair::gemm_core_pair(&tmA, &tmB, sched, epi, err, timeout_ns, -1);
+}
+
+static void launch_pair(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
+                        long long ldc, bool out_f32, float alpha, cudaStream_t stream) {
+  const CUtensorMap tA = make_tmap_2d(A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, lda, BM, BK,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tB = make_tmap_2d(B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldb, pair::BN2 / 2, BK,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  PairPlainSched s;
+  s.M = M;
+  s.N = N;
+  s.K = K;
+  s.num_m = (M + 2 * BM - 1) / (2 * BM);
+  s.num_n = (N + pair::BN2 - 1) / pair::BN2;
+  s.group_m = 8;
+  StoreEpi e;
+  e.C = C;
+  e.ldc = ldc;
+  e.M = M;
+  e.N = N;
+  e.alpha = alpha;
+  e.out_f32 = out_f32 ? 1 : 0;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  GICC_CUDA(cudaGetDevice(&dev));
+  if (!attr_set[dev]) {
+    GICC_CUDA(cudaFuncSetAttribute(k_gemm_bf16_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, pair::kSmemBytes));
+    attr_set[dev] = true;
+  }
+  const int pairs_max = num_sms(dev) / 2;
+  const int tiles = s.num_m * s.num_n;
+  const int grid = 2 * (tiles < pairs_max ? tiles : pairs_max);
+  k_gemm_bf16_pair<<<grid, kThreads, pair::kSmemBytes, stream>>>(tA, tB, s, e, device_error_record(),
+                                                                  default_timeout_ns());
+  GICC_CUDA(cudaGetLastError());
+}
+
 }  // namespace gemm
 
 namespace ops {
@@ -119,7 +184,8 @@ void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long 
   switch (bn) {
     case 256: gemm::launch_plain<256>(A, B, C, M, N, K, lda, ldb, ldc, out_f32, alpha, stream); break;
     case 128: gemm::launch_plain<128>(A, B, C, M, N, K, lda, ldb, ldc, out_f32, alpha, stream); break;
-    default: throw std::runtime_error("gicc::gemm_bf16: bn must be 128 or 256");
+    case 512: gemm::launch_pair(A, B, C, M, N, K, lda, ldb, ldc, out_f32, alpha, stream); break;  // CTA pairs
+    default: throw std::runtime_error("gicc::gemm_bf16: bn must be 128, 256 or 512 (CTA pairs)");
   }
 }
 

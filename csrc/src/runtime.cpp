@@ -502,6 +502,7 @@ DeviceCtx* Runtime::prepare(int peer, int remote_buf_index) {
   c.ops = ops_dev_;
   c.err = err_;
   c.timeout_ns = timeout_ns_;
+  c.checks = checks_enabled() ? 1u : 0u;
   void* d = nullptr;
   GICC_CUDA(cudaMalloc(&d, sizeof(c)));
   GICC_CUDA(cudaMemcpy(d, &c, sizeof(c), cudaMemcpyHostToDevice));
@@ -532,6 +533,7 @@ GiccContext* Runtime::build_context() {
   c->sig_mc = signal_multicast(0);
   c->err = err_;
   c->timeout_ns = timeout_ns_;
+  c->checks = checks_enabled() ? 1 : 0;
   void* d = nullptr;
   GICC_CUDA(cudaMalloc(&d, sizeof(GiccContext)));
   GICC_CUDA(cudaMemcpy(d, c.get(), sizeof(GiccContext), cudaMemcpyHostToDevice));
@@ -550,6 +552,24 @@ void Runtime::reset() {
 }
 
 void Runtime::barrier() { boot_->barrier(); }
+
+bool Runtime::checks_enabled() const {
+  const char* s = std::getenv("GICC_CHECKS");
+  return s && std::atoi(s) != 0;
+}
+
+void Runtime::host_put(const void* src_local, int dest_rank, int dest_buf, size_t dst_off, size_t size,
+                       cudaStream_t s) {
+  const Region& r = *regions_.at(dest_buf);
+  if (dst_off + size > r.size) throw std::runtime_error("gicc::Runtime::host_put: range outside the buffer");
+  GICC_CUDA(cudaMemcpyAsync(remote_ptr(dest_rank, dest_buf, dst_off), src_local, size, cudaMemcpyDeviceToDevice, s));
+}
+
+void Runtime::host_get(void* dst_local, int src_rank, int src_buf, size_t src_off, size_t size, cudaStream_t s) {
+  const Region& r = *regions_.at(src_buf);
+  if (src_off + size > r.size) throw std::runtime_error("gicc::Runtime::host_get: range outside the buffer");
+  GICC_CUDA(cudaMemcpyAsync(dst_local, remote_ptr(src_rank, src_buf, src_off), size, cudaMemcpyDeviceToDevice, s));
+}
 
 Token Runtime::put_no_db(const Buffer& src, int dest_rank, int dest_buf_index, size_t size, size_t src_off,
                          size_t dst_off) {

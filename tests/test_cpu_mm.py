@@ -1,0 +1,7 @@
+"""BASELINE config 1 on CPU gloo ranks: row-block A, broadcast B, gathered C, rtol 1e-5."""
+from opengda_b200.models.cpu_mm import run
+
+
+def test_cpu_distributed_matmul_world2():
+    res = run(2)
+    assert res.get("ok") is True, res

@@ -50,3 +50,18 @@ def test_gemm_strided_views():
     check_errors()
     ref = _ref(A, B)
     assert (C.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item()
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (512, 768, 1024), (300, 520, 136), (2048, 2048, 4096)])
+def test_gemm_cta_pair_matches_fp32_reference(M, N, K):
+    """The cta_group::2 variant (256 x 256 tiles on CTA pairs)."""
+    from opengda_b200.ops.gemm import gemm, check_errors
+    g = torch.Generator(device="cuda").manual_seed(M + 11 * N + K)
+    A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    B = torch.randn(N, K, device="cuda", generator=g).to(torch.bfloat16)
+    C = gemm(A, B, bn=512)
+    torch.cuda.synchronize()
+    check_errors()
+    ref = _ref(A, B)
+    err = (C.float() - ref).abs().max().item()
+    assert err <= 1e-2 * ref.abs().max().item() + 1e-2, err

@@ -126,3 +126,36 @@ def test_active_messages_to_self(rt):
     seq = am.send_handle(0, ECHO, [1234], request=True)
     assert am.poll_once() == 1
     assert am.wait_reply(0, seq) == 1234
+
+
+def test_bounds_checked_put_records_erange_and_skips(rt, monkeypatch):
+    """GICC_CHECKS=1: an out-of-range put through a DeviceCtx is refused and recorded."""
+    n = _n()
+    src = rt.alloc_tensor((4096,), torch.uint8)
+    dst = rt.alloc_tensor((4096,), torch.uint8)
+    src.local.fill_(7)
+    dst.local.zero_()
+    monkeypatch.setenv("GICC_CHECKS", "1")
+    ctx = rt.prepare(0, dst.index)
+    n.read_errors(True)
+    # in range: lands
+    n.k_ctx_put(ctx, src.ptr(), src.index, dst.ptr(0), dst.index, 1024)
+    torch.cuda.synchronize()
+    assert n.read_errors(True)["code"] == 0 and int(dst.local[:1024].sum()) == 7 * 1024
+    # past the end of the destination: refused, nothing written beyond
+    dst.local.zero_()
+    n.k_ctx_put(ctx, src.ptr(), src.index, dst.ptr(0) + 4000, dst.index, 1024)
+    torch.cuda.synchronize()
+    rec = n.read_errors(True)
+    assert rec["status"] == "ERANGE" and rec["where"] == "bounds"
+    assert int(dst.local.sum()) == 0
+
+
+def test_host_put_get(rt):
+    a = rt.alloc_tensor((1 << 20,), torch.uint8)
+    x = torch.randint(0, 255, (1 << 20,), dtype=torch.uint8, device="cuda")
+    rt.native.host_put(x.data_ptr(), 0, a.index, 0, 1 << 20)
+    y = torch.empty_like(x)
+    rt.native.host_get(y.data_ptr(), 0, a.index, 0, 1 << 20)
+    torch.cuda.synchronize()
+    assert torch.equal(x, y) and torch.equal(a.local, x)
