@@ -296,30 +296,56 @@ struct G1Sched {
     const int tid = cw * 32 + lane;
     constexpr int kT = kCommWarps * 32;
     const int nvec = H / 8;  // 16-byte vectors per row
-    for (int p = blockIdx.x; p < npairs; p += G) {
+    constexpr int kBatch = 4;  // rows per fence / barrier
+    constexpr int kVec = 8;    // vectors in flight per thread
+    // CTA c owns pairs c, c+G, c+2G, ... (send order, so every owner's first expert
+    // completes first); kBatch of them share one fence and one barrier.
+    for (int p0 = blockIdx.x; p0 < npairs; p0 += G * kBatch) {
       // one thread samples the CTA's abort flag; all comm threads leave together
       if (tid == 0) comm_stop = *abort_flag;
       asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
       if (comm_stop) break;
-      const int pair = send_pair[p];
-      const int row = send_row[p];
-      const int tok = pair / topk;
-      const int g = topk_idx[pair];
-      const int d = g / El, e = g - (g / El) * El;
-      const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)tok * H);
-      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(recv.p[d]) + (size_t)row * H);
-      for (int i = tid; i < nvec; i += kT) ptx::st_v4_na(dst + i, ptx::ld_v4_nc(src + i));
-      if (tid == 0) {
-        int4 m;
-        m.x = r;
-        m.y = pair;
-        m.z = __float_as_int(topk_w[pair]);
-        m.w = 0;
-        reinterpret_cast<int4*>(meta.p[d])[row] = m;
+#pragma unroll 1
+      for (int j = 0; j < kBatch; ++j) {
+        const int p = p0 + j * G;
+        if (p >= npairs) break;
+        const int pair = send_pair[p];
+        const int row = send_row[p];
+        const int tok = pair / topk;
+        const int d = topk_idx[pair] / El;
+        const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)tok * H);
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(recv.p[d]) + (size_t)row * H);
+        for (int i0 = 0; i0 < nvec; i0 += kVec * kT) {
+          uint4 v[kVec];
+#pragma unroll
+          for (int u = 0; u < kVec; ++u) {
+            const int i = i0 + u * kT + tid;
+            if (i < nvec) v[u] = ptx::ld_v4_nc(src + i);
+          }
+#pragma unroll
+          for (int u = 0; u < kVec; ++u) {
+            const int i = i0 + u * kT + tid;
+            if (i < nvec) ptx::st_v4_na(dst + i, v[u]);
+          }
+        }
+        if (tid == 0) {
+          int4 m;
+          m.x = r;
+          m.y = pair;
+          m.z = __float_as_int(topk_w[pair]);
+          m.w = 0;
+          reinterpret_cast<int4*>(meta.p[d])[row] = m;
+        }
       }
       ptx::fence_acq_rel_sys();
       asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
-      if (tid == 0) ptx::red_release_sys_add(arrivals_peer.p[d] + (size_t)r * El + e, 1);
+      if (tid < kBatch) {
+        const int p = p0 + tid * G;
+        if (p < npairs) {
+          const int g = topk_idx[send_pair[p]];
+          ptx::red_release_sys_add(arrivals_peer.p[g / El] + (size_t)r * El + (g - (g / El) * El), 1);
+        }
+      }
     }
   }
 };
