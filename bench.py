@@ -43,7 +43,8 @@ def main() -> int:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "nccl"],
+                    help="nccl: the NCCL + cuBLAS comparison arm (same shapes, library kernels only)")
     ap.add_argument("--mode", default="ag", choices=["ag", "rs"])
     ap.add_argument("--size", type=int, default=16384)
     ap.add_argument("--e2e-steps", type=int, default=None)
@@ -78,7 +79,12 @@ def main() -> int:
     from opengda_b200.utils.clocks import ClockSampler
 
     M = N = K = args.size
-    model = DistGemm(M, N, K, args.mode, rt=rt, device=dev, fused=not args.unfused)
+    if args.impl == "nccl":
+        from opengda_b200.baselines.gemm_nccl import NcclDistGemm
+
+        model = NcclDistGemm(M, N, K, args.mode, device=dev)
+    else:
+        model = DistGemm(M, N, K, args.mode, rt=rt, device=dev, fused=not args.unfused)
     A, B, (Afull, Bfull) = make_operands(M, N, K, args.mode, world, rank, seed=2, device=dev)
     # numerics spot check (one row block) before timing
     C = model(A, B)
@@ -95,7 +101,7 @@ def main() -> int:
     rel = ((got - ref).norm() / ref.norm()).item()
     del Afull, Bfull
     torch.cuda.empty_cache()
-    zero_copy = world > 1 and args.mode == "ag"
+    zero_copy = world > 1 and args.mode == "ag" and args.impl == "ours"
     if zero_copy:  # the shard lives in the symmetric landing buffers (both parities)
         model.a_slot(0).copy_(A)
         model.a_slot(1).copy_(A)
@@ -184,11 +190,12 @@ def main() -> int:
                 "l2": "inputs exceed L2 (A_full 512 MiB > 126 MB), no flush",
                 "numerics_rel_err_vs_fp32": round(rel, 6),
             },
-            "impl": "ours",
+            "impl": args.impl,
             "clocks": clocks,
             "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 4),
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
-                    "api": "opengda_b200.models.dist_gemm.DistGemm.__call__"},
+                    "api": ("opengda_b200.baselines.gemm_nccl.NcclDistGemm.__call__" if args.impl == "nccl"
+                            else "opengda_b200.models.dist_gemm.DistGemm.__call__")},
             "gpu_launches": model.launches_per_step * args.steps,
         }
         print(json.dumps(out))

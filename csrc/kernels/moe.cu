@@ -157,15 +157,26 @@ __global__ void __launch_bounds__(256) k_plan(PlanArgs a) {
   __syncthreads();
   if (!ok) return;
   const int* C = reinterpret_cast<const int*>(a.count_tab.p[r]);  // [n][E], complete now
-  // (3) per global expert g: where my rows start on its owner
+  // (3) per global expert g: where my rows start on its owner.  Segment sizes go to shared
+  // memory first; one thread per owner scans its segment list (no dependent global loads).
+  __shared__ int seg[1024];  // E <= 1024: padded rows of expert g on its owner, then its base
   for (int g = t; g < E; g += blockDim.x) {
-    const int d = g / El, e = g % El;
+    int rows = 0;
+    for (int s = 0; s < n; ++s) rows += C[(size_t)s * E + g];
+    seg[g] = pad128(rows);
+  }
+  __syncthreads();
+  if (t < n) {
     int base = 0;
-    for (int e2 = 0; e2 < e; ++e2) {
-      int rows = 0;
-      for (int s = 0; s < n; ++s) rows += C[(size_t)s * E + d * El + e2];
-      base += pad128(rows);
+    for (int e = 0; e < El; ++e) {
+      const int sz = seg[t * El + e];
+      seg[t * El + e] = base;
+      base += sz;
     }
+  }
+  __syncthreads();
+  for (int g = t; g < E; g += blockDim.x) {
+    int base = seg[g];
     for (int s = 0; s < r; ++s) base += C[(size_t)s * E + g];
     a.dest_row_base[g] = base;
   }
