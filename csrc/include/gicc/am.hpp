@@ -31,7 +31,8 @@ class GICC_EXPORT Am {
   uint32_t slot_bytes() const { return slot_bytes_; }
 
   // Host-initiated sends (two copies: slot body, then its seq).  Return the sequence
-  // number, or 0 when the receiver has no free slot (check_can_send was false).
+  // number, or 0 when the receiver has no free slot (check_can_send was false).  Host and
+  // device sends share one send cursor per direction, so they may be mixed in stream order.
   uint64_t send_handle(int dst, uint16_t handler, const am_args_t& args, bool request = false);
   uint64_t send_payload(int dst, uint16_t handler, const am_args_t& args, const void* payload, uint32_t len);
   bool check_can_send(int dst);
@@ -46,6 +47,7 @@ class GICC_EXPORT Am {
   void trigger_and_wait() { cudaDeviceSynchronize(); }
 
  private:
+  uint64_t head(int dst);  // messages sent to dst so far (device-resident cursor)
   uint64_t host_send(int dst, uint16_t handler, const am_args_t& args, const void* payload, uint32_t len,
                      uint8_t flags);
   Runtime& rt_;
@@ -54,7 +56,6 @@ class GICC_EXPORT Am {
   int buf_;
   AmView view_{};           // host copy (device pointers)
   AmView* dview_ = nullptr;
-  std::vector<uint64_t> head_;  // host-driven directions
   int* dcount_ = nullptr;
 };
 

@@ -118,7 +118,10 @@ __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensor
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint32_t* epi_cnt = tmem_slot + 2;  // epilogue warps finished with the current tile
+  // Per accumulator: how many epilogue warps have finished a tile held in it (monotonic).
+  // One counter per accumulator, because a fast warp can finish the tile in the other
+  // accumulator before a slow warp finishes this one.
+  uint32_t* epi_cnt = tmem_slot + 2;
 
   const uint32_t warp = ptx::warp_id();
   const uint32_t lane = ptx::lane_id();
@@ -134,7 +137,8 @@ __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensor
     }
     ptx::mbar_init(drain, 1);
     *abort_flag = 0;
-    *epi_cnt = 0;
+    epi_cnt[0] = 0;
+    epi_cnt[1] = 0;
     ptx::fence_mbar_init();
     ptx::prefetch_tmap(tmA);
     ptx::prefetch_tmap(tmB);
@@ -301,13 +305,13 @@ __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensor
       if constexpr (Epi::kNeedsTileDone) {
         // The last of the 4 epilogue warps to finish publishes the tile (e.g. releases a
         // flag on the owner GPU).  The accumulator is handed back only afterwards, so the
-        // counter cannot mix two tiles.
+        // next tile in this accumulator cannot start counting before this one is complete;
+        // the tile in the other accumulator counts on its own counter.
         Epi::fence_before_done();  // every thread: its own (possibly remote) stores first
         __syncwarp();
         if (lane == 0) {
-          const uint32_t old = atomicAdd(epi_cnt, 1u);
-          if (old == 3) {
-            *epi_cnt = 0;
+          const uint32_t old = atomicAdd(&epi_cnt[acc], 1u);
+          if ((old & 3u) == 3u) {
             Epi::fence_before_done();
             epi.tile_done(ti);
           }

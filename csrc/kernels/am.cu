@@ -101,7 +101,6 @@ Am::Am(Runtime& rt, int nslots, uint32_t max_payload) : rt_(rt) {
   GICC_CUDA(cudaMalloc(&dview_, sizeof(AmView)));
   GICC_CUDA(cudaMemcpy(dview_, &view_, sizeof(AmView), cudaMemcpyHostToDevice));
   GICC_CUDA(cudaMalloc(&dcount_, sizeof(int)));
-  head_.assign(n_, 0);
   rt.barrier();
 }
 
@@ -111,10 +110,18 @@ Am::~Am() {
   if (dcount_) cudaFree(dcount_);
 }
 
+// The send cursor of every direction lives in device memory (view_.head), shared by host
+// sends and device sends, so both kinds can be mixed on one direction in stream order.
+uint64_t Am::head(int dst) {
+  uint64_t h = 0;
+  GICC_CUDA(cudaMemcpy(&h, view_.head + dst, sizeof(h), cudaMemcpyDeviceToHost));
+  return h;
+}
+
 bool Am::check_can_send(int dst) {
   uint64_t credit = 0;
   GICC_CUDA(cudaMemcpy(&credit, view_.credit + dst, sizeof(credit), cudaMemcpyDeviceToHost));
-  return head_[dst] - credit < (uint64_t)nslots_;
+  return head(dst) - credit < (uint64_t)nslots_;
 }
 
 uint64_t Am::host_send(int dst, uint16_t handler, const am_args_t& args, const void* payload, uint32_t len,
@@ -126,8 +133,9 @@ uint64_t Am::host_send(int dst, uint16_t handler, const am_args_t& args, const v
     if (std::chrono::steady_clock::now() > deadline) return 0;
     std::this_thread::yield();
   }
-  const uint64_t seq = head_[dst] + 1;
-  uint8_t* slot = view_.peer_inbox[dst] + ((size_t)me_ * nslots_ + head_[dst] % nslots_) * slot_bytes_;
+  const uint64_t cur = head(dst);
+  const uint64_t seq = cur + 1;
+  uint8_t* slot = view_.peer_inbox[dst] + ((size_t)me_ * nslots_ + cur % nslots_) * slot_bytes_;
   std::vector<uint8_t> body(AM_SHORT_SIZE - 8 + len);
   am_hdr_t h{handler, (uint16_t)me_, (uint16_t)len,
              (uint8_t)(flags | (len ? AM_FLAG_HAS_PAYLOAD : AM_FLAG_HANDLE_ONLY)), 0};
@@ -137,7 +145,7 @@ uint64_t Am::host_send(int dst, uint16_t handler, const am_args_t& args, const v
   // body first, then the sequence word: synchronous copies complete in this order
   GICC_CUDA(cudaMemcpy(slot + 8, body.data(), body.size(), cudaMemcpyHostToDevice));
   GICC_CUDA(cudaMemcpy(slot, &seq, sizeof(seq), cudaMemcpyHostToDevice));
-  head_[dst] = seq;
+  GICC_CUDA(cudaMemcpy(view_.head + dst, &seq, sizeof(seq), cudaMemcpyHostToDevice));
   return seq;
 }
 

@@ -5,6 +5,7 @@ import shutil
 import statistics
 import subprocess
 import tempfile
+import time
 from typing import List, Optional
 
 QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -14,13 +15,30 @@ REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_powe
 
 
 class ClockSampler:
-    """``with ClockSampler(gpus) as cs: ...`` then ``cs.summary()``."""
+    """``with ClockSampler(gpus) as cs: ...`` then ``cs.summary()``.
 
-    def __init__(self, gpus: Optional[List[int]] = None, period_ms: int = 200):
+    ``__enter__`` returns only after nvidia-smi has written its first sample (it takes a
+    fraction of a second to start), and the summary keeps only the samples written after
+    that point, so a timed region of a few hundred milliseconds still gets samples of its
+    own.  ``__exit__`` waits for one more sample when the region produced none."""
+
+    def __init__(self, gpus: Optional[List[int]] = None, period_ms: int = 50, start_timeout_s: float = 5.0):
         self.gpus = gpus
         self.period_ms = period_ms
+        self.start_timeout_s = start_timeout_s
         self.proc = None
         self.file = None
+        self.skip = 0
+
+    def _lines(self) -> int:
+        self.file.flush()
+        with open(self.file.name) as f:
+            return sum(1 for _ in f)
+
+    def _wait_lines(self, n: int, timeout_s: float) -> None:
+        t0 = time.monotonic()
+        while self._lines() < n and time.monotonic() - t0 < timeout_s and self.proc.poll() is None:
+            time.sleep(0.01)
 
     def __enter__(self):
         if shutil.which("nvidia-smi") is None:
@@ -30,10 +48,15 @@ class ClockSampler:
         if self.gpus is not None:
             cmd.insert(1, "-i=" + ",".join(str(g) for g in self.gpus))
         self.proc = subprocess.Popen(cmd, stdout=self.file, stderr=subprocess.DEVNULL)
+        per_round = len(self.gpus) if self.gpus is not None else 1
+        self._wait_lines(per_round, self.start_timeout_s)
+        self.skip = self._lines()
         return self
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            if self._lines() <= self.skip:
+                self._wait_lines(self.skip + 1, 4 * self.period_ms / 1000 + 0.5)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -47,7 +70,9 @@ class ClockSampler:
         self.file.flush()
         rows = []
         with open(self.file.name) as f:
-            for line in f:
+            for i, line in enumerate(f):
+                if i < self.skip:
+                    continue
                 parts = [p.strip() for p in line.split(",")]
                 if len(parts) < 9:
                     continue
