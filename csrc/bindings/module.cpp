@@ -38,6 +38,16 @@ at::Tensor gemm(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tens
   return C;
 }
 
+void gemm_tile_done_selftest(const at::Tensor& A, const at::Tensor& B, const at::Tensor& counters, int64_t skew_ns) {
+  check_cuda_bf16(A, "A");
+  check_cuda_bf16(B, "B");
+  TORCH_CHECK(A.is_contiguous() && B.is_contiguous() && A.size(1) == B.size(1), "A[M,K], B[N,K] contiguous");
+  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.is_contiguous(), "int32 counters");
+  const c10::cuda::CUDAGuard g(A.device());
+  gicc::ops::gemm_tile_done_selftest(A.data_ptr(), B.data_ptr(), (int)A.size(0), (int)B.size(0), (int)A.size(1),
+                                     static_cast<uint32_t*>(counters.data_ptr()), (uint32_t)skew_ns, cur_stream());
+}
+
 py::dict read_errors(bool clear) {
   gicc::ErrorRecord r = gicc::read_error_record(clear);
   py::dict d;
@@ -79,6 +89,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "opengda_b200 native ops (sm_100a)";
   m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("out") = py::none(), py::arg("alpha") = 1.0,
         py::arg("out_f32") = false, py::arg("bn") = 0, "C = alpha * A @ B^T with the tcgen05 GEMM");
+  m.def("gemm_tile_done_selftest", &gemm_tile_done_selftest, py::arg("A"), py::arg("B"), py::arg("counters"),
+        py::arg("skew_ns") = 20000, "run the GEMM core with an epilogue that checks the tile-done ordering");
   m.def("read_errors", &read_errors, py::arg("clear") = true, "read (and clear) the device error record");
   m.def("default_timeout_ns", &gicc::default_timeout_ns);
   m.def("tensor_from_ptr", &tensor_from_ptr, py::arg("ptr"), py::arg("shape"), py::arg("dtype"), py::arg("device"));

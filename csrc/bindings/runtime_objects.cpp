@@ -219,7 +219,8 @@ void bind_runtime_objects(py::module_& m) {
   m.def("jacobi_ctas_per_row", &ops::jacobi_ctas_per_row);
   m.def("k_ag_gemm", [](int n, int r, int M, int Ns, int K, std::vector<uint64_t> a_full, uint64_t B, long long ldb,
                         uint64_t C, long long ldc, std::vector<uint64_t> arrivals, std::vector<uint64_t> done,
-                        uint64_t epoch, int units_per_band, int grid, uint64_t timeout_ns) {
+                        uint64_t epoch, int units_per_band, int grid, uint64_t timeout_ns, uint64_t trace,
+                        int diag, int comm_ctas, uint64_t tile_counter, uint64_t a_mc, uint64_t arrivals_mc) {
     if ((int)a_full.size() != n || (int)arrivals.size() != n || (int)done.size() != n || n > 16)
       throw std::runtime_error("k_ag_gemm: per-rank pointer lists must have n <= 16 entries");
     ops::AgGemmArgs a;
@@ -231,8 +232,14 @@ void bind_runtime_objects(py::module_& m) {
     }
     a.B = P<const void>(B); a.ldb = ldb; a.C = P<void>(C); a.ldc = ldc;
     a.epoch = epoch; a.units_per_band = units_per_band; a.grid = grid; a.timeout_ns = timeout_ns;
+    a.trace = P<uint64_t>(trace); a.diag = diag; a.comm_ctas = comm_ctas;
+    a.tile_counter = P<uint64_t>(tile_counter);
+    a.a_mc = P<void>(a_mc); a.arrivals_mc = P<uint64_t>(arrivals_mc);
     ops::ag_gemm(a, cur_stream());
-  });
+  }, py::arg("n"), py::arg("r"), py::arg("M"), py::arg("Ns"), py::arg("K"), py::arg("a_full"), py::arg("B"),
+     py::arg("ldb"), py::arg("C"), py::arg("ldc"), py::arg("arrivals"), py::arg("done"), py::arg("epoch"),
+     py::arg("units_per_band"), py::arg("grid"), py::arg("timeout_ns"), py::arg("trace") = 0, py::arg("diag") = 0,
+     py::arg("comm_ctas") = 0, py::arg("tile_counter") = 0, py::arg("a_mc") = 0, py::arg("arrivals_mc") = 0);
   m.def("k_gemm_rs", [](int n, int r, int M, int N, int K, uint64_t A, long long lda, uint64_t B, long long ldb,
                         std::vector<uint64_t> slots, std::vector<uint64_t> arrivals, std::vector<uint64_t> done,
                         uint64_t out, long long ldo, uint64_t epoch, int grid, uint64_t timeout_ns) {
@@ -248,7 +255,9 @@ void bind_runtime_objects(py::module_& m) {
     }
     a.out = P<void>(out); a.ldo = ldo; a.epoch = epoch; a.grid = grid; a.timeout_ns = timeout_ns;
     ops::gemm_rs(a, cur_stream());
-  });
+  }, py::arg("n"), py::arg("r"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("A"), py::arg("lda"), py::arg("B"),
+     py::arg("ldb"), py::arg("slots"), py::arg("arrivals"), py::arg("done"), py::arg("out"), py::arg("ldo"),
+     py::arg("epoch"), py::arg("grid"), py::arg("timeout_ns"));
   m.def("k_moe_route", [](uint64_t logits, int T, int E, int topk, uint64_t idx, uint64_t w, uint64_t counts) {
     ops::moe_route(P<const float>(logits), T, E, topk, P<int>(idx), P<float>(w), P<int>(counts), cur_stream());
   });

@@ -18,11 +18,18 @@
 // owner GPU) and the MoE grouped GEMM.  This replaces the reference's SIMT stripe kernel
 // (examples/gicc/mm.cu:47-62), which accumulates with per-element atomicAdd.
 //
+// Tile order: static (CTA b takes tiles b, b + grid, ...) or, for schedules that set
+// kDynamic, dynamic: the producer thread takes the next tile index from a global counter
+// (Sched::next_tile) and hands it to the MMA and epilogue warps through a 4-entry smem
+// queue.  Dynamic order lets CTAs that also move data (communication warps) take fewer
+// tiles, and keeps the whole grid on the tiles in index order.
+//
 // Every wait is bounded (timeout_ns via %globaltimer); on timeout the CTA records the
 // error, lets its in-flight TMA loads and MMAs drain (again bounded), frees TMEM and
 // returns.
 #pragma once
 #include <cstdint>
+#include <type_traits>
 
 #include "gicc/device/ptx.cuh"
 #include "gicc/error.hpp"
@@ -38,6 +45,15 @@ constexpr int kEpiThreads = 128;
 // Threads of a CTA for a schedule with `comm_warps` extra communication warps.
 __host__ __device__ constexpr int cta_threads(int comm_warps) { return kThreads + 32 * comm_warps; }
 
+// Schedules opt into dynamic tile order with `static constexpr bool kDynamic = true` and
+// `__device__ int next_tile() const` (an index >= num_tiles() ends the CTA's work).
+template <class S, class = void>
+struct sched_dynamic : std::false_type {};
+template <class S>
+struct sched_dynamic<S, std::void_t<decltype(S::kDynamic)>> : std::bool_constant<S::kDynamic> {};
+
+constexpr int kTileQ = 4;  // entries of the producer -> MMA/epilogue tile queue
+
 template <int BN>
 struct Cfg {
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 32 in [64, 256]");
@@ -48,6 +64,8 @@ struct Cfg {
   static constexpr uint32_t kTmemCols = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
   static constexpr uint32_t kBarBytes = 256;
   static constexpr uint32_t kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
+  // mbarriers (full/empty per stage, 2+2 accumulator, drain, 2 x tile queue) + 8 words
+  static_assert((2 * kStages + 5 + 2 * 4) * 8 + 8 * 4 <= kBarBytes, "barrier area too small");
 };
 
 struct TileInfo {
@@ -116,12 +134,16 @@ __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensor
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* tq_full = drain + 1;        // dynamic order: tile index published
+  uint64_t* tq_empty = tq_full + kTileQ;  // ... and read by the MMA thread and 4 epilogue warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tq_empty + kTileQ);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // Per accumulator: how many epilogue warps have finished a tile held in it (monotonic).
   // One counter per accumulator, because a fast warp can finish the tile in the other
   // accumulator before a slow warp finishes this one.
   uint32_t* epi_cnt = tmem_slot + 2;
+  volatile int* tq = reinterpret_cast<volatile int*>(tmem_slot + 4);  // [kTileQ] tile indices
+  constexpr bool kDyn = sched_dynamic<Sched>::value;
 
   const uint32_t warp = ptx::warp_id();
   const uint32_t lane = ptx::lane_id();
@@ -136,6 +158,10 @@ __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensor
       ptx::mbar_init(&tempty[a], kEpiThreads);
     }
     ptx::mbar_init(drain, 1);
+    for (int q = 0; q < kTileQ; ++q) {
+      ptx::mbar_init(&tq_full[q], 1);
+      ptx::mbar_init(&tq_empty[q], 1 + kEpiThreads / 32);
+    }
     *abort_flag = 0;
     epi_cnt[0] = 0;
     epi_cnt[1] = 0;
@@ -161,7 +187,24 @@ __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensor
       uint32_t armed[S];
 #pragma unroll
       for (int s = 0; s < S; ++s) armed[s] = 0;
-      for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x) {
+      int tq_slot = 0;
+      uint32_t tq_phase = 0;
+      for (int t = blockIdx.x; !*abort_flag; t += gridDim.x) {
+        if constexpr (kDyn) {
+          if (!ptx::mbar_wait(&tq_empty[tq_slot], tq_phase ^ 1, timeout_ns, abort_flag)) {
+            if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_GEMM_PIPE, rank, -1, 4, 0);
+            *abort_flag = 1;
+            break;
+          }
+          t = sched.next_tile();
+          tq[tq_slot] = t < ntiles ? t : -1;
+          ptx::mbar_arrive(&tq_full[tq_slot]);
+          if (++tq_slot == kTileQ) {
+            tq_slot = 0;
+            tq_phase ^= 1;
+          }
+        }
+        if (t >= ntiles) break;
         TileInfo ti = sched.tile(t);
         if (!sched.producer_wait(ti, timeout_ns, abort_flag, err)) {
           *abort_flag = 1;
@@ -202,7 +245,24 @@ __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensor
       int acc = 0;
       uint32_t acc_phase = 0;
       bool issued = false;
-      for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x) {
+      int tq_slot = 0;
+      uint32_t tq_phase = 0;
+      for (int t = blockIdx.x; !*abort_flag; t += gridDim.x) {
+        if constexpr (kDyn) {
+          if (!ptx::mbar_wait(&tq_full[tq_slot], tq_phase, timeout_ns, abort_flag)) {
+            if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_GEMM_PIPE, rank, -1, 5, 0);
+            *abort_flag = 1;
+            break;
+          }
+          t = tq[tq_slot];
+          ptx::mbar_arrive(&tq_empty[tq_slot]);
+          if (++tq_slot == kTileQ) {
+            tq_slot = 0;
+            tq_phase ^= 1;
+          }
+          if (t < 0) break;
+        }
+        if (t >= ntiles) break;
         TileInfo ti = sched.tile(t);
         if (!ptx::mbar_wait(&tempty[acc], acc_phase ^ 1, timeout_ns, abort_flag)) {
           if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_GEMM_PIPE, rank, -1, 1, 0);
@@ -259,7 +319,25 @@ __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensor
     const int row = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    int tq_slot = 0;
+    uint32_t tq_phase = 0;
+    for (int t = blockIdx.x;; t += gridDim.x) {
+      if constexpr (kDyn) {
+        if (!ptx::mbar_wait(&tq_full[tq_slot], tq_phase, timeout_ns, abort_flag)) {
+          if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_GEMM_PIPE, rank, -1, 6, 0);
+          *abort_flag = 1;
+          break;
+        }
+        t = tq[tq_slot];
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&tq_empty[tq_slot]);
+        if (++tq_slot == kTileQ) {
+          tq_slot = 0;
+          tq_phase ^= 1;
+        }
+        if (t < 0) break;
+      }
+      if (t >= ntiles) break;
       TileInfo ti = sched.tile(t);
       if (!ptx::mbar_wait(&tfull[acc], acc_phase, timeout_ns, abort_flag)) {
         if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_GEMM_PIPE, rank, -1, 3, 0);

@@ -15,6 +15,10 @@ namespace ops {
 // bn selects the tile width (0 = default 256).
 GICC_EXPORT void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
                            long long ldc, bool out_f32, float alpha, int bn, cudaStream_t stream);
+// Self-test of the GEMM core's tile-done ordering: counters must hold 2*tiles+1 zeroed
+// words ([warps finished per tile][times published per tile][violations]).
+GICC_EXPORT void gemm_tile_done_selftest(const void* A, const void* B, int M, int N, int K, uint32_t* counters,
+                                         uint32_t skew_ns, cudaStream_t stream);
 
 // ---- communication kernels (comm.cu) ------------------------------------------------------
 GICC_EXPORT void barrier_single(BarrierCtx* ctx, uint64_t* flag, cudaStream_t s);
@@ -84,7 +88,14 @@ struct AgGemmArgs {
   uint64_t epoch = 0;          // call number, >= 1, equal on all ranks
   int units_per_band = 4;
   int grid = 0;
+  int comm_ctas = 0;           // CTAs that push the shard (0 = all)
+  void* a_mc = nullptr;              // NVLS: multicast view of the landing buffer (current parity)
+  uint64_t* arrivals_mc = nullptr;   // NVLS: multicast view of the arrival counters
+  uint64_t* tile_counter = nullptr;  // local word, zero before the first call; calls that share
+                                     // it must use the same shape and grid (dynamic tile order)
   uint64_t timeout_ns = 0;
+  uint64_t* trace = nullptr;   // diagnostics: %globaltimer stamps per tile / unit / CTA
+  int diag = 0;                // diagnostics: bit 0 = no transfer (times the math alone)
 };
 struct GemmRsArgs {
   int n = 0, r = 0, M = 0, N = 0, K = 0;  // K = local K

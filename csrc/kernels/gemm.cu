@@ -169,9 +169,81 @@ static void launch_pair(const void* A, const void* B, void* C, int M, int N, int
   GICC_CUDA(cudaGetLastError());
 }
 
+// ---- self-test of the core's tile-done ordering (used by the distributed epilogues) ----
+// Each epilogue warp records that it finished a tile; the core's tile_done hook must then
+// run exactly once per tile, after all four warps.  Warp 0 is delayed on every other tile
+// so that the other warps run ahead into the tile held in the other accumulator.
+struct TileDoneCheckEpi {
+  static constexpr bool kNeedsTileDone = true;
+  static constexpr bool kPairHalves = false;
+  int num_n, bn;
+  uint32_t* warps_done;  // [tiles]
+  uint32_t* published;   // [tiles]
+  uint32_t* bad;         // tile_done ran before all four warps finished
+  uint32_t skew_ns;
+  __device__ static void fence_before_done() { __threadfence(); }
+  __device__ int index(const TileInfo& ti) const { return (ti.m0 / BM) * num_n + ti.n0 / bn; }
+  __device__ void begin_tile(const TileInfo&, int) {}
+  __device__ void store(const TileInfo&, int, int, const uint32_t*) {}
+  __device__ void end_tile(const TileInfo& ti, int row) {
+    const int idx = index(ti);
+    if (row < 32 && (idx & 1) == 0 && skew_ns) {
+      for (uint32_t t = 0; t < skew_ns; t += 1000) __nanosleep(1000);
+    }
+    __syncwarp();
+    if ((row & 31) == 0) atomicAdd(&warps_done[idx], 1u);
+  }
+  __device__ void tile_done(const TileInfo& ti) {
+    const int idx = index(ti);
+    if (atomicAdd(&warps_done[idx], 0u) != 4u) atomicAdd(bad, 1u);
+    atomicAdd(&published[idx], 1u);
+  }
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_tile_done_check(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           PlainSched sched, TileDoneCheckEpi epi, ErrorRecord* err, uint64_t timeout_ns) {
+  gemm_core<256>(&tmA, &tmB, sched, epi, err, timeout_ns, -1);
+}
+
 }  // namespace gemm
 
 namespace ops {
+
+void gemm_tile_done_selftest(const void* A, const void* B, int M, int N, int K, uint32_t* counters, uint32_t skew_ns,
+                             cudaStream_t stream) {
+  using Cf = gemm::Cfg<256>;
+  if (M % gemm::BM || N % 256 || K % gemm::BK) throw std::runtime_error("gicc::gemm_tile_done_selftest: M%128, N%256, K%64");
+  const CUtensorMap tA = make_tmap_2d(A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, K, gemm::BM, gemm::BK,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tB = make_tmap_2d(B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, K, 256, gemm::BK,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  gemm::PlainSched s;
+  s.M = M;
+  s.N = N;
+  s.K = K;
+  s.bn = 256;
+  s.num_m = M / gemm::BM;
+  s.num_n = N / 256;
+  s.group_m = 16;
+  const int tiles = s.num_m * s.num_n;
+  gemm::TileDoneCheckEpi e;
+  e.num_n = s.num_n;
+  e.bn = 256;
+  e.warps_done = counters;
+  e.published = counters + tiles;
+  e.bad = counters + 2 * tiles;
+  e.skew_ns = skew_ns;
+  GICC_CUDA(cudaFuncSetAttribute(gemm::k_gemm_tile_done_check, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Cf::kSmemBytes));
+  int dev = 0;
+  GICC_CUDA(cudaGetDevice(&dev));
+  const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
+  gemm::k_gemm_tile_done_check<<<grid, gemm::kThreads, Cf::kSmemBytes, stream>>>(tA, tB, s, e, device_error_record(),
+                                                                          default_timeout_ns());
+  GICC_CUDA(cudaGetLastError());
+}
+
 
 void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
                long long ldc, bool out_f32, float alpha, int bn, cudaStream_t stream) {

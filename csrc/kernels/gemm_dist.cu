@@ -55,26 +55,111 @@ __device__ __forceinline__ bool wait_counter(const uint64_t* p, uint64_t target,
   }
 }
 
+// Copy nv 16-byte vectors with the 128 threads of the communication warps, software-
+// pipelined: the loads of batch b+1 (8 vectors per thread) are in flight while batch b is
+// stored, so each thread keeps 16 vectors moving and the SM's push rate is not bound by
+// one load latency per batch.
+template <int kT>
+__device__ __forceinline__ void copy_unit(const uint4* __restrict__ src, uint4* __restrict__ dst, size_t nv, int tid) {
+  constexpr size_t step = 8 * kT;
+  const size_t nbatch = nv / step;
+  uint4 va[8], vb[8];
+  auto load = [&](uint4* v, size_t b) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = ptx::ld_v4_nc(src + b * step + tid + j * kT);
+  };
+  auto store = [&](const uint4* v, size_t b) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ptx::st_v4_na(dst + b * step + tid + j * kT, v[j]);
+  };
+  if (nbatch > 0) load(va, 0);
+  size_t b = 0;
+  for (; b + 1 < nbatch; b += 2) {
+    load(vb, b + 1);
+    store(va, b);
+    if (b + 2 < nbatch) load(va, b + 2);
+    store(vb, b + 1);
+  }
+  if (b < nbatch) store(va, b);  // odd count: the last batch is loaded, not yet stored
+  for (size_t i = nbatch * step + tid; i < nv; i += kT) ptx::st_v4_na(dst + i, ptx::ld_v4_nc(src + i));
+}
+
+// Same, with the stores going through an NVLS multicast view (multimem.st: one store,
+// delivered by the NVSwitch to every GPU of the multicast object).
+template <int kT>
+__device__ __forceinline__ void copy_unit_mc(const uint4* __restrict__ src, uint4* dst_mc, size_t nv, int tid) {
+  constexpr size_t step = 8 * kT;
+  const size_t nbatch = nv / step;
+  uint4 va[8], vb[8];
+  auto load = [&](uint4* v, size_t b) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = ptx::ld_v4_nc(src + b * step + tid + j * kT);
+  };
+  auto store = [&](const uint4* v, size_t b) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ptx::multimem_st_v4(dst_mc + b * step + tid + j * kT, v[j]);
+  };
+  if (nbatch > 0) load(va, 0);
+  size_t b = 0;
+  for (; b + 1 < nbatch; b += 2) {
+    load(vb, b + 1);
+    store(va, b);
+    if (b + 2 < nbatch) load(va, b + 2);
+    store(vb, b + 1);
+  }
+  if (b < nbatch) store(va, b);
+  for (size_t i = nbatch * step + tid; i < nv; i += kT) ptx::multimem_st_v4(dst_mc + i, ptx::ld_v4_nc(src + i));
+}
+
 // ------------------------------------------------------------------------------------------
 // all-gather -> GEMM
 // ------------------------------------------------------------------------------------------
 struct AgSched {
   static constexpr int kCommWarps = kCommWarpsAG;
+  static constexpr bool kDynamic = true;  // CTAs that push take fewer tiles
   int n, r, M, Ns, K, Ms, nb, bn, num_n, Q, G;
+  int C;                           // CTAs that push (blockIdx.x < C); the rest only compute
   const uint16_t* a_local;         // my A_full (this parity)
   uint16_t* a_peer[kMaxR];         // every rank's A_full (this parity), mapped here
   const uint64_t* arrivals;        // my counters [n][nb]
   uint64_t* arrivals_peer[kMaxR];  // each rank's counter base
   const uint64_t* done_local;      // [n] CTA-exit counts received from each rank
   uint64_t epoch;                  // this call, >= 1
+  // Diagnostics (both off in normal use).  trace: %globaltimer stamps, layout in
+  // AgTrace below.  diag bit 0: skip the transfer and the arrival waits, which times the
+  // tensor-core work of the fused kernel alone (the output is then not the product).
+  uint64_t* trace;
+  int diag;
+  unsigned long long* tile_counter;  // local word, monotonic over calls
+  unsigned long long tile_base;      // (epoch - 1) * (tiles + grid): every CTA takes one index past the end
+  // NVLS mode (both non-null): the shard is written once through the multicast view of
+  // A_full and lands in every GPU; one multimem.red bumps every GPU's arrival counter.
+  uint16_t* a_mc;
+  uint64_t* arrivals_mc;
 
   __device__ int num_tiles() const { return n * nb * num_n; }
+  __device__ int num_units() const { return (diag & 1) ? 0 : (a_mc ? nb * Q : (n - 1) * nb * Q); }
+  __device__ int next_tile() const {
+    const unsigned long long v = atomicAdd(tile_counter, 1ull) - tile_base;
+    return v < (unsigned long long)num_tiles() ? (int)v : num_tiles();
+  }
+  __device__ int trace_tile(const TileInfo& ti) const { return (ti.m0 / BM) * num_n + ti.n0 / bn; }
   __device__ TileInfo tile(int t) const {
-    // shard-major (local shard first), grouped rasterisation inside a shard for L2 reuse
+    // Local shard first.  Unicast push: then shard r+1, r+2, ... (each source pushes to
+    // its consumers in that order).  NVLS: every shard arrives at once, band by band, so
+    // the remote tiles go band-major over the sources.  Grouped rasterisation (16 rows of
+    // tiles) throughout, for L2 reuse of A and B.
     const int per = nb * num_n;
-    const int k = t / per;
-    int b, nbk;
-    raster(t - k * per, nb, num_n, 16, b, nbk);
+    int k, b, nbk;
+    if (a_mc && t >= per) {
+      int vm;
+      raster(t - per, nb * (n - 1), num_n, 16, vm, nbk);
+      b = vm / (n - 1);
+      k = 1 + vm - b * (n - 1);
+    } else {
+      k = t / per;
+      raster(t - k * per, nb, num_n, 16, b, nbk);
+    }
     const int s = (r + k) % n;
     TileInfo ti;
     ti.m0 = s * Ms + b * BM;
@@ -89,14 +174,18 @@ struct AgSched {
   }
   __device__ bool producer_wait(const TileInfo& ti, uint64_t timeout_ns, volatile int* abort_flag,
                                 ErrorRecord* err) const {
-    if (ti.aux == r) return true;
-    const uint64_t* c = arrivals + (size_t)ti.aux * nb + ti.aux2;
-    const uint64_t target = epoch * (uint64_t)Q;
-    if (!wait_counter(c, target, timeout_ns, abort_flag)) {
-      if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_AG_FLAG, r, ti.aux, ptx::ld_relaxed_sys(c), target);
-      return false;
+    uint64_t* tr = trace ? trace + 2 * (size_t)trace_tile(ti) : nullptr;
+    if (tr) tr[0] = ptx::globaltimer();
+    if (ti.aux != r && !(diag & 1)) {
+      const uint64_t* c = arrivals + (size_t)ti.aux * nb + ti.aux2;
+      const uint64_t target = epoch * (uint64_t)Q;
+      if (!wait_counter(c, target, timeout_ns, abort_flag)) {
+        if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_AG_FLAG, r, ti.aux, ptx::ld_relaxed_sys(c), target);
+        return false;
+      }
+      ptx::fence_proxy_async_global();  // peer's generic-proxy stores -> our TMA reads
     }
-    ptx::fence_proxy_async_global();  // peer's generic-proxy stores -> our TMA reads
+    if (tr) tr[1] = ptx::globaltimer();
     return true;
   }
   __device__ void issue_loads(const TileInfo& ti, int kb, void* sA, void* sB, uint64_t* bar, const CUtensorMap* tmA,
@@ -112,9 +201,42 @@ struct AgSched {
     constexpr int kT = kCommWarps * 32;
     const size_t band_bytes = (size_t)BM * K * 2;
     const size_t unit_bytes = band_bytes / Q;
-    const int U = (n - 1) * nb * Q;
+    const int U = num_units();
+    uint64_t* tr = trace ? trace + 3 * (size_t)num_tiles() : nullptr;
     int last_d = -1;
-    for (int u = blockIdx.x; u < U; u += G) {
+    if ((int)blockIdx.x >= C) return;
+    if (a_mc) {
+      // NVLS: unit u = b*Q + q of my shard, written to every GPU at once.  First make sure
+      // that every peer finished the call that last used this parity.
+      if (tid == 0) {
+        int stop = *abort_flag;
+        for (int d = 0; d < n && !stop && epoch > 2 && U > 0; ++d) {
+          if (d == r) continue;
+          const uint64_t target = (epoch - 2) * (uint64_t)G;
+          if (!wait_counter(done_local + d, target, timeout_ns, abort_flag)) {
+            if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_AG_FLAG, r, d, ptx::ld_relaxed_sys(done_local + d), target);
+            *abort_flag = 1;
+            stop = 1;
+          }
+        }
+        comm_stop = stop;
+      }
+      asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
+      if (comm_stop) return;
+      for (int u = blockIdx.x; u < U && !*abort_flag; u += C) {
+        const int b = u / Q, q = u - (u / Q) * Q;
+        if (tr && tid == 0) tr[2 * u] = ptx::globaltimer();
+        const size_t off = ((size_t)(r * Ms + b * BM) * K * 2) + (size_t)q * unit_bytes;
+        copy_unit_mc<kT>(reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a_local) + off),
+                         reinterpret_cast<uint4*>(reinterpret_cast<char*>(a_mc) + off), unit_bytes / 16, tid);
+        ptx::fence_acq_rel_sys();
+        asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
+        if (tid == 0) ptx::multimem_red_release_add_u64(arrivals_mc + (size_t)r * nb + b, 1);
+        if (tr && tid == 0) tr[2 * u + 1] = ptx::globaltimer();
+      }
+      return;
+    }
+    for (int u = blockIdx.x; u < U; u += C) {
       const int k = 1 + u / (nb * Q);
       const int rem = u - (k - 1) * nb * Q;
       const int b = rem / Q, q = rem - (rem / Q) * Q;
@@ -134,25 +256,23 @@ struct AgSched {
       asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
       if (comm_stop) break;
       last_d = d;
+      if (tr && tid == 0) tr[2 * u] = ptx::globaltimer();
       const size_t off = ((size_t)(r * Ms + b * BM) * K * 2) + (size_t)q * unit_bytes;
       const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a_local) + off);
       uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a_peer[d]) + off);
-      const size_t nv = unit_bytes / 16;
-      size_t i = tid;
-      for (; i + 7 * kT < nv; i += 8 * kT) {
-        uint4 v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = ptx::ld_v4_nc(src + i + j * kT);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) ptx::st_v4_na(dst + i + j * kT, v[j]);
-      }
-      for (; i < nv; i += kT) ptx::st_v4_na(dst + i, ptx::ld_v4_nc(src + i));
+      copy_unit<kT>(src, dst, unit_bytes / 16, tid);
       ptx::fence_acq_rel_sys();
       asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
       if (tid == 0) ptx::red_release_sys_add(arrivals_peer[d] + (size_t)r * nb + b, 1);
+      if (tr && tid == 0) tr[2 * u + 1] = ptx::globaltimer();
     }
   }
 };
+// Trace layout (uint64 %globaltimer ns), T = tiles (m-block major), U = (n-1)*nb*Q units:
+//   [2t, 2t+1]        producer: before / after the wait for tile t's A band
+//   [2T + t]          epilogue: tile t stored (first epilogue warp)
+//   [3T + 2u, +1]     comm: unit u push start / arrival released
+//   [3T + 2U + 2c, +1] CTA c: start / end
 
 struct PlainStoreEpi {
   static constexpr bool kNeedsTileDone = false;
@@ -160,10 +280,14 @@ struct PlainStoreEpi {
   uint16_t* C;
   long long ldc;
   int M, N;
+  uint64_t* trace_epi;  // diagnostics: [tile] stamp when stored, or null
+  int num_n, bn;
   __device__ static void fence_before_done() {}
   __device__ void tile_done(const TileInfo&) {}
   __device__ void begin_tile(const TileInfo&, int) {}
-  __device__ void end_tile(const TileInfo&, int) {}
+  __device__ void end_tile(const TileInfo& ti, int row) {
+    if (trace_epi && row == 0) trace_epi[(ti.m0 / BM) * num_n + ti.n0 / bn] = ptx::globaltimer();
+  }
   __device__ __forceinline__ void store(const TileInfo& ti, int row, int c, const uint32_t* r) {
     const int gm = ti.m0 + row;
     if (gm >= M) return;
@@ -194,8 +318,11 @@ template <int BN>
 __global__ void __launch_bounds__(cta_threads(kCommWarpsAG), 1)
     k_ag_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, AgSched sched,
               PlainStoreEpi epi, DoneTable done_peer, ErrorRecord* err, uint64_t timeout_ns) {
+  uint64_t* tr = sched.trace ? sched.trace + 3 * (size_t)sched.num_tiles() + 2 * (size_t)sched.num_units() : nullptr;
+  if (tr && threadIdx.x == 0) tr[2 * blockIdx.x] = ptx::globaltimer();
   gemm_core<BN>(&tmA, &tmB, sched, epi, err, timeout_ns, sched.r);
   signal_cta_done(done_peer.p, sched.n, sched.r);
+  if (tr && threadIdx.x == 0) tr[2 * blockIdx.x + 1] = ptx::globaltimer();
 }
 
 // ------------------------------------------------------------------------------------------
@@ -350,6 +477,8 @@ void ag_gemm(const AgGemmArgs& a, cudaStream_t s) {
   if (a.M % (a.n * BM) || a.Ns % BN_ || a.K % BK)
     throw std::runtime_error("gicc::ag_gemm: need M % (ranks*128) == 0, N/ranks % 256 == 0, K % 64 == 0");
   const int Ms = a.M / a.n, nb = Ms / BM;
+  const int Q = a.units_per_band > 0 ? a.units_per_band : 4;
+  if (((long long)BM * a.K * 2 / 16) % Q) throw std::runtime_error("gicc::ag_gemm: units_per_band must divide a band's 16-byte vectors");
   const CUtensorMap tA = make_tmap_2d(a.a_full[a.r], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, a.K, BM, BK,
                                       CU_TENSOR_MAP_SWIZZLE_128B);
   const CUtensorMap tB = make_tmap_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.Ns, a.K, a.ldb, BN_, BK,
@@ -365,8 +494,9 @@ void ag_gemm(const AgGemmArgs& a, cudaStream_t s) {
   sc.nb = nb;
   sc.bn = BN_;
   sc.num_n = a.Ns / BN_;
-  sc.Q = a.units_per_band > 0 ? a.units_per_band : 4;
+  sc.Q = Q;
   sc.G = G;
+  sc.C = a.comm_ctas > 0 && a.comm_ctas < G ? a.comm_ctas : G;
   sc.a_local = static_cast<const uint16_t*>(a.a_full[a.r]);
   for (int i = 0; i < a.n; ++i) {
     sc.a_peer[i] = static_cast<uint16_t*>(a.a_full[i]);
@@ -375,7 +505,17 @@ void ag_gemm(const AgGemmArgs& a, cudaStream_t s) {
   sc.arrivals = a.arrivals[a.r];
   sc.done_local = a.done[a.r];
   sc.epoch = a.epoch;
-  PlainStoreEpi e{static_cast<uint16_t*>(a.C), a.ldc, a.M, a.Ns};
+  sc.trace = a.trace;
+  sc.diag = a.diag;
+  if (!a.tile_counter) throw std::runtime_error("gicc::ag_gemm: tile_counter (one zeroed local word) is required");
+  sc.tile_counter = reinterpret_cast<unsigned long long*>(a.tile_counter);
+  sc.tile_base = (unsigned long long)(a.epoch - 1) * (unsigned long long)(a.n * nb * (a.Ns / BN_) + G);
+  sc.a_mc = static_cast<uint16_t*>(a.a_mc);
+  sc.arrivals_mc = a.arrivals_mc;
+  if ((sc.a_mc == nullptr) != (sc.arrivals_mc == nullptr))
+    throw std::runtime_error("gicc::ag_gemm: NVLS mode needs both a_mc and arrivals_mc");
+  PlainStoreEpi e{static_cast<uint16_t*>(a.C), a.ldc, a.M, a.Ns, a.trace ? a.trace + 2 * (size_t)a.n * nb * (a.Ns / BN_) : nullptr,
+                  a.Ns / BN_, BN_};
   DoneTable dt{};
   for (int i = 0; i < a.n; ++i) dt.p[i] = a.done[i];
   constexpr uint32_t smem = Cfg<BN_>::kSmemBytes;

@@ -24,7 +24,7 @@ from ..ops.gemm import gemm
 
 class DistGemm:
     def __init__(self, M: int, N: int, K: int, mode: str = "ag", rt=None, device: Optional[torch.device] = None,
-                 fused: bool = True):
+                 fused: bool = True, nvls: Optional[bool] = None):
         self.M, self.N, self.K, self.mode = M, N, K, mode
         self.fused = fused
         self.rt = rt
@@ -38,18 +38,35 @@ class DistGemm:
             raise ValueError("M, N and K must be divisible by the number of ranks")
         self.launches_per_step = 1
         self.epoch = 0
+        # Fused AG: the shard goes out through the NVLS multicast view when the node has
+        # NVLS (one write reaches every GPU), else by unicast pushes to each peer.  Only
+        # `comm_ctas` CTAs push (SMs that push stall their own tensor-core work, so few do,
+        # and the dynamic tile order gives them fewer tiles).  Tuning and diagnostics:
+        # units each 128-row band is pushed in, CTAs (0 = one per SM), a uint64 trace
+        # tensor (None = off) and the diag bits.
+        self.nvls = bool(nvls if nvls is not None else (rt is not None and w > 1 and rt.multicast_supported))
+        self.units_per_band = 4
+        self.grid = 0
+        self.comm_ctas = 8 if self.nvls else 32
+        self.trace: Optional[torch.Tensor] = None
+        self.diag = 0
         if w > 1 and fused:
             # fused kernels: double-buffered landing areas + epoch counters in the signal heap
             if mode == "ag":
-                self.A_bufs = [rt.alloc_tensor((M, K), torch.bfloat16, exchange=False) for _ in range(2)]
+                self.A_bufs = [rt.alloc_tensor((M, K), torch.bfloat16, multicast=self.nvls, exchange=False)
+                               for _ in range(2)]
                 nbands = (M // w) // 128
             else:
                 self.slot_bufs = [rt.alloc_tensor((w, M // w, N), torch.bfloat16, exchange=False) for _ in range(2)]
                 nbands = (M // w) // 128
             rt.exchange()
-            off = rt.signal_alloc(w * nbands + w)
+            off = rt.signal_alloc(w * nbands + w + 1)
             self.arrivals = [rt.signal_peer(p, off) for p in range(w)]
             self.done = [rt.signal_peer(p, off + w * nbands) for p in range(w)]
+            self.tile_counter = rt.signal_local(off + w * nbands + w)  # AG dynamic tile order
+            self.arrivals_mc = rt.signal_multicast(off) if self.nvls and mode == "ag" else 0
+            if self.nvls and mode == "ag" and (not self.arrivals_mc or not self.A_bufs[0].mc_ptr):
+                raise RuntimeError("DistGemm: NVLS requested but the runtime has no multicast mapping")
             self.C = torch.empty(*self.out_shape(), dtype=torch.bfloat16, device=self.device)
             self.launches_per_step = 1
         elif w > 1:
@@ -80,6 +97,15 @@ class DistGemm:
         w = self.world
         return (self.M, self.N // w) if self.mode == "ag" else (self.M // w, self.N)
 
+    def trace_words(self) -> int:
+        """Size (uint64 words) of the fused AG trace buffer for the current settings."""
+        w = self.world
+        nb = (self.M // w) // 128
+        tiles = w * nb * ((self.N // w) // 256)
+        units = 0 if self.diag & 1 else (1 if self.nvls else w - 1) * nb * self.units_per_band
+        grid = self.grid or torch.cuda.get_device_properties(self.device).multi_processor_count
+        return 3 * tiles + 2 * units + 2 * grid
+
     def a_slot(self, parity: Optional[int] = None) -> torch.Tensor:
         """Where this rank's A shard must live for the AG mode (zero-copy input).  Fused
         mode alternates two landing buffers; by default the slot of the *next* call."""
@@ -106,8 +132,10 @@ class DistGemm:
                     slot.copy_(A)
                 buf = self.A_bufs[p]
                 n.k_ag_gemm(w, r, self.M, self.N // w, self.K, [buf.ptr(q) for q in range(w)], B.data_ptr(),
-                            B.stride(0), C.data_ptr(), C.stride(0), self.arrivals, self.done, self.epoch, 4, 0,
-                            self.rt.timeout_ns)
+                            B.stride(0), C.data_ptr(), C.stride(0), self.arrivals, self.done, self.epoch,
+                            self.units_per_band, self.grid, self.rt.timeout_ns,
+                            self.trace.data_ptr() if self.trace is not None else 0, self.diag, self.comm_ctas,
+                            self.tile_counter, buf.mc_ptr if self.nvls else 0, self.arrivals_mc)
             else:
                 buf = self.slot_bufs[p]
                 n.k_gemm_rs(w, r, self.M, self.N, self.K // w, A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0),

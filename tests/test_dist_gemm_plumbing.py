@@ -1,0 +1,106 @@
+"""Host-side plumbing of the fused distributed GEMM, on CPU: DistGemm against a fake
+runtime, with the native kernels replaced by recorders whose signatures are read from the
+real bindings' docstrings -- so an argument that the binding would reject (wrong count,
+a method passed where an int is due) fails here, without a GPU."""
+import inspect
+import re
+
+import pytest
+import torch
+
+import opengda_b200
+from opengda_b200.models import dist_gemm
+
+
+class _FakeSym:
+    def __init__(self, base, n):
+        self.base, self.n = base, n
+
+    def ptr(self, rank=None):
+        return self.base + (0 if rank is None else rank << 32)
+
+    @property
+    def mc_ptr(self):
+        return self.base + (1 << 40)
+
+    @property
+    def local(self):
+        return torch.zeros(1)
+
+
+class _FakeRt:
+    def __init__(self, n=2, rank=0, mc=True):
+        self.size, self.rank, self.multicast_supported = n, rank, mc
+        self.timeout_ns = 10 ** 9
+        self._next = 1 << 20
+
+    def alloc_tensor(self, shape, dtype=torch.bfloat16, multicast=False, exchange=True):
+        self._next += 1 << 30
+        return _FakeSym(self._next, self.size)
+
+    def exchange(self):
+        pass
+
+    def signal_alloc(self, n):
+        return 64
+
+    def signal_peer(self, rank, word=0):
+        return (rank + 1) << 36 | word * 8
+
+    def signal_local(self, word=0):
+        return self.signal_peer(self.rank, word)
+
+    def signal_multicast(self, word=0):
+        return 1 << 44 | word * 8
+
+
+def _params(doc: str):
+    head = doc.strip().splitlines()[0]
+    inner = head[head.index("(") + 1:head.rindex(")")]
+    names = re.findall(r"(\w+): [^,=]+(?:\[[^\]]*\])?( = [^,]+)?", inner)
+    return [(n, bool(d)) for n, d in names]
+
+
+class _Recorder:
+    def __init__(self, real):
+        self.calls = []
+        self.sig = {}
+        for name in ("k_ag_gemm", "k_gemm_rs"):
+            params = _params(getattr(real, name).__doc__)
+            self.sig[name] = inspect.Signature([
+                inspect.Parameter(p, inspect.Parameter.POSITIONAL_OR_KEYWORD, default=0 if d else inspect._empty)
+                for p, d in params])
+
+    def __getattr__(self, name):
+        sig = self.sig[name]
+
+        def call(*args, **kw):
+            bound = sig.bind(*args, **kw)
+            for k, v in bound.arguments.items():
+                assert isinstance(v, (int, list)), (name, k, type(v))
+                if isinstance(v, list):
+                    assert all(isinstance(x, int) for x in v), (name, k)
+            self.calls.append((name, dict(bound.arguments)))
+        return call
+
+
+@pytest.mark.parametrize("mode,nvls", [("ag", True), ("ag", False), ("rs", None)])
+def test_fused_dist_gemm_passes_binding_compatible_arguments(monkeypatch, mode, nvls):
+    real = opengda_b200.native()
+    rec = _Recorder(real)
+    monkeypatch.setattr(opengda_b200, "native", lambda: rec)
+    M = N = K = 1024
+    rt = _FakeRt(2, 0, mc=True)
+    m = dist_gemm.DistGemm(M, N, K, mode, rt=rt, device=torch.device("cpu"), nvls=nvls)
+    A = torch.zeros(*m.a_shape(), dtype=torch.bfloat16)
+    B = torch.zeros(*m.b_shape(), dtype=torch.bfloat16)
+    if mode == "ag":
+        m.a_slot = lambda parity=None: A  # zero-copy slot: no copy on the fake buffers
+    for _ in range(3):
+        m(A, B)
+    assert [c[0] for c in rec.calls] == ["k_" + ("ag_gemm" if mode == "ag" else "gemm_rs")] * 3
+    args = rec.calls[-1][1]
+    assert args["epoch"] == 3
+    if mode == "ag":
+        assert (args["a_mc"] != 0) == bool(nvls) and (args["arrivals_mc"] != 0) == bool(nvls)
+        assert args["tile_counter"] != 0 and args["comm_ctas"] > 0

@@ -65,3 +65,24 @@ def test_gemm_cta_pair_matches_fp32_reference(M, N, K):
     ref = _ref(A, B)
     err = (C.float() - ref).abs().max().item()
     assert err <= 1e-2 * ref.abs().max().item() + 1e-2, err
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("skew_ns", [0, 20000])
+def test_gemm_core_publishes_each_tile_once_after_all_epilogue_warps(skew_ns):
+    """The hook that the distributed epilogues use to publish a finished tile (a flag or a
+    counter on the owner GPU) must run once per tile and only after all four epilogue warps
+    are done with it, also when one warp lags behind the others."""
+    from opengda_b200 import native
+
+    torch.manual_seed(0)
+    M, N, K = 128 * 148 * 3, 512, 128  # 3 tiles per CTA in each accumulator parity
+    A = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    B = torch.randn(N, K, device="cuda").to(torch.bfloat16)
+    tiles = (M // 128) * (N // 256)
+    counters = torch.zeros(2 * tiles + 1, dtype=torch.int32, device="cuda")
+    native().gemm_tile_done_selftest(A, B, counters, skew_ns)
+    torch.cuda.synchronize()
+    assert int(counters[2 * tiles]) == 0
+    assert torch.equal(counters[:tiles], torch.full((tiles,), 4, dtype=torch.int32, device="cuda"))
+    assert torch.equal(counters[tiles:2 * tiles], torch.ones(tiles, dtype=torch.int32, device="cuda"))

@@ -166,11 +166,11 @@ def main():
     res["am_counter_ok"] = am.counter() == 20 * (left + 1)
     res["am_checksum_ok"] = am.checksum() == sum((i * 7 + left) % 256 for i in range(1000))
     boot.barrier()
-    out = torch.zeros(1, dtype=torch.int64, device="cuda")
-    if r < 2:
-        am.pingpong(1 - r, 1000, "reqrep", r == 0, out.data_ptr())
+    rtt = torch.zeros(1, dtype=torch.int64, device="cuda")
+    if r < 2:  # device-driven sends on directions that also carried host sends above
+        am.pingpong(1 - r, 1000, "reqrep", r == 0, rtt.data_ptr())
     torch.cuda.synchronize()
-    res["am_reqrep_rtt_us"] = out.item() / 1000 / 1e3 if r == 0 else None
+    res["am_reqrep_rtt_us"] = rtt.item() / 1000 / 1e3 if r == 0 else None
     rt.check_device_errors()
     torch.cuda.synchronize()
     boot.barrier()
