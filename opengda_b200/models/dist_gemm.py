@@ -47,7 +47,10 @@ class DistGemm:
         self.nvls = bool(nvls if nvls is not None else (rt is not None and w > 1 and rt.multicast_supported))
         self.units_per_band = 4
         self.grid = 0
-        self.comm_ctas = 8 if self.nvls else 32
+        # NVLS at 8 GPUs is bound by each GPU's NVLink ingress (7 shards arrive at once), so
+        # more CTAs push there; at 2-4 GPUs 8 keep well ahead of the tensor cores.
+        self.comm_ctas = (16 if w >= 8 else 8) if self.nvls else 32
+        self.rs_reduce_ctas = 16  # RS over NVLS: CTAs whose reduce warps run multimem.ld_reduce
         self.trace: Optional[torch.Tensor] = None
         self.diag = 0
         if w > 1 and fused:
@@ -55,6 +58,11 @@ class DistGemm:
             if mode == "ag":
                 self.A_bufs = [rt.alloc_tensor((M, K), torch.bfloat16, multicast=self.nvls, exchange=False)
                                for _ in range(2)]
+                nbands = (M // w) // 128
+            elif self.nvls:
+                # NVLS reduce-scatter: each rank's whole [M, N] bf16 partial, reduced in the switch
+                self.slot_bufs = [rt.alloc_tensor((M, N), torch.bfloat16, multicast=True, exchange=False)
+                                  for _ in range(2)]
                 nbands = (M // w) // 128
             else:
                 self.slot_bufs = [rt.alloc_tensor((w, M // w, N), torch.bfloat16, exchange=False) for _ in range(2)]
@@ -67,6 +75,10 @@ class DistGemm:
             self.arrivals_mc = rt.signal_multicast(off) if self.nvls and mode == "ag" else 0
             if self.nvls and mode == "ag" and (not self.arrivals_mc or not self.A_bufs[0].mc_ptr):
                 raise RuntimeError("DistGemm: NVLS requested but the runtime has no multicast mapping")
+            if self.nvls and mode == "rs":
+                if not self.slot_bufs[0].mc_ptr:
+                    raise RuntimeError("DistGemm: NVLS requested but the runtime has no multicast mapping")
+                self.band_tiles = rt.signal_local(rt.signal_alloc(w * nbands))
             self.C = torch.empty(*self.out_shape(), dtype=torch.bfloat16, device=self.device)
             self.launches_per_step = 1
         elif w > 1:
@@ -138,9 +150,15 @@ class DistGemm:
                             self.tile_counter, buf.mc_ptr if self.nvls else 0, self.arrivals_mc)
             else:
                 buf = self.slot_bufs[p]
-                n.k_gemm_rs(w, r, self.M, self.N, self.K // w, A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0),
-                            [buf.ptr(q) for q in range(w)], self.arrivals, self.done, C.data_ptr(), C.stride(0),
-                            self.epoch, 0, self.rt.timeout_ns)
+                if self.nvls:
+                    n.k_gemm_rs(w, r, self.M, self.N, self.K // w, A.data_ptr(), A.stride(0), B.data_ptr(),
+                                B.stride(0), [buf.ptr(q) for q in range(w)], self.arrivals, self.done, C.data_ptr(),
+                                C.stride(0), self.epoch, self.grid, self.rt.timeout_ns, buf.mc_ptr, self.band_tiles,
+                                self.tile_counter, self.rs_reduce_ctas, self.units_per_band)
+                else:
+                    n.k_gemm_rs(w, r, self.M, self.N, self.K // w, A.data_ptr(), A.stride(0), B.data_ptr(),
+                                B.stride(0), [buf.ptr(q) for q in range(w)], self.arrivals, self.done, C.data_ptr(),
+                                C.stride(0), self.epoch, self.grid, self.rt.timeout_ns)
             return C
         if self.mode == "ag":
             Ms = self.M // w
