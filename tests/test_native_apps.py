@@ -40,3 +40,18 @@ def test_pingpong_two_ranks():
     p = _launch(2, "gicc_pingpong", 200)
     assert p.returncode == 0, p.stdout + p.stderr
     assert "PASS" in p.stdout
+
+
+def test_gda_api_example_single_rank():
+    p = _launch(1, "gda_api_example")
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert "rank 0: PASS" in p.stdout
+
+
+@pytest.mark.multigpu
+def test_gda_api_example_all_gpus():
+    import torch
+    n = min(torch.cuda.device_count(), 8)
+    p = _launch(n, "gda_api_example")
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert p.stdout.count("PASS") == n
