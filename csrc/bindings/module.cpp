@@ -4,6 +4,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "gicc/config.hpp"
 #include "gicc/error.hpp"
 #include "gicc/ops.hpp"
 
@@ -91,6 +92,20 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out_f32") = false, py::arg("bn") = 0, "C = alpha * A @ B^T with the tcgen05 GEMM");
   m.def("gemm_tile_done_selftest", &gemm_tile_done_selftest, py::arg("A"), py::arg("B"), py::arg("counters"),
         py::arg("skew_ns") = 20000, "run the GEMM core with an epilogue that checks the tile-done ordering");
+  m.def("config", [] {
+    const gicc::Config c = gicc::config();
+    py::dict d;
+    d["timeout_ms"] = c.timeout_ms;
+    d["bootstrap_timeout_ms"] = c.bootstrap_timeout_ms;
+    d["log_level"] = c.log_level;
+    d["checks"] = c.checks;
+    d["disable_nvls"] = c.disable_nvls;
+    d["debug_puts"] = c.debug_puts;
+    d["signal_heap_bytes"] = c.signal_heap_bytes;
+    return d;
+  }, "the GICC_* environment, parsed and range checked (raises ValueError on a bad value)");
+  m.def("config_summary", [] { return gicc::config().summary(); });
+  m.def("log", [](int level, const std::string& msg) { gicc::log(level, "%s", msg.c_str()); });
   m.def("read_errors", &read_errors, py::arg("clear") = true, "read (and clear) the device error record");
   m.def("default_timeout_ns", &gicc::default_timeout_ns);
   m.def("tensor_from_ptr", &tensor_from_ptr, py::arg("ptr"), py::arg("shape"), py::arg("dtype"), py::arg("device"));

@@ -242,7 +242,9 @@ void bind_runtime_objects(py::module_& m) {
      py::arg("comm_ctas") = 0, py::arg("tile_counter") = 0, py::arg("a_mc") = 0, py::arg("arrivals_mc") = 0);
   m.def("k_gemm_rs", [](int n, int r, int M, int N, int K, uint64_t A, long long lda, uint64_t B, long long ldb,
                         std::vector<uint64_t> slots, std::vector<uint64_t> arrivals, std::vector<uint64_t> done,
-                        uint64_t out, long long ldo, uint64_t epoch, int grid, uint64_t timeout_ns) {
+                        uint64_t out, long long ldo, uint64_t epoch, int grid, uint64_t timeout_ns,
+                        uint64_t staging_mc, uint64_t band_tiles, uint64_t tile_counter, int comm_ctas,
+                        int units_per_band) {
     if ((int)slots.size() != n || (int)arrivals.size() != n || (int)done.size() != n || n > 16)
       throw std::runtime_error("k_gemm_rs: per-rank pointer lists must have n <= 16 entries");
     ops::GemmRsArgs a;
@@ -254,10 +256,13 @@ void bind_runtime_objects(py::module_& m) {
       a.done[i] = P<uint64_t>(done[i]);
     }
     a.out = P<void>(out); a.ldo = ldo; a.epoch = epoch; a.grid = grid; a.timeout_ns = timeout_ns;
+    a.staging_mc = P<const void>(staging_mc); a.band_tiles = P<uint64_t>(band_tiles);
+    a.tile_counter = P<uint64_t>(tile_counter); a.comm_ctas = comm_ctas; a.units_per_band = units_per_band;
     ops::gemm_rs(a, cur_stream());
   }, py::arg("n"), py::arg("r"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("A"), py::arg("lda"), py::arg("B"),
      py::arg("ldb"), py::arg("slots"), py::arg("arrivals"), py::arg("done"), py::arg("out"), py::arg("ldo"),
-     py::arg("epoch"), py::arg("grid"), py::arg("timeout_ns"));
+     py::arg("epoch"), py::arg("grid"), py::arg("timeout_ns"), py::arg("staging_mc") = 0, py::arg("band_tiles") = 0,
+     py::arg("tile_counter") = 0, py::arg("comm_ctas") = 0, py::arg("units_per_band") = 4);
   m.def("k_moe_route", [](uint64_t logits, int T, int E, int topk, uint64_t idx, uint64_t w, uint64_t counts) {
     ops::moe_route(P<const float>(logits), T, E, topk, P<int>(idx), P<float>(w), P<int>(counts), cur_stream());
   });

@@ -111,6 +111,14 @@ struct GemmRsArgs {
   uint64_t epoch = 0;
   int grid = 0;
   uint64_t timeout_ns = 0;
+  // NVLS mode (staging_mc non-null): slots[r] is this rank's [M][N] bf16 staging buffer
+  // (current parity), staging_mc its multicast view; arrivals[o] = owner o's [M/n/128]
+  // counters; band_tiles = local [n][M/n/128] words; tile_counter as for ag_gemm.
+  const void* staging_mc = nullptr;
+  uint64_t* band_tiles = nullptr;
+  uint64_t* tile_counter = nullptr;
+  int comm_ctas = 0;           // CTAs running the reduce warps (0 = 16)
+  int units_per_band = 4;      // row slices per 128-row band (divides 128)
 };
 GICC_EXPORT void ag_gemm(const AgGemmArgs& a, cudaStream_t s);
 GICC_EXPORT void gemm_rs(const GemmRsArgs& a, cudaStream_t s);

@@ -5,6 +5,7 @@
 #include <cstring>
 #include <thread>
 
+#include "gicc/device/am.cuh"
 #include "gicc/device/ptx.cuh"
 #include "gicc/host_util.hpp"
 
@@ -16,7 +17,7 @@ using proto::DevMem;
 
 __global__ void k_am_poll(AmView v, int max_per_peer, int* count) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  *count = poll_all_builtin<DevMem>(v, max_per_peer);
+  *count = am_poll_all(&v, max_per_peer);
 }
 
 // mode 0: request/reply (ECHO request, 8-byte reply); mode 1: request/request (NOOP both ways).
@@ -29,24 +30,24 @@ __global__ void k_am_pingpong(AmView v, int peer, int iters, int mode, int initi
     a.data[0] = (uint64_t)i + 1;
     if (mode == 0) {
       if (initiator) {
-        const uint64_t seq = send<DevMem>(v, peer, AM_HANDLER_ECHO, a, nullptr, 0, AM_FLAG_REQUEST);
+        const uint64_t seq = am_send_request(&v, peer, AM_HANDLER_ECHO, a);
         uint64_t val = 0;
-        if (seq == 0 || !wait_reply<DevMem>(v, peer, seq, &val) || val != a.data[0]) {
+        if (seq == 0 || !am_wait_reply(&v, peer, seq, &val) || val != a.data[0]) {
           report_error(v.err, GICC_ETIMEDOUT, W_AM_WAIT, v.rank, peer, val, a.data[0]);
           return;
         }
-      } else if (!wait_one<DevMem>(v, peer)) {
+      } else if (!am_recv_and_reply_fast(&v, peer)) {
         report_error(v.err, GICC_ETIMEDOUT, W_AM_WAIT, v.rank, peer, 0, (uint64_t)i);
         return;
       }
     } else {
       if (initiator) {
-        if (!send<DevMem>(v, peer, AM_HANDLER_NOOP, a, nullptr, 0, 0) || !wait_one<DevMem>(v, peer)) {
+        if (!am_send_short(&v, peer, AM_HANDLER_NOOP, a) || !am_wait_one(&v, peer)) {
           report_error(v.err, GICC_ETIMEDOUT, W_AM_WAIT, v.rank, peer, 0, (uint64_t)i);
           return;
         }
       } else {
-        if (!wait_one<DevMem>(v, peer) || !send<DevMem>(v, peer, AM_HANDLER_NOOP, a, nullptr, 0, 0)) {
+        if (!am_wait_one(&v, peer) || !am_send_short(&v, peer, AM_HANDLER_NOOP, a)) {
           report_error(v.err, GICC_ETIMEDOUT, W_AM_WAIT, v.rank, peer, 0, (uint64_t)i);
           return;
         }

@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include "gicc/device/comm.cuh"
+#include "gicc/config.hpp"
 #include "gicc/host_util.hpp"
 #include "gicc/ops.hpp"
 
@@ -214,6 +215,7 @@ void reduce_bf16(const void* const* srcs, int nsrc, void* out, size_t count, flo
 void allreduce_bf16(int algo, const void* const* in, void* const* out, const void* mc_in, void* mc_out, int n, int me,
                     size_t count, float scale, bool out_f32, uint64_t* const* flag_bases, int max_blocks,
                     uint64_t epoch, uint64_t timeout_ns, int blocks, cudaStream_t s) {
+  NvtxRange nvtx("gicc::ops::allreduce_bf16");
   if (n < 1 || n > kMaxRanks) throw std::runtime_error("gicc::allreduce: 1..8 ranks (one NVSwitch node)");
   if (count % 8) throw std::runtime_error("gicc::allreduce: element count must be a multiple of 8");
   const size_t nvec = count / 8;

@@ -8,6 +8,7 @@
 
 #include "gicc/device/gemm_core.cuh"
 #include "gicc/device/gemm_core2.cuh"
+#include "gicc/config.hpp"
 #include "gicc/host_util.hpp"
 #include "gicc/ops.hpp"
 
@@ -247,6 +248,7 @@ void gemm_tile_done_selftest(const void* A, const void* B, int M, int N, int K, 
 
 void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
                long long ldc, bool out_f32, float alpha, int bn, cudaStream_t stream) {
+  NvtxRange nvtx("gicc::ops::gemm_bf16");
   if (M <= 0 || N <= 0 || K <= 0) throw std::runtime_error("gicc::gemm_bf16: empty shape");
   if (K % 8 != 0 || lda % 8 != 0 || ldb % 8 != 0)
     throw std::runtime_error("gicc::gemm_bf16: K and leading dimensions of A/B must be multiples of 8 (16-byte TMA rows)");

@@ -28,6 +28,7 @@
 
 #include "gicc/device/comm.cuh"
 #include "gicc/device/gemm_core.cuh"
+#include "gicc/config.hpp"
 #include "gicc/host_util.hpp"
 #include "gicc/ops.hpp"
 
@@ -465,12 +466,171 @@ __global__ void __launch_bounds__(kThreads, 1)
   signal_cta_done(done_peer.p, sched.n, sched.r);
 }
 
+// ------------------------------------------------------------------------------------------
+// GEMM -> reduce-scatter over NVLS
+// ------------------------------------------------------------------------------------------
+// Every rank writes its bf16 partial of the whole [M, N] output into its own staging
+// buffer (local HBM, no NVLink traffic from the epilogue).  Tiles go band-major over the
+// owners (band b of owner 0, 1, ..., n-1, then band b+1), the same order on every rank,
+// so a band is finished everywhere at about the same time.  The CTA that completes a
+// band's last tile tells the owner (one release add).  On the owner, `comm_ctas` CTAs run
+// reduce warps: once all n ranks reported a band, multimem.ld_reduce reads the band
+// through the staging buffer's multicast view -- the NVSwitch fetches the n partials and
+// adds them (f32) -- and the bf16 sum is stored into the owner's output rows.  The
+// reduction of band b overlaps the MMAs of the bands after it.
+struct RsNvSched {
+  static constexpr int kCommWarps = kCommWarpsAG;
+  static constexpr bool kDynamic = true;
+  int n, r, M, N, K, Mr, nbo, bn, num_n, Q, G, C;
+  const uint16_t* staging_mc;      // multicast view of the staging buffers (this parity)
+  const uint64_t* arrivals;        // mine: [nbo] ranks that finished my band b (monotonic)
+  const uint64_t* done_local;      // [n] CTA-exit counts received from each rank
+  uint16_t* out;                   // [Mr][N] bf16
+  long long ldo;
+  uint64_t epoch;
+  unsigned long long* tile_counter;
+  unsigned long long tile_base;
+
+  __device__ int num_tiles() const { return n * nbo * num_n; }
+  __device__ int next_tile() const {
+    const unsigned long long v = atomicAdd(tile_counter, 1ull) - tile_base;
+    return v < (unsigned long long)num_tiles() ? (int)v : num_tiles();
+  }
+  __device__ TileInfo tile(int t) const {
+    int vm, nbk;
+    raster(t, nbo * n, num_n, 16, vm, nbk);
+    const int b = vm / n, o = vm - b * n;
+    TileInfo ti;
+    ti.m0 = o * Mr + b * BM;
+    ti.a_row = ti.m0;
+    ti.n0 = nbk * bn;
+    ti.b_row = ti.n0;
+    ti.kb0 = 0;
+    ti.kb1 = (K + BK - 1) / BK;
+    ti.aux = o;
+    ti.aux2 = b;
+    return ti;
+  }
+  // Before this CTA's first tile: every owner finished reading (ld_reduce) the staging
+  // parity this call writes, i.e. finished call epoch-2.
+  __device__ int* checked_flag() const {
+    __shared__ int checked;  // set to 0 at kernel entry
+    return &checked;
+  }
+  __device__ bool producer_wait(const TileInfo&, uint64_t timeout_ns, volatile int* abort_flag,
+                                ErrorRecord* err) const {
+    int* checked = checked_flag();
+    if (*checked) return true;
+    for (int d = 0; d < n && epoch > 2; ++d) {
+      if (d == r) continue;
+      const uint64_t target = (epoch - 2) * (uint64_t)G;
+      if (!wait_counter(done_local + d, target, timeout_ns, abort_flag)) {
+        if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_RS_FLAG, r, d, ptx::ld_relaxed_sys(done_local + d), target);
+        return false;
+      }
+    }
+    *checked = 1;
+    return true;
+  }
+  __device__ void issue_loads(const TileInfo& ti, int kb, void* sA, void* sB, uint64_t* bar, const CUtensorMap* tmA,
+                              const CUtensorMap* tmB) const {
+    ptx::tma_load_2d(sA, tmA, bar, kb * BK, ti.a_row);
+    ptx::tma_load_2d(sB, tmB, bar, kb * BK, ti.b_row);
+  }
+  // Reduce warps: unit u = b*Q + q covers rows [q*128/Q, (q+1)*128/Q) of my band b.
+  __device__ void comm(int cw, int lane, volatile int* abort_flag, ErrorRecord* err, uint64_t timeout_ns) const {
+    __shared__ int comm_stop;
+    const int tid = cw * 32 + lane;
+    constexpr int kT = kCommWarps * 32;
+    if ((int)blockIdx.x >= C) return;
+    const int U = nbo * Q;
+    const int rows = BM / Q;
+    const int vpr = N / 8;  // 16-byte vectors per row
+    const size_t nv = (size_t)rows * vpr;
+    for (int u = blockIdx.x; u < U; u += C) {
+      const int b = u / Q, q = u - (u / Q) * Q;
+      if (tid == 0) {
+        int stop = *abort_flag;
+        const uint64_t target = epoch * (uint64_t)n;
+        if (!stop && !wait_counter(arrivals + b, target, timeout_ns, abort_flag)) {
+          if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_RS_FLAG, r, -1, ptx::ld_relaxed_sys(arrivals + b), target);
+          *abort_flag = 1;
+          stop = 1;
+        }
+        comm_stop = stop;
+      }
+      asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
+      if (comm_stop) break;
+      const int lrow0 = b * BM + q * rows;  // first row within my block
+      const uint4* src = reinterpret_cast<const uint4*>(staging_mc + ((size_t)r * Mr + lrow0) * N);
+      size_t i = tid;
+      for (; i + 15 * kT < nv; i += 16 * kT) {
+        uint4 v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = ptx::multimem_ld_reduce_bf16x8(src + i + j * kT);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const size_t e = i + j * kT;
+          const int rr = (int)(e / vpr), cc = (int)(e - (size_t)rr * vpr);
+          ptx::st_v4(out + (size_t)(lrow0 + rr) * ldo + (size_t)cc * 8, v[j]);
+        }
+      }
+      for (; i < nv; i += kT) {
+        const int rr = (int)(i / vpr), cc = (int)(i - (size_t)rr * vpr);
+        ptx::st_v4(out + (size_t)(lrow0 + rr) * ldo + (size_t)cc * 8, ptx::multimem_ld_reduce_bf16x8(src + i));
+      }
+      asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
+    }
+  }
+};
+
+struct RsNvEpi {
+  static constexpr bool kNeedsTileDone = true;
+  static constexpr bool kPairHalves = false;
+  int N, nbo, num_n;
+  uint16_t* staging;                   // mine [M][N] (this parity)
+  unsigned long long* band_tiles;      // mine [n][nbo]: tiles of band (o, b) finished here (monotonic)
+  uint64_t* arrivals_peer[kMaxR];      // owner o's [nbo] counters, mapped here
+  uint64_t epoch;
+  __device__ static void fence_before_done() { ptx::fence_acq_rel_sys(); }
+  __device__ void begin_tile(const TileInfo&, int) {}
+  __device__ void end_tile(const TileInfo&, int) {}
+  __device__ __forceinline__ void store(const TileInfo& ti, int row, int c, const uint32_t* acc) {
+    uint16_t* p = staging + (size_t)(ti.m0 + row) * N + ti.n0 + c;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 v;
+      v.x = ptx::pack_bf16x2(__uint_as_float(acc[8 * j + 0]), __uint_as_float(acc[8 * j + 1]));
+      v.y = ptx::pack_bf16x2(__uint_as_float(acc[8 * j + 2]), __uint_as_float(acc[8 * j + 3]));
+      v.z = ptx::pack_bf16x2(__uint_as_float(acc[8 * j + 4]), __uint_as_float(acc[8 * j + 5]));
+      v.w = ptx::pack_bf16x2(__uint_as_float(acc[8 * j + 6]), __uint_as_float(acc[8 * j + 7]));
+      ptx::st_v4(p + 8 * j, v);
+    }
+  }
+  // Last epilogue warp of a tile: count it; the CTA that completes the band tells the owner.
+  __device__ void tile_done(const TileInfo& ti) {
+    unsigned long long* c = band_tiles + (size_t)ti.aux * nbo + ti.aux2;
+    const unsigned long long old = ptx::atom_add_acq_rel_sys(reinterpret_cast<uint64_t*>(c), 1);
+    if (old + 1 == epoch * (unsigned long long)num_n) ptx::red_release_sys_add(arrivals_peer[ti.aux] + ti.aux2, 1);
+  }
+};
+
+template <int BN>
+__global__ void __launch_bounds__(cta_threads(kCommWarpsAG), 1)
+    k_gemm_rs_nvls(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, RsNvSched sched,
+                   RsNvEpi epi, DoneTable done_peer, ErrorRecord* err, uint64_t timeout_ns) {
+  if (threadIdx.x == 0) *sched.checked_flag() = 0;  // ordered by the core's set-up barrier
+  gemm_core<BN>(&tmA, &tmB, sched, epi, err, timeout_ns, sched.r);
+  signal_cta_done(done_peer.p, sched.n, sched.r);
+}
+
 }  // namespace
 }  // namespace gemm
 
 namespace ops {
 
 void ag_gemm(const AgGemmArgs& a, cudaStream_t s) {
+  NvtxRange nvtx("gicc::ops::ag_gemm");
   using namespace gemm;
   constexpr int BN_ = 256;
   if (a.n < 2 || a.n > kMaxR) throw std::runtime_error("gicc::ag_gemm: 2..16 ranks");
@@ -532,6 +692,7 @@ void ag_gemm(const AgGemmArgs& a, cudaStream_t s) {
 }
 
 void gemm_rs(const GemmRsArgs& a, cudaStream_t s) {
+  NvtxRange nvtx("gicc::ops::gemm_rs");
   using namespace gemm;
   constexpr int BN_ = 256;
   if (a.n < 2 || a.n > kMaxR) throw std::runtime_error("gicc::gemm_rs: 2..16 ranks");
@@ -543,6 +704,43 @@ void gemm_rs(const GemmRsArgs& a, cudaStream_t s) {
   const CUtensorMap tB = make_tmap_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.ldb, BN_, BK,
                                       CU_TENSOR_MAP_SWIZZLE_128B);
   const int G = a.grid > 0 ? a.grid : num_sms();
+  if (a.staging_mc) {
+    const int Q = a.units_per_band > 0 ? a.units_per_band : 4;
+    if (BM % Q || !a.band_tiles || !a.tile_counter || !a.slots[a.r])
+      throw std::runtime_error("gicc::gemm_rs (NVLS): units_per_band | 128, band_tiles, tile_counter, staging required");
+    RsNvSched sc{};
+    sc.n = a.n; sc.r = a.r; sc.M = a.M; sc.N = a.N; sc.K = a.K; sc.Mr = Mr; sc.nbo = Mr / BM; sc.bn = BN_;
+    sc.num_n = a.N / BN_; sc.Q = Q; sc.G = G;
+    sc.C = a.comm_ctas > 0 && a.comm_ctas < G ? a.comm_ctas : 16;
+    sc.staging_mc = static_cast<const uint16_t*>(a.staging_mc);
+    sc.arrivals = a.arrivals[a.r];
+    sc.done_local = a.done[a.r];
+    sc.out = static_cast<uint16_t*>(a.out);
+    sc.ldo = a.ldo;
+    sc.epoch = a.epoch;
+    sc.tile_counter = reinterpret_cast<unsigned long long*>(a.tile_counter);
+    sc.tile_base = (unsigned long long)(a.epoch - 1) * (unsigned long long)(a.n * sc.nbo * sc.num_n + G);
+    RsNvEpi e{};
+    e.N = a.N; e.nbo = sc.nbo; e.num_n = sc.num_n;
+    e.staging = static_cast<uint16_t*>(a.slots[a.r]);
+    e.band_tiles = reinterpret_cast<unsigned long long*>(a.band_tiles);
+    for (int i = 0; i < a.n; ++i) e.arrivals_peer[i] = a.arrivals[i];
+    e.epoch = a.epoch;
+    DoneTable dt{};
+    for (int i = 0; i < a.n; ++i) dt.p[i] = a.done[i];
+    constexpr uint32_t smem = Cfg<BN_>::kSmemBytes;
+    static bool attr_nv[64] = {false};
+    int dev = 0;
+    GICC_CUDA(cudaGetDevice(&dev));
+    if (!attr_nv[dev]) {
+      GICC_CUDA(cudaFuncSetAttribute(k_gemm_rs_nvls<BN_>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      attr_nv[dev] = true;
+    }
+    k_gemm_rs_nvls<BN_><<<G, cta_threads(kCommWarpsAG), smem, s>>>(tA, tB, sc, e, dt, device_error_record(),
+                                                                   a.timeout_ns ? a.timeout_ns : default_timeout_ns());
+    GICC_CUDA(cudaGetLastError());
+    return;
+  }
   RsSched sc{a.n, a.r, a.M, a.N, a.K, Mr, Mr / BM, BN_, a.N / BN_};
   RsEpi e{};
   e.n = a.n;

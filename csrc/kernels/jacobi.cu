@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 
 #include "gicc/device/comm.cuh"
+#include "gicc/config.hpp"
 #include "gicc/host_util.hpp"
 #include "gicc/ops.hpp"
 
@@ -184,6 +185,7 @@ void jacobi_init(float* a, float* b, int nx, int ny, int rows, int g0, uint64_t 
 }
 
 void jacobi_step(const JacobiStep& st, cudaStream_t s) {
+  NvtxRange nvtx("gicc::ops::jacobi_step");
   if (st.nx % 4 != 0) throw std::runtime_error("gicc::jacobi: nx must be a multiple of 4");
   if (st.rows < 1) throw std::runtime_error("gicc::jacobi: a rank needs at least one row");
   JacobiArgs p;

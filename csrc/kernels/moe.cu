@@ -27,6 +27,7 @@
 
 #include "gicc/device/comm.cuh"
 #include "gicc/device/gemm_core.cuh"
+#include "gicc/config.hpp"
 #include "gicc/host_util.hpp"
 #include "gicc/ops.hpp"
 
@@ -558,6 +559,7 @@ void moe_route(const float* logits, int T, int E, int topk, int* topk_idx, float
 }
 
 void moe_forward(const MoeArgs& a, cudaStream_t s) {
+  NvtxRange nvtx("gicc::ops::moe_forward");
   using namespace gemm;
   const int n = a.n, r = a.r, El = a.E / a.n;
   if (n < 1 || n > moe::kMaxR) throw std::runtime_error("gicc::moe: 1..8 ranks");

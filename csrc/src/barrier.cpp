@@ -1,6 +1,8 @@
 // barrier.cpp -- host side of gicc::Barrier.
 #include "gicc/barrier.hpp"
 
+#include "gicc/config.hpp"
+
 #include <chrono>
 #include <cstring>
 #include <thread>
@@ -66,12 +68,14 @@ void Barrier::finalize() {
 }
 
 void Barrier::setup() {
+  NvtxRange nvtx("gicc::Barrier::setup");
   ++epoch_;
   GICC_CUDA(cudaMemcpy(&dctx_->expected_signal, &epoch_, sizeof(epoch_), cudaMemcpyHostToDevice));
   target_ = epoch_;
 }
 
 void Barrier::start_continuous(uint64_t n) {
+  NvtxRange nvtx("gicc::Barrier::start_continuous");
   const uint64_t first = epoch_ + 1;
   GICC_CUDA(cudaMemcpy(&dctx_->expected_signal, &first, sizeof(first), cudaMemcpyHostToDevice));
   epoch_ += n;
@@ -84,6 +88,7 @@ void Barrier::advance(uint64_t n) {
 }
 
 void Barrier::wait_done(uint64_t target) {
+  NvtxRange nvtx("gicc::Barrier::wait");
   const auto deadline = std::chrono::steady_clock::now() + std::chrono::nanoseconds(rt_.timeout_ns());
   volatile uint64_t* d = done_host_;
   while (*d < target) {

@@ -1,6 +1,8 @@
 // bootstrap.cpp -- socket store server/client and the collectives built on it.
 #include "gicc/bootstrap.hpp"
 
+#include "gicc/config.hpp"
+
 #include <arpa/inet.h>
 #include <fcntl.h>
 #include <netdb.h>
@@ -383,8 +385,7 @@ static std::mutex g_req_mu;
 Bootstrap::Bootstrap() {
   rank_ = env_int("GICC_RANK", "RANK", 0);
   size_ = env_int("GICC_SIZE", "WORLD_SIZE", 1);
-  const char* t = std::getenv("GICC_BOOTSTRAP_TIMEOUT_MS");
-  if (t) timeout_s_ = std::atof(t) / 1000.0;
+  if (const uint64_t ms = config().bootstrap_timeout_ms) timeout_s_ = ms / 1000.0;
   std::string addr;
   if (const char* a = std::getenv("GICC_BOOTSTRAP_ADDR")) {
     addr = a;
@@ -417,8 +418,8 @@ Bootstrap::Bootstrap(int rank, int size, const std::string& addr, double timeout
   size_ = size;
   if (timeout_s > 0) {
     timeout_s_ = timeout_s;
-  } else if (const char* t = std::getenv("GICC_BOOTSTRAP_TIMEOUT_MS")) {
-    timeout_s_ = std::atof(t) / 1000.0;
+  } else if (const uint64_t ms = config().bootstrap_timeout_ms) {
+    timeout_s_ = ms / 1000.0;
   }
   std::string host;
   int port = 0;

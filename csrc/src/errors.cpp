@@ -2,6 +2,7 @@
 //
 // The record lives in device memory (device atomics pick the first error); the host
 // copies it back after a synchronize.  One record per device, allocated on first use.
+#include "gicc/config.hpp"
 #include "gicc/error.hpp"
 
 #include <cuda_runtime.h>
@@ -94,11 +95,6 @@ const char* where_name(int w) {
   return "?";
 }
 
-uint64_t default_timeout_ns() {
-  const char* s = std::getenv("GICC_TIMEOUT_MS");
-  long ms = s ? std::atol(s) : 5000;
-  if (ms <= 0) ms = 5000;
-  return static_cast<uint64_t>(ms) * 1000000ull;
-}
+uint64_t default_timeout_ns() { return config().timeout_ms * 1000000ull; }
 
 }  // namespace gicc

@@ -1,6 +1,8 @@
 // runtime.cpp -- symmetric memory over CUDA VMM / IPC, NVLS multicast, device contexts.
 #include "gicc/runtime.hpp"
 
+#include "gicc/config.hpp"
+
 #include <unistd.h>
 
 #include <algorithm>
@@ -62,6 +64,11 @@ Runtime::Runtime() : Runtime(std::make_shared<Bootstrap>()) {}
 Runtime::Runtime(std::shared_ptr<Bootstrap> boot, RuntimeOptions opt) : boot_(std::move(boot)) { init(opt); }
 
 void Runtime::init(RuntimeOptions opt) {
+  NvtxRange nvtx("gicc::Runtime::init");
+  const Config cfg = config();  // validates every GICC_* variable (throws on a bad one)
+  set_log_rank(boot_->rank());
+  if (boot_->rank() == 0) log(LOG_INFO, "%s", cfg.summary().c_str());
+  if (cfg.signal_heap_bytes) opt.signal_heap_bytes = cfg.signal_heap_bytes;
   int ndev = 0;
   GICC_CUDA(cudaGetDeviceCount(&ndev));
   if (ndev <= 0) throw std::runtime_error("gicc::Runtime: no CUDA device");
@@ -78,11 +85,11 @@ void Runtime::init(RuntimeOptions opt) {
   int mc = 0;
   driver().DeviceGetAttribute(&mc, CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED, cudev_);
   mc_supported_ = opt.enable_multicast && mc != 0 && size() > 1 && driver().MulticastCreate != nullptr &&
-                  std::getenv("GICC_DISABLE_NVLS") == nullptr;
+                  !cfg.disable_nvls;
   // every rank must agree on NVLS use
   auto all = boot_->allgather_fixed<int>(mc_supported_ ? 1 : 0);
   for (int v : all) mc_supported_ = mc_supported_ && v;
-  timeout_ns_ = default_timeout_ns();
+  timeout_ns_ = cfg.timeout_ms * 1000000ull;
   err_ = device_error_record();
 
   CUmemAllocationProp p{};
@@ -143,6 +150,7 @@ Runtime::~Runtime() {
 }
 
 void Runtime::finalize() {
+  NvtxRange nvtx("gicc::Runtime::finalize");
   if (finalized_) return;
   finalized_ = true;
   cudaSetDevice(device_);
@@ -190,6 +198,7 @@ void Runtime::finalize() {
 }
 
 Buffer Runtime::alloc(size_t bytes, bool multicast) {
+  NvtxRange nvtx("gicc::Runtime::alloc");
   if (regions_.size() >= (size_t)GICC_MAX_BUFS) throw std::runtime_error("gicc::Runtime::alloc: GICC_MAX_BUFS reached");
   auto r = std::make_unique<Region>();
   size_t g = granularity_;
@@ -231,6 +240,7 @@ Buffer Runtime::alloc(size_t bytes, bool multicast) {
 }
 
 Buffer Runtime::register_buffer(void* ptr, size_t size, bool is_device) {
+  NvtxRange nvtx("gicc::Runtime::register_buffer");
   if (regions_.size() >= (size_t)GICC_MAX_BUFS)
     throw std::runtime_error("gicc::Runtime::register_buffer: GICC_MAX_BUFS reached");
   if (!ptr || !size) throw std::runtime_error("gicc::Runtime::register_buffer: empty buffer");
@@ -263,6 +273,7 @@ Buffer Runtime::register_buffer(void* ptr, size_t size, bool is_device) {
 }
 
 void Runtime::exchange() {
+  NvtxRange nvtx("gicc::Runtime::exchange");
   // collective: every rank must have registered the same number of buffers
   const int mine = (int)regions_.size();
   auto counts = boot_->allgather_fixed<int>(mine);
@@ -476,6 +487,7 @@ uint64_t* Runtime::signal_multicast(size_t w) const {
 }
 
 DeviceCtx* Runtime::prepare(int peer, int remote_buf_index) {
+  NvtxRange nvtx("gicc::Runtime::prepare");
   if (peer < 0) peer = (rank() + 1) % size();
   if (peer >= size()) throw std::runtime_error("gicc::Runtime::prepare: bad peer");
   DeviceCtx c;
@@ -511,6 +523,7 @@ DeviceCtx* Runtime::prepare(int peer, int remote_buf_index) {
 }
 
 GiccContext* Runtime::build_context() {
+  NvtxRange nvtx("gicc::Runtime::build_context");
   if (size() > GICC_MAX_PEERS) throw std::runtime_error("gicc::Runtime::build_context: more than GICC_MAX_PEERS ranks");
   auto c = std::make_unique<GiccContext>();
   std::memset(c.get(), 0, sizeof(GiccContext));
@@ -551,21 +564,25 @@ void Runtime::reset() {
   ops_host_->epoch = ++op_epoch_;
 }
 
-void Runtime::barrier() { boot_->barrier(); }
-
-bool Runtime::checks_enabled() const {
-  const char* s = std::getenv("GICC_CHECKS");
-  return s && std::atoi(s) != 0;
+void Runtime::barrier() {
+  NvtxRange nvtx("gicc::Runtime::barrier");
+  boot_->barrier();
 }
+
+bool Runtime::checks_enabled() const { return config().checks; }
 
 void Runtime::host_put(const void* src_local, int dest_rank, int dest_buf, size_t dst_off, size_t size,
                        cudaStream_t s) {
+  NvtxRange nvtx("gicc::Runtime::host_put");
+  if (config().debug_puts) log(LOG_ERROR, "host_put %zu bytes -> rank %d buf %d +%zu", size, dest_rank, dest_buf, dst_off);
   const Region& r = *regions_.at(dest_buf);
   if (dst_off + size > r.size) throw std::runtime_error("gicc::Runtime::host_put: range outside the buffer");
   GICC_CUDA(cudaMemcpyAsync(remote_ptr(dest_rank, dest_buf, dst_off), src_local, size, cudaMemcpyDeviceToDevice, s));
 }
 
 void Runtime::host_get(void* dst_local, int src_rank, int src_buf, size_t src_off, size_t size, cudaStream_t s) {
+  NvtxRange nvtx("gicc::Runtime::host_get");
+  if (config().debug_puts) log(LOG_ERROR, "host_get %zu bytes <- rank %d buf %d +%zu", size, src_rank, src_buf, src_off);
   const Region& r = *regions_.at(src_buf);
   if (src_off + size > r.size) throw std::runtime_error("gicc::Runtime::host_get: range outside the buffer");
   GICC_CUDA(cudaMemcpyAsync(dst_local, remote_ptr(src_rank, src_buf, src_off), size, cudaMemcpyDeviceToDevice, s));
@@ -573,6 +590,8 @@ void Runtime::host_get(void* dst_local, int src_rank, int src_buf, size_t src_of
 
 Token Runtime::put_no_db(const Buffer& src, int dest_rank, int dest_buf_index, size_t size, size_t src_off,
                          size_t dst_off) {
+  NvtxRange nvtx("gicc::Runtime::put_no_db");
+  if (config().debug_puts) log(LOG_ERROR, "put_no_db %zu bytes -> rank %d buf %d +%zu", size, dest_rank, dest_buf_index, dst_off);
   if (ops_host_->n_ops >= (uint32_t)GICC_POOL_SIZE)
     throw std::runtime_error("gicc::Runtime::put_no_db: more than GICC_POOL_SIZE queued ops; call reset()");
   if (src.index < 0 || src.index >= (int)regions_.size()) throw std::runtime_error("put_no_db: bad source buffer");
@@ -597,6 +616,7 @@ DeviceCtx* Runtime::prepare_trigger(Token t) {
 }
 
 void Runtime::wait(Token t) {
+  NvtxRange nvtx("gicc::Runtime::wait");
   if (t.slot < 0) return;
   const double deadline = now_s() + (double)timeout_ns_ * 1e-9;
   volatile uint64_t* c = completion_host_ + t.slot;

@@ -3,7 +3,6 @@ runtime, with the native kernels replaced by recorders whose signatures are read
 real bindings' docstrings -- so an argument that the binding would reject (wrong count,
 a method passed where an int is due) fails here, without a GPU."""
 import inspect
-import re
 
 import pytest
 import torch
@@ -57,8 +56,17 @@ class _FakeRt:
 def _params(doc: str):
     head = doc.strip().splitlines()[0]
     inner = head[head.index("(") + 1:head.rindex(")")]
-    names = re.findall(r"(\w+): [^,=]+(?:\[[^\]]*\])?( = [^,]+)?", inner)
-    return [(n, bool(d)) for n, d in names]
+    parts, depth, cur = [], 0, ""
+    for ch in inner:  # split on the commas outside brackets
+        depth += ch == "["
+        depth -= ch == "]"
+        if ch == "," and depth == 0:
+            parts.append(cur)
+            cur = ""
+        else:
+            cur += ch
+    parts.append(cur)
+    return [(p.split(":")[0].strip(), "=" in p) for p in parts if p.strip()]
 
 
 class _Recorder:
@@ -84,7 +92,7 @@ class _Recorder:
         return call
 
 
-@pytest.mark.parametrize("mode,nvls", [("ag", True), ("ag", False), ("rs", None)])
+@pytest.mark.parametrize("mode,nvls", [("ag", True), ("ag", False), ("rs", True), ("rs", False)])
 def test_fused_dist_gemm_passes_binding_compatible_arguments(monkeypatch, mode, nvls):
     real = opengda_b200.native()
     rec = _Recorder(real)
@@ -104,3 +112,7 @@ def test_fused_dist_gemm_passes_binding_compatible_arguments(monkeypatch, mode, 
     if mode == "ag":
         assert (args["a_mc"] != 0) == bool(nvls) and (args["arrivals_mc"] != 0) == bool(nvls)
         assert args["tile_counter"] != 0 and args["comm_ctas"] > 0
+    else:
+        assert (args.get("staging_mc", 0) != 0) == bool(nvls)
+        if nvls:
+            assert args["band_tiles"] != 0 and args["tile_counter"] != 0
