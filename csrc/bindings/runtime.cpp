@@ -21,6 +21,8 @@ size_t am_region_bytes(int size, int nslots, uint32_t slot_bytes);
 int am_run(uint8_t* shm, int rank, int size, int nslots, int nmsg, int nreq, uint64_t timeout_ns, uint64_t* out_counter,
            uint64_t* out_checksum);
 int am_wait_one(uint8_t* shm, int rank, int size, int nslots, int src, uint64_t timeout_ns);
+int litmus_run(uint64_t* shm, int rank, int test, int iters, int k, int use_fence, uint32_t seed, uint32_t max_delay,
+               uint64_t timeout_ns, uint64_t* violations);
 }  // namespace fake
 }  // namespace gicc
 
@@ -139,6 +141,17 @@ void bind_runtime(py::module_& m) {
       st = gicc::fake::am_run(reinterpret_cast<uint8_t*>(shm), rank, size, nslots, nmsg, nreq, timeout_ns, &c, &k);
     }
     return py::make_tuple(st, c, k);
+  });
+  m.def("cpu_litmus_run", [](uint64_t shm, int rank, int test, int iters, int k, int use_fence, uint32_t seed,
+                             uint32_t max_delay, uint64_t timeout_ns) {
+    uint64_t v = 0;
+    int st;
+    {
+      py::gil_scoped_release nogil;
+      st = gicc::fake::litmus_run(reinterpret_cast<uint64_t*>(shm), rank, test, iters, k, use_fence, seed, max_delay,
+                                  timeout_ns, &v);
+    }
+    return py::make_tuple(st, v);
   });
   m.def("cpu_am_wait_one", [](uint64_t shm, int rank, int size, int nslots, int src, uint64_t timeout_ns) {
     py::gil_scoped_release rel;

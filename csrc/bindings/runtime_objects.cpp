@@ -263,6 +263,23 @@ void bind_runtime_objects(py::module_& m) {
      py::arg("ldb"), py::arg("slots"), py::arg("arrivals"), py::arg("done"), py::arg("out"), py::arg("ldo"),
      py::arg("epoch"), py::arg("grid"), py::arg("timeout_ns"), py::arg("staging_mc") = 0, py::arg("band_tiles") = 0,
      py::arg("tile_counter") = 0, py::arg("comm_ctas") = 0, py::arg("units_per_band") = 4);
+  m.def("k_litmus", [](int test, int iters, int k, int use_fence, uint32_t seed, uint32_t max_delay, uint64_t timeout_ns,
+                       int role_base, int nroles_here, std::vector<std::vector<uint64_t>> roles) {
+    if (roles.size() != 2) throw std::runtime_error("k_litmus: two role pointer lists");
+    ops::LitmusArgs a;
+    a.test = test; a.iters = iters; a.k = k; a.use_fence = use_fence; a.seed = seed; a.max_delay = max_delay;
+    a.timeout_ns = timeout_ns; a.role_base = role_base;
+    for (int r = 0; r < 2; ++r) {
+      const auto& v = roles[r];
+      if (v.size() != 8) throw std::runtime_error("k_litmus: 8 pointers per role");
+      a.role[r].data = P<uint64_t>(v[0]); a.role[r].flag = P<uint64_t>(v[1]);
+      a.role[r].ready_remote = P<uint64_t>(v[2]); a.role[r].ready_local = P<const uint64_t>(v[3]);
+      a.role[r].mine_remote = P<uint64_t>(v[4]); a.role[r].theirs_local = P<const uint64_t>(v[5]);
+      a.role[r].out = P<uint64_t>(v[6]); a.role[r].result = P<uint64_t>(v[7]);
+    }
+    ops::litmus(a, nroles_here, cur_stream());
+  }, py::arg("test"), py::arg("iters"), py::arg("k"), py::arg("use_fence"), py::arg("seed"), py::arg("max_delay"),
+     py::arg("timeout_ns"), py::arg("role_base"), py::arg("nroles_here"), py::arg("roles"));
   m.def("k_moe_route", [](uint64_t logits, int T, int E, int topk, uint64_t idx, uint64_t w, uint64_t counts) {
     ops::moe_route(P<const float>(logits), T, E, topk, P<int>(idx), P<float>(w), P<int>(counts), cur_stream());
   });

@@ -120,6 +120,27 @@ struct GemmRsArgs {
   int comm_ctas = 0;           // CTAs running the reduce warps (0 = 16)
   int units_per_band = 4;      // row slices per 128-row band (divides 128)
 };
+// Memory-model litmus tests (gicc/proto/litmus.hpp).  test 0 = MP (role 0 writes data and
+// flag into role 1's memory; role 1 checks), test 1 = SB (each role stores into the other's
+// word array, optionally fence.sc, then loads its own copy of the other's word).
+struct LitmusRole {
+  uint64_t* data = nullptr;          // MP: the reader's data ring (k words)
+  uint64_t* flag = nullptr;          // MP: the reader's flag word
+  uint64_t* ready_remote = nullptr;  // SB: the other role's ready word
+  const uint64_t* ready_local = nullptr;
+  uint64_t* mine_remote = nullptr;   // SB: the other role's copy of this role's word array
+  const uint64_t* theirs_local = nullptr;
+  uint64_t* out = nullptr;           // SB: [iters] loaded values
+  uint64_t* result = nullptr;        // [2]: status, MP violations (device memory)
+};
+struct LitmusArgs {
+  int test = 0, iters = 0, k = 64, use_fence = 1;
+  uint32_t seed = 1, max_delay = 256;
+  uint64_t timeout_ns = 0;
+  int role_base = 0;                 // first role run on this GPU
+  LitmusRole role[2];
+};
+GICC_EXPORT void litmus(const LitmusArgs& a, int nroles_here, cudaStream_t s);
 GICC_EXPORT void ag_gemm(const AgGemmArgs& a, cudaStream_t s);
 GICC_EXPORT void gemm_rs(const GemmRsArgs& a, cudaStream_t s);
 

@@ -54,7 +54,11 @@ struct DevMem {
   static __device__ __forceinline__ void add_release(uint64_t* p, uint64_t v) {
     asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
   }
+  static __device__ __forceinline__ void store_relaxed(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+  }
   static __device__ __forceinline__ void fence() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+  static __device__ __forceinline__ void fence_sc() { asm volatile("fence.sc.sys;" ::: "memory"); }
   static __device__ __forceinline__ uint64_t now_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -69,7 +73,9 @@ struct HostMem {
   static inline uint64_t load_relaxed(const uint64_t* p) { return __atomic_load_n(p, __ATOMIC_RELAXED); }
   static inline void store_release(uint64_t* p, uint64_t v) { __atomic_store_n(p, v, __ATOMIC_RELEASE); }
   static inline void add_release(uint64_t* p, uint64_t v) { __atomic_fetch_add(p, v, __ATOMIC_RELEASE); }
+  static inline void store_relaxed(uint64_t* p, uint64_t v) { __atomic_store_n(p, v, __ATOMIC_RELAXED); }
   static inline void fence() { __atomic_thread_fence(__ATOMIC_SEQ_CST); }
+  static inline void fence_sc() { __atomic_thread_fence(__ATOMIC_SEQ_CST); }
 #if !defined(__CUDA_ARCH__)
   static inline uint64_t now_ns() {
     timespec ts;

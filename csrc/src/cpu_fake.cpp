@@ -9,6 +9,7 @@
 
 #include "gicc/proto/am.hpp"
 #include "gicc/proto/barrier.hpp"
+#include "gicc/proto/litmus.hpp"
 #include "gicc/types.hpp"
 #include "gicc/visibility.hpp"
 
@@ -183,6 +184,33 @@ GICC_EXPORT int am_run(uint8_t* shm, int rank, int size, int nslots, int nmsg, i
 GICC_EXPORT int am_wait_one(uint8_t* shm, int rank, int size, int nslots, int src, uint64_t timeout_ns) {
   am::AmView v = make_view(shm, rank, size, nslots, am::AM_SHORT_SIZE + 256, timeout_ns);
   return am::wait_one<HostMem>(v, src);
+}
+
+// Litmus tests (proto/litmus.hpp) between CPU ranks 0 and 1.  shm holds two regions of
+// 2 + k + 2*iters + 2 words: ready, flag, data[k], W[iters], out[iters], result[2].
+GICC_EXPORT int litmus_run(uint64_t* shm, int rank, int test, int iters, int k, int use_fence, uint32_t seed,
+                           uint32_t max_delay, uint64_t timeout_ns, uint64_t* violations) {
+  if (rank < 0 || rank > 1) return GICC_OK;
+  const size_t words = 2 + (size_t)k + 2 * (size_t)iters + 2;
+  uint64_t* mine = shm + (size_t)rank * words;
+  uint64_t* other = shm + (size_t)(1 - rank) * words;
+  uint64_t* result = mine + 2 + k + 2 * (size_t)iters;
+  uint64_t v = 0;
+  int st = GICC_OK;
+  if (test == 0) {
+    if (rank == 0) {
+      proto::litmus_mp_writer<HostMem>(other + 2, other + 1, k, iters, seed, max_delay);
+    } else {
+      st = proto::litmus_mp_reader<HostMem>(mine + 2, mine + 1, k, iters, seed + 17u, max_delay, timeout_ns, &v);
+    }
+  } else {
+    st = proto::litmus_sb_side<HostMem>(other + 0, mine + 0, other + 2 + k, mine + 2 + k, iters, use_fence,
+                                        seed + 17u * rank, max_delay, timeout_ns, mine + 2 + k + iters);
+  }
+  result[0] = (uint64_t)st;
+  result[1] = v;
+  if (violations) *violations = v;
+  return st;
 }
 
 }  // namespace fake

@@ -30,4 +30,7 @@ def test_multigpu_suite(tmp_path):
         assert r["jacobi_mismatch"] == 0, r
         assert r["moe_relerr"] < 2e-2, r
         assert r["am_counter_ok"] and r["am_checksum_ok"], r
+    mp, sb = res[0]["litmus_mp"], res[0]["litmus_sb"]
+    assert mp["status"] == 0 and mp["violations"] == 0, mp
+    assert sb["status"] == 0 and sb["outcomes"]["00"] == 0 and sum(sb["outcomes"].values()) == 20000, sb
     print(json.dumps(res))

@@ -56,3 +56,30 @@ def test_active_message_drop_times_out(tmp_path):
     path = _shm(tmp_path, 2 * native().cpu_am_region_bytes(2, 4, 64 + 256) + 4096)
     rc, res = _run(2, path, "am_drop", [], tmp_path)
     assert res[0] == "0", res  # 0 messages handled: the wait ended by timeout
+
+
+def _litmus(tmp_path, test, iters, k, fence, max_delay):
+    words = 2 + k + 2 * iters + 2
+    path = _shm(tmp_path, 2 * words * 8 + 4096)
+    rc, res = _run(2, path, "litmus", [test, iters, k, fence, max_delay], tmp_path)
+    import numpy as np
+    arr = np.fromfile(path, dtype=np.uint64, count=2 * words).reshape(2, words)
+    return rc, res, arr, words
+
+
+def test_litmus_message_passing_cpu_ranks(tmp_path):
+    """MP: new flag with old data never happens with release/acquire (the signal protocol)."""
+    rc, res, arr, _ = _litmus(tmp_path, 0, 20000, 64, 1, 64)
+    assert rc == 0, res
+    assert res[1] == "0 0", res  # reader: ok, zero violations
+
+
+def test_litmus_store_buffering_with_fence_cpu_ranks(tmp_path):
+    """SB with a seq_cst fence between store and load: (0, 0) is forbidden."""
+    iters, k = 20000, 1
+    rc, res, arr, words = _litmus(tmp_path, 1, iters, k, 1, 64)
+    assert rc == 0 and res == ["0 0", "0 0"], res
+    out0 = arr[0, 2 + k + iters:2 + k + 2 * iters]
+    out1 = arr[1, 2 + k + iters:2 + k + 2 * iters]
+    assert int(((out0 == 0) & (out1 == 0)).sum()) == 0
+    assert int(((out0 == 1) | (out1 == 1)).sum()) == iters

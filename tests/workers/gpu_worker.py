@@ -173,6 +173,15 @@ def main():
     res["am_reqrep_rtt_us"] = rtt.item() / 1000 / 1e3 if r == 0 else None
     rt.check_device_errors()
     torch.cuda.synchronize()
+
+    # 10. litmus tests across GPUs 0 and 1 (NVLink peer words, random delays)
+    from opengda_b200.utils import litmus
+    mp = litmus.run(litmus.MP, iters=20000, k=64, max_delay=512, rt=rt)
+    sb = litmus.run(litmus.SB, iters=20000, use_fence=True, max_delay=512, rt=rt)
+    if r == 0:
+        res["litmus_mp"] = mp
+        res["litmus_sb"] = sb
+    torch.cuda.synchronize()
     boot.barrier()
     with open(f"{out}.{r}", "w") as f:
         json.dump(res, f)
