@@ -17,6 +17,8 @@ void bind_runtime_objects(py::module_& m);  // runtime_objects.cpp
 namespace gicc {
 namespace fake {
 int barrier_run(uint64_t* shm, int rank, int size, int iters, int mode, uint64_t timeout_ns, int skip_at, int* fail_iter);
+int barrier_run_inject(uint64_t* shm, int rank, int size, int iters, int mode, uint64_t timeout_ns, int skip_at,
+                       int* fail_iter, int inject_mode, int inject_at);
 size_t am_region_bytes(int size, int nslots, uint32_t slot_bytes);
 int am_run(uint8_t* shm, int rank, int size, int nslots, int nmsg, int nreq, uint64_t timeout_ns, uint64_t* out_counter,
            uint64_t* out_checksum);
@@ -141,6 +143,16 @@ void bind_runtime(py::module_& m) {
       st = gicc::fake::am_run(reinterpret_cast<uint8_t*>(shm), rank, size, nslots, nmsg, nreq, timeout_ns, &c, &k);
     }
     return py::make_tuple(st, c, k);
+  });
+  m.def("cpu_barrier_run_inject", [](uint64_t shm, int rank, int size, int iters, int mode, uint64_t timeout_ns,
+                                     int inject_mode, int inject_at) {
+    int fail = -1, st;
+    {
+      py::gil_scoped_release nogil;
+      st = gicc::fake::barrier_run_inject(reinterpret_cast<uint64_t*>(shm), rank, size, iters, mode, timeout_ns, -1,
+                                          &fail, inject_mode, inject_at);
+    }
+    return py::make_tuple(st, fail);
   });
   m.def("cpu_litmus_run", [](uint64_t shm, int rank, int test, int iters, int k, int use_fence, uint32_t seed,
                              uint32_t max_delay, uint64_t timeout_ns) {

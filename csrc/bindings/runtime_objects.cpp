@@ -113,6 +113,8 @@ void bind_runtime_objects(py::module_& m) {
       .def("device_ctx", [](Barrier& b) { return A(b.device_ctx()); })
       .def("advance", &Barrier::advance)
       .def("count", &Barrier::count)
+      .def("inject_fault", &Barrier::inject_fault, py::arg("mode"), py::arg("epoch"), py::arg("timeout_ms") = 0)
+      .def_property_readonly("next_epoch", &Barrier::next_epoch)
       .def_property_readonly("uses_nvls", &Barrier::uses_nvls);
 
   py::class_<am::Am, std::shared_ptr<am::Am>>(m, "Am")

@@ -33,6 +33,11 @@ class GICC_EXPORT Barrier {
   // device epoch themselves (ops::barrier_continuous); no device memory is touched.
   void advance(uint64_t n);
   uint64_t count() const;              // barriers completed on this rank
+  // Failure-detection tests: at barrier number `epoch` (the value of expected_signal) this
+  // rank leaves its signal out (mode 1) or sends a stale epoch (mode 2); peers then end
+  // that barrier with GICC_ETIMEDOUT after timeout_ms (0 = keep the current bound).
+  void inject_fault(int mode, uint64_t epoch, uint64_t timeout_ms = 0);
+  uint64_t next_epoch() const { return epoch_ + 1; }
   bool uses_nvls() const { return nvls_; }
 
  private:

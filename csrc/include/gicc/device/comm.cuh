@@ -258,16 +258,17 @@ __device__ __forceinline__ void* remote_ptr(GiccContext* ctx, const void* local,
 // once at the end: a pending PCIe write would otherwise stall the next barrier's fence).
 __device__ __forceinline__ int barrier(BarrierCtx* ctx, bool report = true) {
   const uint64_t epoch = *reinterpret_cast<volatile uint64_t*>(&ctx->expected_signal);
+  const int inject = (ctx->inject_mode && epoch == ctx->inject_epoch) ? ctx->inject_mode : proto::INJECT_NONE;
   uint64_t seen = 0;
   int st;
   if (ctx->mc_counter != nullptr) {
     uint64_t* mc = ctx->mc_counter;
     st = proto::counter_barrier<proto::DevMem>([mc] { ptx::multimem_red_release_add_u64(mc, 1); }, ctx->mc_local,
-                                               ctx->size, epoch, ctx->timeout_ns, &seen);
+                                               ctx->size, epoch, ctx->timeout_ns, &seen, inject);
   } else {
     int round = -1;
     st = proto::dissemination_barrier<proto::DevMem>(ctx->n_rounds, ctx->trigger_addrs, ctx->signals, epoch,
-                                                     ctx->timeout_ns, &round, &seen);
+                                                     ctx->timeout_ns, &round, &seen, inject);
   }
   if (st != GICC_OK) {
     report_error(ctx->err, st, W_BARRIER, ctx->rank, -1, seen, epoch);

@@ -19,12 +19,23 @@ GICC_HD int n_rounds_for(int n) {
   return r;
 }
 
+// Failure injection for the failure-detection tests: this rank's round-0 signal is left
+// out (SKIP_SIGNAL) or carries the previous epoch (STALE_EPOCH).  Either way the peer that
+// waits for it runs out its bounded wait and reports GICC_ETIMEDOUT; nothing faults.
+enum Inject : int { INJECT_NONE = 0, INJECT_SKIP_SIGNAL = 1, INJECT_STALE_EPOCH = 2 };
+
 template <class Mem>
 GICC_HD int dissemination_barrier(int n_rounds, uint64_t* const* trigger, uint64_t* signals, uint64_t epoch,
-                                  uint64_t timeout_ns, int* fail_round, uint64_t* seen) {
+                                  uint64_t timeout_ns, int* fail_round, uint64_t* seen, int inject = INJECT_NONE) {
   Mem::fence();  // everything before the barrier is visible before our first signal
   for (int k = 0; k < n_rounds; ++k) {
-    Mem::store_release(trigger[k], epoch);
+    if (k == 0 && inject == INJECT_SKIP_SIGNAL) {
+      // signal left out
+    } else if (k == 0 && inject == INJECT_STALE_EPOCH) {
+      Mem::store_release(trigger[k], epoch - 1);
+    } else {
+      Mem::store_release(trigger[k], epoch);
+    }
     if (!wait_until<Mem>(&signals[k], CMP_GE, epoch, timeout_ns, seen)) {
       if (fail_round) *fail_round = k;
       return GICC_ETIMEDOUT;
@@ -38,9 +49,9 @@ GICC_HD int dissemination_barrier(int n_rounds, uint64_t* const* trigger, uint64
 // epoch * n.  `add` performs the release-add on the shared counter.
 template <class Mem, class AddFn>
 GICC_HD int counter_barrier(AddFn add, const uint64_t* local_counter, int n, uint64_t epoch, uint64_t timeout_ns,
-                            uint64_t* seen) {
+                            uint64_t* seen, int inject = INJECT_NONE) {
   Mem::fence();
-  add();
+  if (inject == INJECT_NONE) add();  // both injections leave this rank's arrival out
   if (!wait_until<Mem>(local_counter, CMP_GE, epoch * (uint64_t)n, timeout_ns, seen)) return GICC_ETIMEDOUT;
   return GICC_OK;
 }

@@ -106,6 +106,10 @@ struct BarrierCtx {
   uint64_t* mc_local;                        // NVLS: this rank's copy of that counter
   ErrorRecord* err;
   uint64_t timeout_ns;
+  // failure injection (tests only): at barrier epoch inject_epoch this rank applies
+  // inject_mode (proto::Inject) to its own signal
+  int inject_mode;
+  uint64_t inject_epoch;
 };
 
 }  // namespace gicc

@@ -103,6 +103,17 @@ void Barrier::wait_done(uint64_t target) {
 
 void Barrier::wait_completion() { wait_done(target_); }
 void Barrier::wait_continuous() { wait_done(target_); }
+void Barrier::inject_fault(int mode, uint64_t epoch, uint64_t timeout_ms) {
+  if (mode < proto::INJECT_NONE || mode > proto::INJECT_STALE_EPOCH)
+    throw std::runtime_error("gicc::Barrier::inject_fault: mode 0 (none), 1 (skip signal) or 2 (stale epoch)");
+  BarrierCtx c;
+  GICC_CUDA(cudaMemcpy(&c, dctx_, sizeof(c), cudaMemcpyDeviceToHost));
+  c.inject_mode = mode;
+  c.inject_epoch = epoch;
+  if (timeout_ms) c.timeout_ns = timeout_ms * 1000000ull;
+  GICC_CUDA(cudaMemcpy(dctx_, &c, sizeof(c), cudaMemcpyHostToDevice));
+}
+
 uint64_t Barrier::count() const { return done_host_ ? *reinterpret_cast<volatile uint64_t*>(done_host_) : 0; }
 
 }  // namespace gicc

@@ -29,8 +29,16 @@ struct BarrierLayout {
 // reference's barrier verifier, legacy/ofi/prototype/barrier-verify.cpp:347-400).
 // mode 0 = dissemination, 1 = shared-counter.  skip_at >= 0: this rank stops participating
 // at that barrier (to test timeouts).  Returns 0 ok, 1 timeout, 2 ordering violation.
+GICC_EXPORT int barrier_run_inject(uint64_t* shm, int rank, int size, int iters, int mode, uint64_t timeout_ns,
+                                   int skip_at, int* fail_iter, int inject_mode, int inject_at);
 GICC_EXPORT int barrier_run(uint64_t* shm, int rank, int size, int iters, int mode, uint64_t timeout_ns, int skip_at,
                             int* fail_iter) {
+  return barrier_run_inject(shm, rank, size, iters, mode, timeout_ns, skip_at, fail_iter, 0, -1);
+}
+
+// inject_mode (proto::Inject) is applied by this rank to its own signal at iteration inject_at.
+GICC_EXPORT int barrier_run_inject(uint64_t* shm, int rank, int size, int iters, int mode, uint64_t timeout_ns,
+                                   int skip_at, int* fail_iter, int inject_mode, int inject_at) {
   uint64_t* sig = shm;                       // [size][16]
   uint64_t* counter = shm + (size_t)size * 16;
   uint64_t* progress = counter + 8;          // [size]
@@ -43,12 +51,14 @@ GICC_EXPORT int barrier_run(uint64_t* shm, int rank, int size, int iters, int mo
     HostMem::store_release(&progress[rank], epoch);
     int st;
     uint64_t seen = 0;
+    const int inj = it == inject_at ? inject_mode : proto::INJECT_NONE;
     if (mode == 0) {
       int round = -1;
-      st = proto::dissemination_barrier<HostMem>(rounds, trig, sig + (size_t)rank * 16, epoch, timeout_ns, &round, &seen);
+      st = proto::dissemination_barrier<HostMem>(rounds, trig, sig + (size_t)rank * 16, epoch, timeout_ns, &round, &seen,
+                                                 inj);
     } else {
       st = proto::counter_barrier<HostMem>([counter] { HostMem::add_release(counter, 1); }, counter, size, epoch,
-                                           timeout_ns, &seen);
+                                           timeout_ns, &seen, inj);
     }
     if (st != GICC_OK) {
       if (fail_iter) *fail_iter = it;

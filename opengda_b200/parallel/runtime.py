@@ -210,6 +210,18 @@ class Barrier:
     def uses_nvls(self) -> bool:
         return self._b.uses_nvls
 
+    # failure detection tests ---------------------------------------------------------------
+    SKIP_SIGNAL, STALE_EPOCH = 1, 2
+
+    def inject_fault(self, mode: int, after: int = 0, timeout_ms: int = 0) -> int:
+        """Make this rank misbehave in the barrier ``after`` barriers from now: leave its
+        signal out (``SKIP_SIGNAL``) or send the previous epoch (``STALE_EPOCH``).  The peers
+        (and possibly this rank) end that barrier with ETIMEDOUT after ``timeout_ms``;
+        nothing faults or hangs.  Returns the epoch of the affected barrier."""
+        epoch = self._b.next_epoch + after
+        self._b.inject_fault(mode, epoch, timeout_ms)
+        return epoch
+
     # kernels -------------------------------------------------------------------------------
     def run_single(self, flag_ptr: int = 0) -> None:
         """setup() + one device barrier kernel (reference examples/ofi/barrier_test.cpp:20-24)."""

@@ -30,6 +30,9 @@ def test_multigpu_suite(tmp_path):
         assert r["jacobi_mismatch"] == 0, r
         assert r["moe_relerr"] < 2e-2, r
         assert r["am_counter_ok"] and r["am_checksum_ok"], r
+    assert all(r["context_ok_after_inject"] for r in res), res
+    timed_out = [r["rank"] for r in res if r["inject_error"]["status"] == "ETIMEDOUT"]
+    assert timed_out and all(res[i]["inject_error"]["where"] == "barrier" for i in timed_out), res
     mp, sb = res[0]["litmus_mp"], res[0]["litmus_sb"]
     assert mp["status"] == 0 and mp["violations"] == 0, mp
     assert sb["status"] == 0 and sb["outcomes"]["00"] == 0 and sum(sb["outcomes"].values()) == 20000, sb

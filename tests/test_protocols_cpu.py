@@ -83,3 +83,20 @@ def test_litmus_store_buffering_with_fence_cpu_ranks(tmp_path):
     out1 = arr[1, 2 + k + iters:2 + k + 2 * iters]
     assert int(((out0 == 0) & (out1 == 0)).sum()) == 0
     assert int(((out0 == 1) | (out1 == 1)).sum()) == iters
+
+
+@pytest.mark.parametrize("mode,inject", [(0, 1), (0, 2), (1, 1)])
+def test_injected_signal_fault_ends_in_timeout(mode, inject, tmp_path):
+    """Failure injection (host side of the device feature): rank 1 leaves its signal out
+    (1) or sends the previous epoch (2) at barrier 50.  The rank waiting for that signal
+    reports a timeout at barrier 50 -- no hang, and nobody passes a barrier early (the
+    progress check of every barrier would report 2)."""
+    n = 3
+    path = _shm(tmp_path, (n * 16 + 8 + n) * 8 + 4096)
+    rc, res = _run(n, path, "barrier_inject", [100, mode, 1, inject, 50], tmp_path)
+    parsed = [tuple(int(x) for x in r.split()) for r in res]
+    assert all(st in (0, 1) for st, _ in parsed), parsed           # never an ordering violation (2)
+    assert (1, 50) in parsed, parsed                               # the waiting rank saw the timeout there
+    # a rank whose own signals all arrived may pass barrier 50 (every rank did arrive) and
+    # time out in the next one; nothing fails earlier
+    assert all(fail in (-1, 50, 51) for _, fail in parsed), parsed

@@ -182,6 +182,26 @@ def main():
         res["litmus_mp"] = mp
         res["litmus_sb"] = sb
     torch.cuda.synchronize()
+
+    # 11. failure injection: in a dissemination barrier rank 1 leaves its signal out; the rank
+    # waiting for it ends the barrier with ETIMEDOUT (300 ms bound), and every context still
+    # runs kernels afterwards.  Nobody leaves the job and no multicast memory is involved.
+    boot.barrier()
+    fb = Barrier(rt)  # dissemination (no NVLS)
+    fb.device_barrier(3)
+    torch.cuda.synchronize()
+    N.read_errors(True)
+    fb.inject_fault(Barrier.SKIP_SIGNAL if r == 1 else 0, after=0, timeout_ms=300)
+    fb.device_barrier(1)
+    torch.cuda.synchronize()
+    e = N.read_errors(True)
+    res["inject_error"] = {"status": e["status"], "where": e["where"]}
+    probe = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
+    N.k_fill_pattern(probe.data_ptr(), 1 << 20, 7)
+    badp = torch.zeros(1, dtype=torch.int64, device="cuda")
+    N.k_check_pattern(probe.data_ptr(), 1 << 20, 7, badp.data_ptr())
+    torch.cuda.synchronize()
+    res["context_ok_after_inject"] = int(badp.item()) == 0
     boot.barrier()
     with open(f"{out}.{r}", "w") as f:
         json.dump(res, f)

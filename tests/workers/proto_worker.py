@@ -31,6 +31,11 @@ def main():
     elif what == "am_drop":
         # rank 0 waits for a message from rank 1, which never sends it
         res = str(n.cpu_am_wait_one(addr, rank, size, 4, 1, 300_000_000)) if rank == 0 else "idle"
+    elif what == "barrier_inject":
+        iters, mode, inj_rank, inj_mode, inj_at = args
+        st, fail = n.cpu_barrier_run_inject(addr, rank, size, iters, mode, 10_000_000_000,
+                                            inj_mode if rank == inj_rank else 0, inj_at)
+        res = f"{st} {fail}"
     elif what == "litmus":
         test, iters, k, fence, max_delay = args
         st, v = n.cpu_litmus_run(addr, rank, test, iters, k, fence, 7, max_delay, 20_000_000_000)
