@@ -23,6 +23,7 @@ size_t am_region_bytes(int size, int nslots, uint32_t slot_bytes);
 int am_run(uint8_t* shm, int rank, int size, int nslots, int nmsg, int nreq, uint64_t timeout_ns, uint64_t* out_counter,
            uint64_t* out_checksum);
 int am_wait_one(uint8_t* shm, int rank, int size, int nslots, int src, uint64_t timeout_ns);
+int cmdring_selftest(int ncmds, int nslots, uint64_t idle_timeout_ns);
 int litmus_run(uint64_t* shm, int rank, int test, int iters, int k, int use_fence, uint32_t seed, uint32_t max_delay,
                uint64_t timeout_ns, uint64_t* violations);
 }  // namespace fake
@@ -153,6 +154,10 @@ void bind_runtime(py::module_& m) {
                                           &fail, inject_mode, inject_at);
     }
     return py::make_tuple(st, fail);
+  });
+  m.def("cpu_cmdring_selftest", [](int ncmds, int nslots, uint64_t idle_timeout_ns) {
+    py::gil_scoped_release nogil;
+    return gicc::fake::cmdring_selftest(ncmds, nslots, idle_timeout_ns);
   });
   m.def("cpu_litmus_run", [](uint64_t shm, int rank, int test, int iters, int k, int use_fence, uint32_t seed,
                              uint32_t max_delay, uint64_t timeout_ns) {

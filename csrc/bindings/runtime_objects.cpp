@@ -3,6 +3,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <torch/extension.h>
 
+#include "gicc/cmdring.hpp"
 #include "gicc/am.hpp"
 #include "gicc/barrier.hpp"
 #include "gicc/ops.hpp"
@@ -116,6 +117,27 @@ void bind_runtime_objects(py::module_& m) {
       .def("inject_fault", &Barrier::inject_fault, py::arg("mode"), py::arg("epoch"), py::arg("timeout_ms") = 0)
       .def_property_readonly("next_epoch", &Barrier::next_epoch)
       .def_property_readonly("uses_nvls", &Barrier::uses_nvls);
+
+  py::class_<CmdRing, std::shared_ptr<CmdRing>>(m, "CmdRing")
+      .def(py::init<Runtime&, int, int, uint64_t>(), py::arg("runtime"), py::arg("nslots") = 64,
+           py::arg("threads") = 256, py::arg("idle_timeout_ms") = 10000, py::keep_alive<1, 2>())
+      .def("start", &CmdRing::start)
+      .def("put", [](CmdRing& c, uint64_t src, int rank, int buf, size_t off, size_t size, uint64_t user) {
+             return c.put(P<const void>(src), rank, buf, off, size, user);
+           }, py::arg("src"), py::arg("dst_rank"), py::arg("dst_buf"), py::arg("dst_off"), py::arg("size"),
+           py::arg("user") = 0)
+      .def("get", [](CmdRing& c, uint64_t dst, int rank, int buf, size_t off, size_t size, uint64_t user) {
+             return c.get(P<void>(dst), rank, buf, off, size, user);
+           }, py::arg("dst"), py::arg("src_rank"), py::arg("src_buf"), py::arg("src_off"), py::arg("size"),
+           py::arg("user") = 0)
+      .def("signal", &CmdRing::signal, py::arg("dst_rank"), py::arg("word"), py::arg("value"))
+      .def("add", &CmdRing::add, py::arg("dst_rank"), py::arg("word"), py::arg("value"))
+      .def("fence", &CmdRing::fence)
+      .def("wait", &CmdRing::wait, py::call_guard<py::gil_scoped_release>())
+      .def("completed", &CmdRing::completed)
+      .def("stop", &CmdRing::stop, py::call_guard<py::gil_scoped_release>())
+      .def("status", &CmdRing::status)
+      .def_property_readonly("running", &CmdRing::running);
 
   py::class_<am::Am, std::shared_ptr<am::Am>>(m, "Am")
       .def(py::init<Runtime&, int, uint32_t>(), py::arg("runtime"), py::arg("nslots") = am::AM_DEFAULT_RING_SLOTS,

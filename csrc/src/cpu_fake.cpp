@@ -5,10 +5,12 @@
 #include <cstring>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "gicc/proto/am.hpp"
 #include "gicc/proto/barrier.hpp"
+#include "gicc/proto/cmdring.hpp"
 #include "gicc/proto/litmus.hpp"
 #include "gicc/types.hpp"
 #include "gicc/visibility.hpp"
@@ -221,6 +223,66 @@ GICC_EXPORT int litmus_run(uint64_t* shm, int rank, int test, int iters, int k, 
   result[1] = v;
   if (violations) *violations = v;
   return st;
+}
+
+// Command ring (proto/cmdring.hpp) with a CPU consumer thread: the producer queues
+// ncmds puts of varying size and offset into dst plus a signal after every 8th, through a
+// ring of nslots; the consumer thread executes them.  Returns 0 ok, 1 consumer timeout,
+// 2 data mismatch, 3 producer could not get a slot.
+GICC_EXPORT int cmdring_selftest(int ncmds, int nslots, uint64_t idle_timeout_ns) {
+  std::vector<proto::Command> cmds(nslots);
+  uint64_t done = 0, status = ~0ull, sig = 0;
+  proto::CmdRingView v{cmds.data(), nslots, &done, &status, idle_timeout_ns};
+  std::vector<uint8_t> src(1 << 16), dst(1 << 16, 0);
+  for (size_t i = 0; i < src.size(); ++i) src[i] = (uint8_t)(i * 13 + 7);
+  std::thread consumer([&] {
+    for (uint64_t i = 0;; ++i) {
+      proto::Command c;
+      if (!proto::cmdring_next<HostMem>(v, i, &c)) {
+        __atomic_store_n(&status, (uint64_t)GICC_ETIMEDOUT, __ATOMIC_RELEASE);
+        return;
+      }
+      if (c.op == proto::CMD_EXIT) {
+        proto::cmdring_complete<HostMem>(v, i);
+        __atomic_store_n(&status, (uint64_t)GICC_OK, __ATOMIC_RELEASE);
+        return;
+      }
+      if (c.op == proto::CMD_PUT) std::memcpy(reinterpret_cast<void*>(c.dst), reinterpret_cast<const void*>(c.src), c.size);
+      if (c.op == proto::CMD_ADD) HostMem::add_release(reinterpret_cast<uint64_t*>(c.dst), c.value);
+      proto::cmdring_complete<HostMem>(v, i);
+    }
+  });
+  int rc = 0;
+  uint64_t next = 0;
+  for (int k = 0; k < ncmds && rc == 0; ++k) {
+    proto::Command c{};
+    const size_t off = ((size_t)k * 977) % (dst.size() - 4096), len = 1 + ((size_t)k * 131) % 4096;
+    c.op = proto::CMD_PUT;
+    c.src = reinterpret_cast<uint64_t>(src.data() + off);
+    c.dst = reinterpret_cast<uint64_t>(dst.data() + off);
+    c.size = len;
+    if (!proto::cmdring_push<HostMem>(v, next++, c, 10000000000ull)) rc = 3;
+    if (k % 8 == 7) {
+      proto::Command a{};
+      a.op = proto::CMD_ADD;
+      a.dst = reinterpret_cast<uint64_t>(&sig);
+      a.value = 1;
+      if (!proto::cmdring_push<HostMem>(v, next++, a, 10000000000ull)) rc = 3;
+    }
+  }
+  proto::Command e{};
+  e.op = proto::CMD_EXIT;
+  if (rc == 0 && !proto::cmdring_push<HostMem>(v, next++, e, 10000000000ull)) rc = 3;
+  consumer.join();
+  if (rc) return rc;
+  if (status != GICC_OK || done != next) return 1;
+  if (sig != (uint64_t)(ncmds / 8)) return 2;
+  for (int k = 0; k < ncmds; ++k) {
+    const size_t off = ((size_t)k * 977) % (dst.size() - 4096), len = 1 + ((size_t)k * 131) % 4096;
+    for (size_t j = off; j < off + len; ++j)
+      if (dst[j] != src[j]) return 2;
+  }
+  return 0;
 }
 
 }  // namespace fake

@@ -100,3 +100,11 @@ def test_injected_signal_fault_ends_in_timeout(mode, inject, tmp_path):
     # a rank whose own signals all arrived may pass barrier 50 (every rank did arrive) and
     # time out in the next one; nothing fails earlier
     assert all(fail in (-1, 50, 51) for _, fail in parsed), parsed
+
+
+@pytest.mark.parametrize("ncmds,nslots", [(500, 2), (2000, 8), (300, 64)])
+def test_command_ring_protocol_cpu_consumer(ncmds, nslots):
+    """The host -> GPU command ring's producer/consumer code with a CPU consumer thread:
+    puts land, adds count, credits recycle slots, EXIT ends the consumer."""
+    from opengda_b200 import native
+    assert native().cpu_cmdring_selftest(ncmds, nslots, 5_000_000_000) == 0
