@@ -7,6 +7,10 @@
 // stop() or after idle_timeout_ms without commands (status() then reports ETIMEDOUT);
 // start() launches it again, and stop() drops commands the kernel did not reach.  Commands
 // complete in order; wait(seq) covers seq and all before it.
+//
+// While the ring kernel is resident, the first launch of a kernel that this process has not
+// loaded yet (CUDA lazy module loading, the default) waits until the ring kernel exits.
+// Launch such kernels once before start(), or run with CUDA_MODULE_LOADING=EAGER.
 #pragma once
 #include <cuda_runtime.h>
 

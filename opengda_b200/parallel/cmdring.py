@@ -6,6 +6,10 @@
     ring.signal(dst_rank, word, value)
     ring.wait(seq); ring.stop()
 
+While the ring kernel is resident, the first launch of a kernel this process has not yet
+loaded (CUDA lazy module loading) waits until the ring exits -- warm such kernels up before
+``start()`` or set ``CUDA_MODULE_LOADING=EAGER``.
+
 The reference has the same component, unused, for its NIC path
 (src/gicc/platform/mlx5/persistent.cuh:27-47, 239-311).
 """

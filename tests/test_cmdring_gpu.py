@@ -18,10 +18,13 @@ def rt():
 
 
 def test_cmdring_puts_gets_signals(rt):
+    # Everything is allocated before start() and checked after stop(): no kernel launches
+    # while the ring kernel is resident (see the lazy-loading note in CmdRing).
     from opengda_b200 import native
     from opengda_b200.parallel.cmdring import CmdRing
     buf = rt.alloc_tensor((1 << 20,), torch.uint8)
     src = torch.randint(0, 256, (1 << 20,), dtype=torch.uint8, device="cuda")
+    back = torch.zeros(4096, dtype=torch.uint8, device="cuda")
     word = rt.signal_alloc(1)
     torch.cuda.synchronize()
     ring = CmdRing(rt, nslots=8)
@@ -31,20 +34,20 @@ def test_cmdring_puts_gets_signals(rt):
         off = (k * 12289) % ((1 << 20) - 8192)
         last = ring.put(src.data_ptr() + off, rt.rank, buf.index, off, 1 + (k * 131) % 8192)
     sig = ring.signal(rt.rank, word, 4242)
-    ring.wait(sig)
-    assert sig == last + 1 and ring.completed() == sig
-    got = buf.local.clone()
+    got = ring.get(back.data_ptr(), rt.rank, buf.index, 0, 4096)
+    ring.wait(got)
+    assert sig == last + 1 and got == sig + 1 and ring.completed() == got
+    ring.stop()
+    assert ring.status() == 0 and not ring.running
+    host = buf.local.cpu()
+    s = src.cpu()
     for k in range(64):
         off = (k * 12289) % ((1 << 20) - 8192)
         n = 1 + (k * 131) % 8192
-        assert torch.equal(got[off:off + n], src[off:off + n]), k
-    back = torch.zeros(4096, dtype=torch.uint8, device="cuda")
-    ring.wait(ring.get(back.data_ptr(), rt.rank, buf.index, 0, 4096))
-    assert torch.equal(back, buf.local[:4096])
+        assert torch.equal(host[off:off + n], s[off:off + n]), k
+    assert torch.equal(back.cpu(), host[:4096])
     sig_word = native().tensor_from_ptr(rt.signal_local(word), [1], "int64", rt.gpu_id)
     assert int(sig_word.item()) == 4242
-    ring.stop()
-    assert ring.status() == 0 and not ring.running
 
 
 def test_cmdring_idle_timeout_exit_and_restart(rt):
@@ -61,5 +64,5 @@ def test_cmdring_idle_timeout_exit_and_restart(rt):
     ring.stop()
     ring.start()  # launches again from the same ring
     ring.wait(ring.put(src.data_ptr(), rt.rank, buf.index, 0, 4096))
-    assert torch.equal(buf.local, src)
     ring.stop()
+    assert torch.equal(buf.local.cpu(), src.cpu())
