@@ -304,6 +304,22 @@ void bind_runtime_objects(py::module_& m) {
     ops::litmus(a, nroles_here, cur_stream());
   }, py::arg("test"), py::arg("iters"), py::arg("k"), py::arg("use_fence"), py::arg("seed"), py::arg("max_delay"),
      py::arg("timeout_ns"), py::arg("role_base"), py::arg("nroles_here"), py::arg("roles"));
+  m.def("k_phase_loop", [](uint64_t bar, uint64_t x, uint64_t y, uint64_t recv, uint64_t send_remote, size_t n,
+                           int iters, float a, int rank, int left, uint64_t stamps, uint64_t bad) {
+    ops::phase_loop(P<BarrierCtx>(bar), P<float>(x), P<float>(y), P<const float>(recv), P<float>(send_remote), n, iters,
+                    a, rank, left, P<uint64_t>(stamps), P<unsigned long long>(bad), cur_stream());
+  });
+  m.def("k_saxpy_put", [](uint64_t x, uint64_t y, float a, size_t n, uint64_t dst_remote, uint64_t arrivals_remote,
+                          int blocks) {
+    ops::saxpy_put(P<const float>(x), P<float>(y), a, n, P<float>(dst_remote), P<uint64_t>(arrivals_remote), blocks,
+                   cur_stream());
+  });
+  m.def("k_wait_count", [](uint64_t counter, uint64_t target, uint64_t timeout_ns, int rank) {
+    ops::wait_count(P<const uint64_t>(counter), target, timeout_ns, rank, cur_stream());
+  });
+  m.def("k_saxpy", [](uint64_t x, uint64_t y, float a, size_t n) {
+    ops::saxpy(P<const float>(x), P<float>(y), a, n, cur_stream());
+  });
   m.def("k_moe_route", [](uint64_t logits, int T, int E, int topk, uint64_t idx, uint64_t w, uint64_t counts) {
     ops::moe_route(P<const float>(logits), T, E, topk, P<int>(idx), P<float>(w), P<int>(counts), cur_stream());
   });

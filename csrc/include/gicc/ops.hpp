@@ -141,6 +141,18 @@ struct LitmusArgs {
   LitmusRole role[2];
 };
 GICC_EXPORT void litmus(const LitmusArgs& a, int nroles_here, cudaStream_t s);
+// Measurement kernels of the reference's example programs (csrc/kernels/examples.cu).
+// phase_loop: one block; stamps = [iters][6] %globaltimer values; bar is advanced by
+// 3 * iters epochs (the caller tells the host Barrier with advance()).
+GICC_EXPORT void phase_loop(BarrierCtx* bar, float* x, float* y, const float* recv, float* send_remote, size_t n,
+                            int iters, float a, int rank, int left, uint64_t* stamps, unsigned long long* bad,
+                            cudaStream_t s);
+// y = a*x + y and the result stored into dst_remote, per CTA; each CTA adds 1 to
+// *arrivals_remote when its chunk is visible.
+GICC_EXPORT void saxpy_put(const float* x, float* y, float a, size_t n, float* dst_remote, uint64_t* arrivals_remote,
+                           int blocks, cudaStream_t s);
+GICC_EXPORT void wait_count(const uint64_t* counter, uint64_t target, uint64_t timeout_ns, int rank, cudaStream_t s);
+GICC_EXPORT void saxpy(const float* x, float* y, float a, size_t n, cudaStream_t s);
 GICC_EXPORT void ag_gemm(const AgGemmArgs& a, cudaStream_t s);
 GICC_EXPORT void gemm_rs(const GemmRsArgs& a, cudaStream_t s);
 
