@@ -2,6 +2,7 @@
 a few launches, a few GB on the device at most.
 
     python bench/profile_kernels.py gemm 8192          # k_gemm_bf16, 4 launches
+    python bench/profile_kernels.py gemm_pair 8192     # k_gemm_bf16_pair (CTA pairs), 4 launches
     python bench/profile_kernels.py jacobi 8192 8192   # k_jacobi, 4 launches
     python bench/profile_kernels.py moe 1024           # MoE layer (n=1), 2 forwards
     python bench/profile_kernels.py copy 268435456     # k_copy (local HBM copy)
@@ -27,13 +28,16 @@ def main():
     from opengda_b200 import native
     from opengda_b200.ops.gemm import check_errors, gemm
     torch.manual_seed(0)
-    if case == "gemm":
+    if case in ("gemm", "gemm_pair"):
         M = N = K = args[0] if args else 8192
         A = torch.randn(M, K, device="cuda").to(torch.bfloat16)
         B = torch.randn(N, K, device="cuda").to(torch.bfloat16)
         C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
         for _ in range(4):
-            gemm(A, B, out=C)
+            if case == "gemm":
+                gemm(A, B, out=C)
+            else:
+                native().gemm(A, B, out=C, bn=512)
     elif case == "jacobi":
         from opengda_b200.models.jacobi import Jacobi
         nx = args[0] if args else 8192
