@@ -378,6 +378,9 @@ void bind_runtime_objects(py::module_& m) {
     return out;
   });
   m.def("k_fill_pattern", [](uint64_t buf, size_t n, uint32_t seed) { ops::fill_pattern(P<void>(buf), n, seed, cur_stream()); });
+  m.def("k_check_pattern_range", [](uint64_t buf, size_t n, uint32_t seed, size_t base, uint64_t bad) {
+    ops::check_pattern(P<const void>(buf), n, seed, P<unsigned long long>(bad), cur_stream(), base);
+  });
   m.def("k_check_pattern", [](uint64_t buf, size_t n, uint32_t seed, uint64_t bad) {
     ops::check_pattern(P<const void>(buf), n, seed, P<unsigned long long>(bad), cur_stream());
   });

@@ -40,7 +40,9 @@ GICC_EXPORT void flush_queued(DeviceCtx* ctx, int* status, cudaStream_t s);
 GICC_EXPORT void ctx_put(DeviceCtx* ctx, uint64_t laddr, uint32_t lkey, uint64_t raddr, uint32_t rkey, uint32_t size,
                          cudaStream_t s);
 GICC_EXPORT void fill_pattern(void* buf, size_t n, uint32_t seed, cudaStream_t s);
-GICC_EXPORT void check_pattern(const void* buf, size_t n, uint32_t seed, unsigned long long* bad, cudaStream_t s);
+// Counts bytes of buf[0, n) that differ from the fill_pattern(seed) bytes at [base, base + n).
+GICC_EXPORT void check_pattern(const void* buf, size_t n, uint32_t seed, unsigned long long* bad, cudaStream_t s,
+                               size_t base = 0);
 
 // ---- collectives (collectives.cu) ---------------------------------------------------------
 enum AllreduceAlgo : int { ALLREDUCE_ONESHOT = 0, ALLREDUCE_TWOSHOT = 1, ALLREDUCE_NVLS = 2 };

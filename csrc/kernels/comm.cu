@@ -170,11 +170,12 @@ __global__ void k_fill(uint8_t* buf, size_t n, uint32_t seed) {
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
     buf[i] = (uint8_t)((seed * 2654435761u + (uint32_t)i * 40503u + (uint32_t)(i >> 16)) >> 13);
 }
-__global__ void k_check(const uint8_t* buf, size_t n, uint32_t seed, unsigned long long* bad) {
+__global__ void k_check(const uint8_t* buf, size_t n, uint32_t seed, size_t base, unsigned long long* bad) {
   unsigned long long local = 0;
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+  for (size_t j = (size_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (size_t)gridDim.x * blockDim.x) {
+    const size_t i = base + j;  // index in the filled buffer
     const uint8_t e = (uint8_t)((seed * 2654435761u + (uint32_t)i * 40503u + (uint32_t)(i >> 16)) >> 13);
-    local += buf[i] != e;
+    local += buf[j] != e;
   }
   if (local) atomicAdd(bad, local);
 }
@@ -253,9 +254,9 @@ void fill_pattern(void* buf, size_t n, uint32_t seed, cudaStream_t s) {
   k_fill<<<2 * num_sms(), 256, 0, s>>>(static_cast<uint8_t*>(buf), n, seed);
   GICC_CUDA(cudaGetLastError());
 }
-void check_pattern(const void* buf, size_t n, uint32_t seed, unsigned long long* bad, cudaStream_t s) {
+void check_pattern(const void* buf, size_t n, uint32_t seed, unsigned long long* bad, cudaStream_t s, size_t base) {
   if (!n) return;
-  k_check<<<2 * num_sms(), 256, 0, s>>>(static_cast<const uint8_t*>(buf), n, seed, bad);
+  k_check<<<2 * num_sms(), 256, 0, s>>>(static_cast<const uint8_t*>(buf), n, seed, base, bad);
   GICC_CUDA(cudaGetLastError());
 }
 
