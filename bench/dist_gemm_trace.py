@@ -1,7 +1,10 @@
-"""Timeline of the fused all-gather -> GEMM kernel (BASELINE config 3a) on N GPUs.
+"""Timeline of the fused distributed GEMM kernels on N GPUs.
 
-    torchrun --nproc-per-node N bench/dist_gemm_trace.py [--size 16384] [--comm-ctas 16]
-             [--no-nvls] [--units 4] [--steps 40] [--out DIR]
+    torchrun --nproc-per-node N bench/dist_gemm_trace.py [--mode ag|rs] [--size 16384]
+             [--comm-ctas C] [--no-nvls] [--units 4] [--steps 40] [--out DIR]
+
+--mode rs traces the NVLS reduce-scatter kernel (last tile stored, reduce start / end,
+reduction lag behind each band, owner-side reduce rate); the rest below is for --mode ag.
 
 Times the fused kernel (device time, max over ranks), then runs one more call with the
 kernel's %globaltimer trace buffer switched on and summarises, per rank:
@@ -56,6 +59,41 @@ def summarize(t, n, M, nvls, Q, G):
     }
 
 
+def summarize_rs(t, n, M, Q, G):
+    """NVLS reduce-scatter trace: [T] tile stored, [2U] reduce unit start/end, [2G] CTA."""
+    import numpy as np
+
+    t = t.astype(np.int64)
+    nbo = M // n // 128
+    num_n = M // 256
+    T = n * nbo * num_n
+    U = nbo * Q
+    epi = t[:T]
+    units = t[T:T + 2 * U].reshape(U, 2)
+    cta = t[T + 2 * U:T + 2 * U + 2 * G].reshape(G, 2)
+    t0 = cta[:, 0].min()
+    us = lambda x: (x - t0) / 1e3  # noqa: E731
+    span = float(us(cta[:, 1].max()))
+    gemm_end = float(us(epi.max()))
+    # per band b: when its last tile (any owner) was stored vs when its reduction ended
+    mb = np.arange(T) // num_n                       # global m-block of tile t
+    band_of = mb % nbo                               # band within the owner's block
+    band_done = np.array([us(epi[band_of == b].max()) for b in range(nbo)])
+    red_end = np.array([us(units[b * Q:(b + 1) * Q, 1].max()) for b in range(nbo)])
+    red_start = np.array([us(units[b * Q:(b + 1) * Q, 0].min()) for b in range(nbo)])
+    out_bytes = (M // n) * M * 2
+    return {
+        "span_us": round(span, 1),
+        "last_tile_stored_us": round(gemm_end, 1),
+        "reduce_after_gemm_us": round(span - gemm_end, 1),
+        "reduce_first_start_us": round(float(red_start.min()), 1),
+        "reduce_last_end_us": round(float(red_end.max()), 1),
+        "reduce_lag_mean_us": round(float((red_end - band_done).mean()), 1),
+        "owner_GBps_while_reducing": round(out_bytes / ((red_end.max() - red_start.min()) * 1e-6) / 1e9, 1),
+        "tiles_per_ms": round(T / max(gemm_end, 1e-3) * 1e3, 1),
+    }
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--size", type=int, default=16384)
@@ -65,6 +103,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--out", default=None)
+    ap.add_argument("--mode", default="ag", choices=["ag", "rs"], help="rs: the NVLS reduce-scatter kernel")
     args = ap.parse_args()
 
     import numpy as np
@@ -81,38 +120,51 @@ def main() -> int:
 
     rt = Runtime()
     M = N = K = args.size
-    A, B, (Af, Bf) = make_operands(M, N, K, "ag", world, rank, seed=2, device=dev)
-    rows = torch.arange(0, M, 61, device=dev)
-    ref = Af[rows].float() @ B.float().t()
+    A, B, (Af, Bf) = make_operands(M, N, K, args.mode, world, rank, seed=2, device=dev)
+    rows = torch.arange(0, M // world if args.mode == "rs" else M, 61, device=dev)
+    if args.mode == "ag":
+        ref = Af[rows].float() @ B.float().t()
+    else:
+        ref = Af[rank * (M // world) + rows].float() @ Bf.float().t()
     del Af, Bf
-    m = DistGemm(M, N, K, "ag", rt=rt, device=dev, nvls=False if args.no_nvls else None)
+    m = DistGemm(M, N, K, args.mode, rt=rt, device=dev, nvls=False if args.no_nvls else None)
+    if args.mode == "rs" and not m.nvls:
+        raise SystemExit("the trace covers the NVLS reduce-scatter kernel only")
     m.units_per_band = args.units
     if args.comm_ctas:
-        m.comm_ctas = args.comm_ctas
-    m.a_slot(0).copy_(A)
-    m.a_slot(1).copy_(A)
+        if args.mode == "ag":
+            m.comm_ctas = args.comm_ctas
+        else:
+            m.rs_reduce_ctas = args.comm_ctas
+    if args.mode == "ag":
+        m.a_slot(0).copy_(A)
+        m.a_slot(1).copy_(A)
+    step = (lambda: m(m.a_slot(), B)) if args.mode == "ag" else (lambda: m(A, B))
     for _ in range(args.warmup):
-        m(m.a_slot(), B)
+        step()
     torch.cuda.synchronize()
     dist.barrier()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for _ in range(args.steps):
-        m(m.a_slot(), B)
+        step()
     e.record()
     torch.cuda.synchronize()
     ms = max_over_ranks(s.elapsed_time(e) / args.steps)
-    C = m(m.a_slot(), B)
+    C = step()
     torch.cuda.synchronize()
     rel = ((C[rows].float() - ref).norm() / ref.norm()).item()
     m.trace = torch.zeros(m.trace_words(), dtype=torch.int64, device=dev)
-    m(m.a_slot(), B)
+    step()
     torch.cuda.synchronize()
     rt.check_device_errors()
     tr = m.trace.cpu().numpy()
     m.trace = None
     G = m.grid or torch.cuda.get_device_properties(dev).multi_processor_count
-    summ = summarize(tr, world, M, m.nvls, m.units_per_band, G)
+    if args.mode == "ag":
+        summ = summarize(tr, world, M, m.nvls, m.units_per_band, G)
+    else:
+        summ = summarize_rs(tr, world, M, m.units_per_band, G)
     if args.out:
         os.makedirs(args.out, exist_ok=True)
         np.save(os.path.join(args.out, f"ag_trace_r{rank}.npy"), tr)
@@ -120,8 +172,9 @@ def main() -> int:
     dist.all_gather_object(allsum, summ)
     if rank == 0:
         print(json.dumps({
-            "kernel": "k_ag_gemm", "n_gpus": world, "M": M, "N": N, "K": K, "nvls": m.nvls,
-            "comm_ctas": m.comm_ctas, "units_per_band": m.units_per_band,
+            "kernel": "k_ag_gemm" if args.mode == "ag" else "k_gemm_rs_nvls", "n_gpus": world, "M": M, "N": N,
+            "K": K, "nvls": m.nvls, "comm_ctas": m.comm_ctas if args.mode == "ag" else m.rs_reduce_ctas,
+            "units_per_band": m.units_per_band,
             "ms_per_call_max_over_ranks": round(ms, 4), "tflops": round(2.0 * M * N * K / ms / 1e9, 1),
             "relerr_vs_fp32": rel, "per_rank_trace": allsum}))
     del m

@@ -121,6 +121,7 @@ struct GemmRsArgs {
   uint64_t* tile_counter = nullptr;
   int comm_ctas = 0;           // CTAs running the reduce warps (0 = 16)
   int units_per_band = 4;      // row slices per 128-row band (divides 128)
+  uint64_t* trace = nullptr;   // NVLS mode diagnostics: %globaltimer stamps (layout at RsNvSched)
 };
 // Memory-model litmus tests (gicc/proto/litmus.hpp).  test 0 = MP (role 0 writes data and
 // flag into role 1's memory; role 1 checks), test 1 = SB (each role stores into the other's

@@ -490,8 +490,12 @@ struct RsNvSched {
   uint64_t epoch;
   unsigned long long* tile_counter;
   unsigned long long tile_base;
+  // Diagnostics: %globaltimer stamps or null.  Layout (uint64), T = tiles (m-block major),
+  // U = nbo * Q reduce units: [T] tile stored, [2U] unit start / end, [2G] CTA start / end.
+  uint64_t* trace;
 
   __device__ int num_tiles() const { return n * nbo * num_n; }
+  __device__ int num_units() const { return nbo * Q; }
   __device__ int next_tile() const {
     const unsigned long long v = atomicAdd(tile_counter, 1ull) - tile_base;
     return v < (unsigned long long)num_tiles() ? (int)v : num_tiles();
@@ -561,6 +565,8 @@ struct RsNvSched {
       }
       asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
       if (comm_stop) break;
+      uint64_t* tr = trace ? trace + (size_t)num_tiles() + 2 * (size_t)u : nullptr;
+      if (tr && tid == 0) tr[0] = ptx::globaltimer();
       const int lrow0 = b * BM + q * rows;  // first row within my block
       const uint4* src = reinterpret_cast<const uint4*>(staging_mc + ((size_t)r * Mr + lrow0) * N);
       size_t i = tid;
@@ -580,6 +586,7 @@ struct RsNvSched {
         ptx::st_v4(out + (size_t)(lrow0 + rr) * ldo + (size_t)cc * 8, ptx::multimem_ld_reduce_bf16x8(src + i));
       }
       asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
+      if (tr && tid == 0) tr[1] = ptx::globaltimer();
     }
   }
 };
@@ -592,9 +599,12 @@ struct RsNvEpi {
   unsigned long long* band_tiles;      // mine [n][nbo]: tiles of band (o, b) finished here (monotonic)
   uint64_t* arrivals_peer[kMaxR];      // owner o's [nbo] counters, mapped here
   uint64_t epoch;
+  uint64_t* trace_epi;                 // diagnostics: [tile] stamp when stored, or null
   __device__ static void fence_before_done() { ptx::fence_acq_rel_sys(); }
   __device__ void begin_tile(const TileInfo&, int) {}
-  __device__ void end_tile(const TileInfo&, int) {}
+  __device__ void end_tile(const TileInfo& ti, int row) {
+    if (trace_epi && row == 0) trace_epi[(ti.m0 / BM) * num_n + ti.n0 / 256] = ptx::globaltimer();
+  }
   __device__ __forceinline__ void store(const TileInfo& ti, int row, int c, const uint32_t* acc) {
     uint16_t* p = staging + (size_t)(ti.m0 + row) * N + ti.n0 + c;
 #pragma unroll
@@ -620,8 +630,11 @@ __global__ void __launch_bounds__(cta_threads(kCommWarpsAG), 1)
     k_gemm_rs_nvls(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, RsNvSched sched,
                    RsNvEpi epi, DoneTable done_peer, ErrorRecord* err, uint64_t timeout_ns) {
   if (threadIdx.x == 0) *sched.checked_flag() = 0;  // ordered by the core's set-up barrier
+  uint64_t* tr = sched.trace ? sched.trace + (size_t)sched.num_tiles() + 2 * (size_t)sched.num_units() : nullptr;
+  if (tr && threadIdx.x == 0) tr[2 * blockIdx.x] = ptx::globaltimer();
   gemm_core<BN>(&tmA, &tmB, sched, epi, err, timeout_ns, sched.r);
   signal_cta_done(done_peer.p, sched.n, sched.r);
+  if (tr && threadIdx.x == 0) tr[2 * blockIdx.x + 1] = ptx::globaltimer();
 }
 
 }  // namespace
@@ -720,7 +733,9 @@ void gemm_rs(const GemmRsArgs& a, cudaStream_t s) {
     sc.epoch = a.epoch;
     sc.tile_counter = reinterpret_cast<unsigned long long*>(a.tile_counter);
     sc.tile_base = (unsigned long long)(a.epoch - 1) * (unsigned long long)(a.n * sc.nbo * sc.num_n + G);
+    sc.trace = a.trace;
     RsNvEpi e{};
+    e.trace_epi = a.trace;  // first T words
     e.N = a.N; e.nbo = sc.nbo; e.num_n = sc.num_n;
     e.staging = static_cast<uint16_t*>(a.slots[a.r]);
     e.band_tiles = reinterpret_cast<unsigned long long*>(a.band_tiles);

@@ -110,12 +110,16 @@ class DistGemm:
         return (self.M, self.N // w) if self.mode == "ag" else (self.M // w, self.N)
 
     def trace_words(self) -> int:
-        """Size (uint64 words) of the fused AG trace buffer for the current settings."""
+        """Size (uint64 words) of the fused kernel's trace buffer for the current settings
+        (AG: unicast or NVLS; RS: NVLS only)."""
         w = self.world
         nb = (self.M // w) // 128
+        grid = self.grid or torch.cuda.get_device_properties(self.device).multi_processor_count
+        if self.mode == "rs":
+            tiles = w * nb * (self.N // 256)
+            return tiles + 2 * nb * self.units_per_band + 2 * grid
         tiles = w * nb * ((self.N // w) // 256)
         units = 0 if self.diag & 1 else (1 if self.nvls else w - 1) * nb * self.units_per_band
-        grid = self.grid or torch.cuda.get_device_properties(self.device).multi_processor_count
         return 3 * tiles + 2 * units + 2 * grid
 
     def a_slot(self, parity: Optional[int] = None) -> torch.Tensor:
@@ -154,7 +158,8 @@ class DistGemm:
                     n.k_gemm_rs(w, r, self.M, self.N, self.K // w, A.data_ptr(), A.stride(0), B.data_ptr(),
                                 B.stride(0), [buf.ptr(q) for q in range(w)], self.arrivals, self.done, C.data_ptr(),
                                 C.stride(0), self.epoch, self.grid, self.rt.timeout_ns, buf.mc_ptr, self.band_tiles,
-                                self.tile_counter, self.rs_reduce_ctas, self.units_per_band)
+                                self.tile_counter, self.rs_reduce_ctas, self.units_per_band,
+                                self.trace.data_ptr() if self.trace is not None else 0)
                 else:
                     n.k_gemm_rs(w, r, self.M, self.N, self.K // w, A.data_ptr(), A.stride(0), B.data_ptr(),
                                 B.stride(0), [buf.ptr(q) for q in range(w)], self.arrivals, self.done, C.data_ptr(),
