@@ -55,3 +55,18 @@ def test_gda_api_example_all_gpus():
     p = _launch(n, "gda_api_example")
     assert p.returncode == 0, p.stdout + p.stderr
     assert p.stdout.count("PASS") == n
+
+
+def test_gicc_api_example_single_rank():
+    p = _launch(1, "gicc_api_example")
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert "rank 0 of 1: PASS" in p.stdout
+
+
+@pytest.mark.multigpu
+def test_gicc_api_example_all_gpus():
+    import torch
+    n = min(torch.cuda.device_count(), 8)
+    p = _launch(n, "gicc_api_example")
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert p.stdout.count("PASS") == n
