@@ -52,3 +52,16 @@ def test_barrier_timeout(tmp_path):
     rc, res = _run(2, "timeout", tmp_path, env={"GICC_BOOTSTRAP_TIMEOUT_MS": "1000"})
     assert res[0] is not None and res[0].startswith("err:") and "timed out" in res[0], res
     assert float(res[0].rsplit(":", 1)[1]) < 3.0, res
+
+
+def test_native_host_collectives_cpu():
+    """gicc::coll::allreduce_sum/min/max, allgather, broadcast and sendrecv from C++
+    (opengda_b200/bin/gicc_coll_test), 3 CPU ranks through the local launcher."""
+    import subprocess
+    from opengda_b200.parallel.launch import free_port
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    p = subprocess.run([sys.executable, "-m", "opengda_b200.parallel.launch", "-n", "3", "--port", str(free_port()),
+                        "--timeout", "60", os.path.join(root, "opengda_b200", "bin", "gicc_coll_test")],
+                       cwd=root, capture_output=True, text=True, timeout=120)
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert p.stdout.count("PASS") == 3
