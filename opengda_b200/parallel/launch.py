@@ -3,7 +3,9 @@
 Forks N ranks on this host with GICC_RANK / GICC_SIZE / GICC_LOCAL_RANK / GICC_LOCAL_SIZE
 and GICC_BOOTSTRAP_ADDR set (the reference relies on ``srun``/``mpirun``,
 scripts/LC/run.sh:45-50).  If one rank exits non-zero the launcher terminates the rest
-(their process groups) and returns that rank's exit code.
+(their process groups; SIGKILL after `grace` seconds if one ignores SIGTERM) and returns
+that rank's exit code.  With `timeout`, every rank still running after that many seconds is
+killed and the launcher returns 124.
 """
 from __future__ import annotations
 
@@ -25,8 +27,16 @@ def free_port(host: str = "127.0.0.1") -> int:
     return port
 
 
+def _kill_groups(procs, ranks, sig) -> None:
+    for q in ranks:
+        try:
+            os.killpg(procs[q].pid, sig)
+        except ProcessLookupError:
+            pass
+
+
 def launch(n: int, cmd: List[str], host: str = "127.0.0.1", port: Optional[int] = None,
-           timeout: Optional[float] = None, extra_env: Optional[dict] = None) -> int:
+           timeout: Optional[float] = None, extra_env: Optional[dict] = None, grace: float = 10.0) -> int:
     port = port or free_port(host)
     procs = []
     for r in range(n):
@@ -40,6 +50,7 @@ def launch(n: int, cmd: List[str], host: str = "127.0.0.1", port: Optional[int] 
         procs.append(subprocess.Popen(cmd, env=env, start_new_session=True))
     t0 = time.time()
     rc = 0
+    term_at = None  # when the surviving ranks were sent SIGTERM
     alive = set(range(n))
     try:
         while alive:
@@ -50,25 +61,19 @@ def launch(n: int, cmd: List[str], host: str = "127.0.0.1", port: Optional[int] 
                 alive.discard(r)
                 if c != 0 and rc == 0:
                     rc = c
-                    for q in alive:
-                        try:
-                            os.killpg(procs[q].pid, signal.SIGTERM)
-                        except ProcessLookupError:
-                            pass
+                    _kill_groups(procs, alive, signal.SIGTERM)
+                    term_at = time.time()
+            if alive and term_at is not None and time.time() - term_at > grace:
+                _kill_groups(procs, alive, signal.SIGKILL)
+                term_at = float("inf")  # sent once
             if timeout is not None and time.time() - t0 > timeout:
+                _kill_groups(procs, alive, signal.SIGKILL)
                 for q in alive:
-                    try:
-                        os.killpg(procs[q].pid, signal.SIGKILL)
-                    except ProcessLookupError:
-                        pass
+                    procs[q].wait()
                 return 124
             time.sleep(0.02)
     except KeyboardInterrupt:
-        for p in procs:
-            try:
-                os.killpg(p.pid, signal.SIGTERM)
-            except ProcessLookupError:
-                pass
+        _kill_groups(procs, range(n), signal.SIGTERM)
         raise
     return rc
 
