@@ -109,6 +109,20 @@ class DistGemm:
         w = self.world
         return (self.M, self.N // w) if self.mode == "ag" else (self.M // w, self.N)
 
+    def _check_frozen_settings(self) -> None:
+        """The counters of a fused instance advance by amounts that depend on the grid, the
+        units per band and the diag bits (tile counter: tiles + grid per call; arrival
+        counters: units per band per call, none with diag bit 0).  They are fixed by the first
+        call; changing them later would desynchronise the counters, so it is refused.
+        comm_ctas, rs_reduce_ctas and trace may change freely."""
+        now = (self.grid, self.units_per_band, self.diag)
+        first = getattr(self, "_frozen", None)
+        if first is None:
+            self._frozen = now
+        elif first != now:
+            raise ValueError(f"DistGemm: grid / units_per_band / diag were {first} at the first call and are {now} "
+                             "now; create a new DistGemm to change them")
+
     def trace_words(self) -> int:
         """Size (uint64 words) of the fused kernel's trace buffer for the current settings
         (AG: unicast or NVLS; RS: NVLS only)."""
@@ -138,6 +152,7 @@ class DistGemm:
         if self.fused:
             from .. import native
 
+            self._check_frozen_settings()
             self.epoch += 1
             p = self.epoch % 2
             C = out if out is not None else self.C

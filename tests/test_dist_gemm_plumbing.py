@@ -116,3 +116,19 @@ def test_fused_dist_gemm_passes_binding_compatible_arguments(monkeypatch, mode, 
         assert (args.get("staging_mc", 0) != 0) == bool(nvls)
         if nvls:
             assert args["band_tiles"] != 0 and args["tile_counter"] != 0
+
+
+def test_counter_settings_are_frozen_after_the_first_call(monkeypatch):
+    real = opengda_b200.native()
+    rec = _Recorder(real)
+    monkeypatch.setattr(opengda_b200, "native", lambda: rec)
+    m = dist_gemm.DistGemm(1024, 1024, 1024, "ag", rt=_FakeRt(2, 0), device=torch.device("cpu"), nvls=True)
+    A = torch.zeros(*m.a_shape(), dtype=torch.bfloat16)
+    B = torch.zeros(*m.b_shape(), dtype=torch.bfloat16)
+    m.a_slot = lambda parity=None: A
+    m(A, B)
+    m.comm_ctas = 24  # free to change
+    m(A, B)
+    m.units_per_band = 8
+    with pytest.raises(ValueError, match="units_per_band"):
+        m(A, B)
