@@ -31,6 +31,7 @@ def main() -> int:
     ap.add_argument("--min-log2", type=int, default=12)
     ap.add_argument("--max-log2", type=int, default=26)
     ap.add_argument("--out", default=None)
+    ap.add_argument("--resume", default=None, help="JSON-lines store: sizes finished by an earlier run are skipped")
     args = ap.parse_args()
 
     import torch
@@ -71,8 +72,14 @@ def main() -> int:
         rt.barrier()
         return max_over_ranks(s.elapsed_time(e) * 1e3 / args.iters)
 
+    from opengda_b200.utils.results import ResultStore
+    store = ResultStore(args.resume) if args.resume else None  # read by every rank before any write
     for lg in range(args.min_log2, args.max_log2 + 1, 2):
         n = (1 << lg) // 4
+        key = f"put_compare:n={world}:bytes={4 * n}:iters={args.iters}"
+        if store is not None and store.done(key):
+            res["sizes"].append(store.get(key))
+            continue
         row = {"bytes": 4 * n}
 
         def gpu_step():
@@ -101,6 +108,8 @@ def main() -> int:
         row["cpu_driven"] = round(timed(cpu_step), 2)
         row["nccl"] = round(timed(nccl_step), 2)
         res["sizes"].append(row)
+        if store is not None and rank == 0:
+            store.add(key, row)
     rt.check_device_errors()
     if rank == 0:
         print(json.dumps(res))

@@ -29,6 +29,7 @@ def main() -> int:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--best", type=int, default=10)
     ap.add_argument("--out", default=None)
+    ap.add_argument("--resume", default=None, help="JSON-lines store: sizes finished by an earlier run are skipped")
     args = ap.parse_args()
 
     import torch
@@ -55,9 +56,15 @@ def main() -> int:
     right, left = (rank + 1) % world, (rank - 1) % world
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     bad = torch.zeros(1, dtype=torch.int64, device="cuda")
+    from opengda_b200.utils.results import ResultStore
+    store = ResultStore(args.resume) if args.resume else None  # read by every rank before any write
     rows, total_bad = [], 0
     for lg in range(0, args.max_log2 + 1, 2):
         size = 1 << lg
+        key = f"put_streams:n={world}:streams={S}:bytes={size}:iters={args.iters}"
+        if store is not None and store.done(key):
+            rows.append(store.get(key))
+            continue
         times = []
         for it in range(args.iters):
             seed = 1000 * lg + it + 7 * rank
@@ -88,6 +95,8 @@ def main() -> int:
         ms = max_over_ranks(sum(best) / len(best))
         rows.append({"bytes": size, "streams": S, "us": round(ms * 1e3, 3),
                      "GBps": round(S * size / (ms * 1e-3) / 1e9, 3)})
+        if store is not None and rank == 0:
+            store.add(key, rows[-1])
     assert int(status.item()) == 0, "flush reported an error"
     if rank == 0:
         out = {"n_gpus": world, "iters": args.iters, "best_of": args.best, "bad_bytes": total_bad, "sizes": rows}
