@@ -1,6 +1,6 @@
-"""Communication microbenchmarks on 2..8 GPUs of one node, ours vs NCCL.
+"""Communication microbenchmarks (put/get/ping-pong/barrier/allreduce configuration) on 2..8 GPUs of one node, ours vs NCCL.
 
-    torchrun --nproc-per-node N bench/comm_bench.py [--quick] [--out gpurun_out/comm_n{N}.json]
+    torchrun --nproc-per-node N bench/comm_bench.py [--quick] [--out results/comm_n{N}.json]
 
 * put / get bandwidth, 8 B .. 256 MiB (powers of 2), byte buffers filled from seed 1:
   every rank puts to (or gets from) its right neighbour at the same time; per-GPU GB/s.

@@ -1,4 +1,4 @@
-"""Jacobi benchmark (BASELINE config 4): 5-point fp32 stencil on a 32768 x 32768 grid,
+"""Jacobi benchmark: 5-point fp32 stencil on a 32768 x 32768 grid,
 1-D row decomposition over 1..8 GPUs, 1000 iterations, ours (halo puts fused into the
 stencil kernel) vs an NCCL arm (same stencil kernel, halos exchanged with NCCL send/recv
 between launches -- the host-driven pattern of the reference's MPI build).

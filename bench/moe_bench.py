@@ -1,4 +1,4 @@
-"""MoE expert-parallel layer benchmark (BASELINE config 5): 4096 tokens per GPU, hidden
+"""MoE expert-parallel layer benchmark: 4096 tokens per GPU, hidden
 7168, 256 experts (E/n per GPU), top-8 softmax routing (router logits N(0,1), seed 4),
 SwiGLU experts with intermediate 2048, weights N(0, 0.02).
 

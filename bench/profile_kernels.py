@@ -9,7 +9,7 @@ a few launches, a few GB on the device at most.
 
 Example capture (after the same command has exited 0 without ncu):
     ncu --set full --clock-control none -k regex:k_gemm_bf16 -s 2 -c 1 \
-        -o gpurun_out/gemm8k python bench/profile_kernels.py gemm 8192
+        -o prof/gemm8k python bench/profile_kernels.py gemm 8192
 """
 from __future__ import annotations
 

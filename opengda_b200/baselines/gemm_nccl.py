@@ -1,4 +1,4 @@
-"""NCCL + cuBLAS distributed GEMM: the comparison arm for BASELINE config 3.
+"""NCCL + cuBLAS distributed GEMM: the comparison arm for the 16384^3 distributed GEMM.
 
 * ``ag``: ``all_gather_into_tensor`` of the A row shards, then ``torch.matmul`` (cuBLAS)
   with the local column shard of B -- the unfused all-gather -> GEMM.

@@ -1,4 +1,4 @@
-"""NCCL + PyTorch MoE layer: the comparison arm for BASELINE config 5.
+"""NCCL + PyTorch MoE layer: the comparison arm for the MoE layer.
 
 Routing with torch softmax/top-k, dispatch with ``all_to_all_single`` (variable splits),
 one cuBLAS matmul pair per local expert, combine with ``all_to_all_single`` and a

@@ -1,4 +1,4 @@
-"""distributed dense matmul on CPU ranks (plumbing, no GPU).
+"""Distributed dense matmul on CPU ranks (the plumbing configuration, no GPU).
 
 C = A . B in fp32 with M = N = K = 1024; A and B i.i.d. uniform[-1, 1) from seed 0.
 A is row-block partitioned across the ranks, B is broadcast from rank 0, each rank

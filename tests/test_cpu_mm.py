@@ -1,4 +1,4 @@
-"""BASELINE config 1 on CPU gloo ranks: row-block A, broadcast B, gathered C, rtol 1e-5."""
+"""Distributed matmul on CPU gloo ranks (fp32 1024^3): row-block A, broadcast B, gathered C, rtol 1e-5."""
 from opengda_b200.models.cpu_mm import run
 
 

@@ -205,8 +205,9 @@ def main():
     boot.barrier()
     with open(f"{out}.{r}", "w") as f:
         json.dump(res, f)
-    if os.path.isdir(os.path.join(ROOT, "gpurun_out")):
-        with open(os.path.join(ROOT, "gpurun_out", f"multigpu_rank{r}.json"), "w") as f:
+    keep = os.environ.get("GICC_RESULTS_DIR")  # optional copy of every rank's results
+    if keep and os.path.isdir(keep):
+        with open(os.path.join(keep, f"multigpu_rank{r}.json"), "w") as f:
             json.dump(res, f)
     del ar
     rt.finalize()
