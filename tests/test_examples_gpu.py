@@ -52,3 +52,24 @@ def test_saxpy_put_lands_result_and_counts_ctas(rt):
     torch.cuda.synchronize()
     rt.check_device_errors()
     assert torch.allclose(dst.local, ref) and torch.allclose(y, ref)
+
+
+def test_torch_comm_ops_put_get_signal(rt):
+    from opengda_b200.ops import comm
+    x = rt.alloc_tensor((1 << 16,), torch.float32)
+    src = torch.arange(1 << 16, dtype=torch.float32, device="cuda")
+    word = rt.signal_alloc(1)
+    blocks = comm.put_signal(x, src, rt.rank, rt, word)
+    comm.wait_signal(rt, word, blocks)
+    assert torch.equal(x.local, src)
+    back = torch.empty(1000, dtype=torch.float32, device="cuda")
+    comm.get(back, x, rt.rank, offset=4 * 500)
+    assert torch.equal(back, src[500:1500])
+    comm.signal(rt, rt.rank, word, 5, op="add")
+    comm.wait_signal(rt, word, blocks + 5, cmp="eq")
+    with pytest.raises(TimeoutError):
+        comm.wait_signal(rt, word, blocks + 6, timeout_ns=50_000_000)
+    with pytest.raises(ValueError):
+        comm.put(x, torch.zeros(1 << 17, device="cuda"), rt.rank)
+    from opengda_b200 import native
+    native().read_errors(True)  # the deliberate timeout above left a record
