@@ -70,3 +70,18 @@ def test_gicc_api_example_all_gpus():
     p = _launch(n, "gicc_api_example")
     assert p.returncode == 0, p.stdout + p.stderr
     assert p.stdout.count("PASS") == n
+
+
+def test_gicc_jacobi_single_rank():
+    p = _launch(1, "gicc_jacobi", "-nx", 1024, "-ny", 1024, "-niter", 50, "-nccheck", 10)
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert "PASS" in p.stdout
+
+
+@pytest.mark.multigpu
+def test_gicc_jacobi_all_gpus_matches_single_gpu():
+    import torch
+    n = min(torch.cuda.device_count(), 8)
+    p = _launch(n, "gicc_jacobi", "-nx", 2048, "-ny", 2051, "-niter", 100, "-csv")
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert ",PASS" in p.stdout
