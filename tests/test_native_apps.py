@@ -85,3 +85,12 @@ def test_gicc_jacobi_all_gpus_matches_single_gpu():
     p = _launch(n, "gicc_jacobi", "-nx", 2048, "-ny", 2051, "-niter", 100, "-csv")
     assert p.returncode == 0, p.stdout + p.stderr
     assert ",PASS" in p.stdout
+
+
+@pytest.mark.multigpu
+def test_gicc_mm_all_gpus_analytic_check():
+    import torch
+    n = min(torch.cuda.device_count(), 8)
+    p = _launch(n, "gicc_mm", "-n", 4096, "-iters", 5, "-samples", 128)
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert "PASS" in p.stdout
