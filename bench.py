@@ -1,4 +1,4 @@
-"""Headline benchmark: distributed GEMM (BASELINE config 3), all-gather -> GEMM,
+"""Headline benchmark: distributed GEMM, all-gather -> GEMM,
 bf16 in / f32 accumulate, M = N = K = 16384, A row-sharded, B column-sharded,
 on 1..8 GPUs of one node (strong scaling: the problem is fixed, the GPUs grow).
 
@@ -24,7 +24,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "dist-GEMM TFLOPS (all-gather->GEMM, bf16 in / fp32 accumulate, M=N=K=16384)"
-BASELINE_METRIC = "put GB/s & latency vs size; barrier µs; dist-GEMM TFLOPS; MoE dispatch+combine µs @1/2/4/8"
+HEADLINE_METRIC_FAMILY = "put GB/s & latency vs size; barrier µs; dist-GEMM TFLOPS; MoE dispatch+combine µs @1/2/4/8"
 
 
 def reference_unavailable(args) -> None:
@@ -49,6 +49,8 @@ def main() -> int:
     ap.add_argument("--size", type=int, default=16384)
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--unfused", action="store_true", help="decomposed path: copy kernels + GEMM (A/B only)")
+    ap.add_argument("--transfer", default="sm", choices=["sm", "ce"],
+                    help="fused AG: SM pushes (NVLS multicast or unicast) or copy engines (A/B option)")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_unavailable(args)
@@ -84,7 +86,8 @@ def main() -> int:
 
         model = NcclDistGemm(M, N, K, args.mode, device=dev)
     else:
-        model = DistGemm(M, N, K, args.mode, rt=rt, device=dev, fused=not args.unfused)
+        model = DistGemm(M, N, K, args.mode, rt=rt, device=dev, fused=not args.unfused,
+                         transfer=args.transfer if args.mode == "ag" else "sm")
     A, B, (Afull, Bfull) = make_operands(M, N, K, args.mode, world, rank, seed=2, device=dev)
     # numerics spot check (one row block) before timing
     C = model(A, B)
@@ -176,7 +179,7 @@ def main() -> int:
     if rank == 0:
         out = {
             "metric": METRIC,
-            "baseline_metric": BASELINE_METRIC,
+            "baseline_metric": HEADLINE_METRIC_FAMILY,
             "value": round(value, 2),
             "unit": "TFLOP/s",
             "n_gpus": world,
@@ -192,6 +195,9 @@ def main() -> int:
                 "model": f"dist_gemm_{args.mode}", "M": M, "N": N, "K": K,
                 "global_batch": M, "seq_len": K,
                 "parallelism": (f"tp{world}-" + ("allgather-gemm" if args.mode == "ag" else "gemm-reducescatter")),
+                "transfer": ("none" if world == 1 else "nccl" if args.impl == "nccl" else
+                             "unfused-copy-kernels" if args.unfused else
+                             model.transfer + ("-nvls" if model.nvls else "")),
                 "l2": "inputs exceed L2 (A_full 512 MiB > 126 MB), no flush",
                 "numerics_rel_err_vs_fp32": round(rel, 6),
             },

@@ -104,6 +104,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--out", default=None)
     ap.add_argument("--mode", default="ag", choices=["ag", "rs"], help="rs: the NVLS reduce-scatter kernel")
+    ap.add_argument("--transfer", default="sm", choices=["sm", "ce"], help="ag: SM pushes or copy engines")
     args = ap.parse_args()
 
     import numpy as np
@@ -127,7 +128,8 @@ def main() -> int:
     else:
         ref = Af[rank * (M // world) + rows].float() @ Bf.float().t()
     del Af, Bf
-    m = DistGemm(M, N, K, args.mode, rt=rt, device=dev, nvls=False if args.no_nvls else None)
+    m = DistGemm(M, N, K, args.mode, rt=rt, device=dev, nvls=False if args.no_nvls else None,
+                 transfer=args.transfer if args.mode == "ag" else "sm")
     if args.mode == "rs" and not m.nvls:
         raise SystemExit("the trace covers the NVLS reduce-scatter kernel only")
     m.units_per_band = args.units

@@ -97,7 +97,8 @@ struct AgGemmArgs {
                                      // it must use the same shape and grid (dynamic tile order)
   uint64_t timeout_ns = 0;
   uint64_t* trace = nullptr;   // diagnostics: %globaltimer stamps per tile / unit / CTA
-  int diag = 0;                // diagnostics: bit 0 = no transfer (times the math alone)
+  int diag = 0;                // bit 0 = no transfer (diagnostics: times the math alone);
+                               // bit 1 = external transfer (ag_transfer_ce): no pushes, waits kept
 };
 struct GemmRsArgs {
   int n = 0, r = 0, M = 0, N = 0, K = 0;  // K = local K
@@ -156,6 +157,23 @@ GICC_EXPORT void saxpy_put(const float* x, float* y, float a, size_t n, float* d
                            int blocks, cudaStream_t s);
 GICC_EXPORT void wait_count(const uint64_t* counter, uint64_t target, uint64_t timeout_ns, int rank, cudaStream_t s);
 GICC_EXPORT void saxpy(const float* x, float* y, float a, size_t n, cudaStream_t s);
+// Copy-engine transfer for ag_gemm (the A/B alternative to SM pushes): on stream `s`, for
+// each peer d in the consumption order (r-1, r-2, ...): wait (stream memory operation)
+// until d finished the call that last used this parity, copy this rank's shard into d's
+// landing buffer with cudaMemcpyAsync, `chunks` pieces per peer, and after each piece write
+// d's arrival counters of its bands to epoch * units_per_band.  No SM issues NVLink
+// traffic; launch ag_gemm with diag bit 1 (external transfer) on another stream.
+struct AgCeArgs {
+  int n = 0, r = 0, M = 0, K = 0;
+  void* a_full[16] = {};        // each rank's landing buffer (current parity), mapped here
+  uint64_t* arrivals[16] = {};  // each rank's [n][M/n/128] counters, mapped here
+  const uint64_t* done_local = nullptr;  // [n] CTA-exit counts received from each rank
+  uint64_t epoch = 0;
+  int grid = 0;                 // CTAs of the ag_gemm launch (done-counter unit)
+  int units_per_band = 4;
+  int chunks = 4;               // copies per peer (each followed by its bands' counters)
+};
+GICC_EXPORT void ag_transfer_ce(const AgCeArgs& a, cudaStream_t s);
 GICC_EXPORT void ag_gemm(const AgGemmArgs& a, cudaStream_t s);
 GICC_EXPORT void gemm_rs(const GemmRsArgs& a, cudaStream_t s);
 

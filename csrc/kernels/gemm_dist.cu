@@ -29,6 +29,7 @@
 #include "gicc/device/comm.cuh"
 #include "gicc/device/gemm_core.cuh"
 #include "gicc/config.hpp"
+#include "gicc/driver.hpp"
 #include "gicc/host_util.hpp"
 #include "gicc/ops.hpp"
 
@@ -139,7 +140,7 @@ struct AgSched {
   uint64_t* arrivals_mc;
 
   __device__ int num_tiles() const { return n * nb * num_n; }
-  __device__ int num_units() const { return (diag & 1) ? 0 : (a_mc ? nb * Q : (n - 1) * nb * Q); }
+  __device__ int num_units() const { return (diag & 3) ? 0 : (a_mc ? nb * Q : (n - 1) * nb * Q); }
   __device__ int next_tile() const {
     const unsigned long long v = atomicAdd(tile_counter, 1ull) - tile_base;
     return v < (unsigned long long)num_tiles() ? (int)v : num_tiles();
@@ -702,6 +703,34 @@ void ag_gemm(const AgGemmArgs& a, cudaStream_t s) {
   k_ag_gemm<BN_><<<G, cta_threads(kCommWarpsAG), smem, s>>>(tA, tB, sc, e, dt, device_error_record(),
                                                              a.timeout_ns ? a.timeout_ns : default_timeout_ns());
   GICC_CUDA(cudaGetLastError());
+}
+
+void ag_transfer_ce(const AgCeArgs& a, cudaStream_t s) {
+  NvtxRange nvtx("gicc::ops::ag_transfer_ce");
+  using namespace gemm;
+  if (a.n < 2 || a.n > kMaxR || a.M % (a.n * BM)) throw std::runtime_error("gicc::ag_transfer_ce: bad shape");
+  const DriverApi& d = driver();
+  if (!d.StreamWaitValue64 || !d.StreamWriteValue64)
+    throw std::runtime_error("gicc::ag_transfer_ce: stream memory operations unavailable");
+  const int Ms = a.M / a.n, nb = Ms / BM;
+  const int chunks = a.chunks > 0 && a.chunks <= nb ? a.chunks : 1;
+  const size_t row_bytes = (size_t)a.K * 2;
+  const uint64_t target = a.epoch * (uint64_t)(a.units_per_band > 0 ? a.units_per_band : 4);
+  for (int k = 1; k < a.n; ++k) {
+    const int dst = (a.r - k + a.n) % a.n;
+    if (a.epoch > 2)  // dst finished the call that last used this parity (its CTAs' exit counts)
+      GICC_DRV(d.StreamWaitValue64(s, reinterpret_cast<CUdeviceptr>(a.done_local + dst),
+                                   (a.epoch - 2) * (uint64_t)a.grid, CU_STREAM_WAIT_VALUE_GEQ));
+    for (int c = 0; c < chunks; ++c) {
+      const int b0 = nb * c / chunks, b1 = nb * (c + 1) / chunks;
+      const size_t off = ((size_t)a.r * Ms + (size_t)b0 * BM) * row_bytes;
+      GICC_CUDA(cudaMemcpyAsync(static_cast<char*>(a.a_full[dst]) + off, static_cast<const char*>(a.a_full[a.r]) + off,
+                                (size_t)(b1 - b0) * BM * row_bytes, cudaMemcpyDeviceToDevice, s));
+      for (int b = b0; b < b1; ++b)  // default write: ordered after the copy's stores
+        GICC_DRV(d.StreamWriteValue64(s, reinterpret_cast<CUdeviceptr>(a.arrivals[dst] + (size_t)a.r * nb + b), target,
+                                      CU_STREAM_WRITE_VALUE_DEFAULT));
+    }
+  }
 }
 
 void gemm_rs(const GemmRsArgs& a, cudaStream_t s) {

@@ -24,7 +24,7 @@ from ..ops.gemm import gemm
 
 class DistGemm:
     def __init__(self, M: int, N: int, K: int, mode: str = "ag", rt=None, device: Optional[torch.device] = None,
-                 fused: bool = True, nvls: Optional[bool] = None):
+                 fused: bool = True, nvls: Optional[bool] = None, transfer: str = "sm"):
         self.M, self.N, self.K, self.mode = M, N, K, mode
         self.fused = fused
         self.rt = rt
@@ -44,6 +44,15 @@ class DistGemm:
         # and the dynamic tile order gives them fewer tiles).  Tuning and diagnostics:
         # units each 128-row band is pushed in, CTAs (0 = one per SM), a uint64 trace
         # tensor (None = off) and the diag bits.
+        # transfer="ce" (AG only): the copy engines move the shard (ops ag_transfer_ce on a side
+        # stream, arrival counters written by stream memory operations) and no SM pushes.
+        if transfer not in ("sm", "ce") or (transfer == "ce" and mode != "ag"):
+            raise ValueError("transfer must be 'sm', or 'ce' for the ag mode")
+        self.transfer = transfer
+        self.ce_chunks = 4
+        self._side = None
+        if transfer == "ce":
+            nvls = False
         self.nvls = bool(nvls if nvls is not None else (rt is not None and w > 1 and rt.multicast_supported))
         self.units_per_band = 4
         self.grid = 0
@@ -162,11 +171,31 @@ class DistGemm:
                 if A.data_ptr() != slot.data_ptr():
                     slot.copy_(A)
                 buf = self.A_bufs[p]
-                n.k_ag_gemm(w, r, self.M, self.N // w, self.K, [buf.ptr(q) for q in range(w)], B.data_ptr(),
+                ptrs = [buf.ptr(q) for q in range(w)]
+                diag = self.diag
+                done_ev = None
+                if self.transfer == "ce":
+                    diag |= 2  # the kernel waits for arrivals but does not push
+                    cur = torch.cuda.current_stream()
+                    if self._side is None:
+                        self._side = torch.cuda.Stream(device=self.device)
+                    ready = torch.cuda.Event()
+                    ready.record(cur)  # the shard is in the slot
+                    self._side.wait_event(ready)
+                    grid = self.grid or torch.cuda.get_device_properties(self.device).multi_processor_count
+                    with torch.cuda.stream(self._side):
+                        n.ag_transfer_ce(w, r, self.M, self.K, ptrs, self.arrivals, self.done[r], self.epoch, grid,
+                                         self.units_per_band, self.ce_chunks)
+                    done_ev = torch.cuda.Event()
+                    done_ev.record(self._side)
+                n.k_ag_gemm(w, r, self.M, self.N // w, self.K, ptrs, B.data_ptr(),
                             B.stride(0), C.data_ptr(), C.stride(0), self.arrivals, self.done, self.epoch,
                             self.units_per_band, self.grid, self.rt.timeout_ns,
-                            self.trace.data_ptr() if self.trace is not None else 0, self.diag, self.comm_ctas,
+                            self.trace.data_ptr() if self.trace is not None else 0, diag, self.comm_ctas,
                             self.tile_counter, buf.mc_ptr if self.nvls else 0, self.arrivals_mc)
+                if done_ev is not None:
+                    # later work on this stream (e.g. rewriting the shard slot) waits for the outgoing copies
+                    torch.cuda.current_stream().wait_event(done_ev)
             else:
                 buf = self.slot_bufs[p]
                 if self.nvls:
