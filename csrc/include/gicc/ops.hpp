@@ -163,6 +163,9 @@ GICC_EXPORT void saxpy(const float* x, float* y, float a, size_t n, cudaStream_t
 // landing buffer with cudaMemcpyAsync, `chunks` pieces per peer, and after each piece write
 // d's arrival counters of its bands to epoch * units_per_band.  No SM issues NVLink
 // traffic; launch ag_gemm with diag bit 1 (external transfer) on another stream.
+// The peer-progress wait is a stream memory operation and has no time bound: if a peer
+// stops for good, stream `s` waits (the consumer kernels still end with ETIMEDOUT).  The
+// SM-push path keeps every wait bounded and is the default.
 struct AgCeArgs {
   int n = 0, r = 0, M = 0, K = 0;
   void* a_full[16] = {};        // each rank's landing buffer (current parity), mapped here
