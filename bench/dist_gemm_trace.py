@@ -105,6 +105,7 @@ def main() -> int:
     ap.add_argument("--out", default=None)
     ap.add_argument("--mode", default="ag", choices=["ag", "rs"], help="rs: the NVLS reduce-scatter kernel")
     ap.add_argument("--transfer", default="sm", choices=["sm", "ce"], help="ag: SM pushes or copy engines")
+    ap.add_argument("--join", action="store_true", help="rs: CTAs out of GEMM tiles join the reduction")
     args = ap.parse_args()
 
     import numpy as np
@@ -133,6 +134,7 @@ def main() -> int:
     if args.mode == "rs" and not m.nvls:
         raise SystemExit("the trace covers the NVLS reduce-scatter kernel only")
     m.units_per_band = args.units
+    m.rs_join = bool(args.join)
     if args.comm_ctas:
         if args.mode == "ag":
             m.comm_ctas = args.comm_ctas

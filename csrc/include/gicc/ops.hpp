@@ -123,6 +123,8 @@ struct GemmRsArgs {
   int comm_ctas = 0;           // CTAs running the reduce warps (0 = 16)
   int units_per_band = 4;      // row slices per 128-row band (divides 128)
   uint64_t* trace = nullptr;   // NVLS mode diagnostics: %globaltimer stamps (layout at RsNvSched)
+  int join_reduce = 0;         // NVLS: CTAs that finished their GEMM tiles join the reduction
+  uint64_t* unit_counter = nullptr;  // NVLS + join_reduce: local word, zero before the first call
 };
 // Memory-model litmus tests (gicc/proto/litmus.hpp).  test 0 = MP (role 0 writes data and
 // flag into role 1's memory; role 1 checks), test 1 = SB (each role stores into the other's

@@ -494,12 +494,26 @@ struct RsNvSched {
   // Diagnostics: %globaltimer stamps or null.  Layout (uint64), T = tiles (m-block major),
   // U = nbo * Q reduce units: [T] tile stored, [2U] unit start / end, [2G] CTA start / end.
   uint64_t* trace;
+  // join != 0: reduce units are handed out by a global counter (base (epoch-1) * (U + grid):
+  // every CTA takes one index past the end) and a CTA whose producer has taken its last
+  // GEMM tile joins the reduction, so the bands that finish last are reduced by many SMs.
+  int join;
+  unsigned long long* unit_counter;
+  unsigned long long unit_base;
 
   __device__ int num_tiles() const { return n * nbo * num_n; }
   __device__ int num_units() const { return nbo * Q; }
+  __device__ volatile int* gemm_done_flag() const {
+    __shared__ int gemm_done;  // set to 0 at kernel entry; 1 once the producer ran out of tiles
+    return &gemm_done;
+  }
   __device__ int next_tile() const {
     const unsigned long long v = atomicAdd(tile_counter, 1ull) - tile_base;
-    return v < (unsigned long long)num_tiles() ? (int)v : num_tiles();
+    if (v >= (unsigned long long)num_tiles()) {
+      if (join) *gemm_done_flag() = 1;
+      return num_tiles();
+    }
+    return (int)v;
   }
   __device__ TileInfo tile(int t) const {
     int vm, nbk;
@@ -545,27 +559,52 @@ struct RsNvSched {
   // Reduce warps: unit u = b*Q + q covers rows [q*128/Q, (q+1)*128/Q) of my band b.
   __device__ void comm(int cw, int lane, volatile int* abort_flag, ErrorRecord* err, uint64_t timeout_ns) const {
     __shared__ int comm_stop;
+    __shared__ int comm_unit;
     const int tid = cw * 32 + lane;
     constexpr int kT = kCommWarps * 32;
-    if ((int)blockIdx.x >= C) return;
+    if (!join && (int)blockIdx.x >= C) return;
     const int U = nbo * Q;
     const int rows = BM / Q;
     const int vpr = N / 8;  // 16-byte vectors per row
     const size_t nv = (size_t)rows * vpr;
-    for (int u = blockIdx.x; u < U; u += C) {
-      const int b = u / Q, q = u - (u / Q) * Q;
+    if (join && (int)blockIdx.x >= C) {
+      // not a dedicated reducer: join once this CTA's producer has taken its last tile
       if (tid == 0) {
-        int stop = *abort_flag;
-        const uint64_t target = epoch * (uint64_t)n;
-        if (!stop && !wait_counter(arrivals + b, target, timeout_ns, abort_flag)) {
-          if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_RS_FLAG, r, -1, ptx::ld_relaxed_sys(arrivals + b), target);
-          *abort_flag = 1;
-          stop = 1;
+        const uint64_t t0 = ptx::globaltimer();
+        while (!*gemm_done_flag() && !*abort_flag) {
+          __nanosleep(1000);
+          if (ptx::globaltimer() - t0 > timeout_ns) break;  // the producer's own waits report
         }
+      }
+      asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
+    }
+    for (int it = 0;; ++it) {
+      if (tid == 0) {
+        int u;
+        if (join) {
+          const unsigned long long v = atomicAdd(unit_counter, 1ull) - unit_base;
+          u = v < (unsigned long long)U ? (int)v : U;
+        } else {
+          u = (int)blockIdx.x + it * C;
+          if (u > U) u = U;
+        }
+        int stop = *abort_flag || u >= U;
+        if (!stop) {
+          const uint64_t target = epoch * (uint64_t)n;
+          const int b = u / Q;
+          if (!wait_counter(arrivals + b, target, timeout_ns, abort_flag)) {
+            if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_RS_FLAG, r, -1, ptx::ld_relaxed_sys(arrivals + b), target);
+            *abort_flag = 1;
+            stop = 1;
+          }
+        }
+        comm_unit = u;
         comm_stop = stop;
       }
       asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
       if (comm_stop) break;
+      const int u = comm_unit;
+      const int b = u / Q, q = u - (u / Q) * Q;
       uint64_t* tr = trace ? trace + (size_t)num_tiles() + 2 * (size_t)u : nullptr;
       if (tr && tid == 0) tr[0] = ptx::globaltimer();
       const int lrow0 = b * BM + q * rows;  // first row within my block
@@ -630,7 +669,10 @@ template <int BN>
 __global__ void __launch_bounds__(cta_threads(kCommWarpsAG), 1)
     k_gemm_rs_nvls(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, RsNvSched sched,
                    RsNvEpi epi, DoneTable done_peer, ErrorRecord* err, uint64_t timeout_ns) {
-  if (threadIdx.x == 0) *sched.checked_flag() = 0;  // ordered by the core's set-up barrier
+  if (threadIdx.x == 0) {  // ordered by the core's set-up barrier
+    *sched.checked_flag() = 0;
+    *sched.gemm_done_flag() = 0;
+  }
   uint64_t* tr = sched.trace ? sched.trace + (size_t)sched.num_tiles() + 2 * (size_t)sched.num_units() : nullptr;
   if (tr && threadIdx.x == 0) tr[2 * blockIdx.x] = ptx::globaltimer();
   gemm_core<BN>(&tmA, &tmB, sched, epi, err, timeout_ns, sched.r);
@@ -763,6 +805,10 @@ void gemm_rs(const GemmRsArgs& a, cudaStream_t s) {
     sc.tile_counter = reinterpret_cast<unsigned long long*>(a.tile_counter);
     sc.tile_base = (unsigned long long)(a.epoch - 1) * (unsigned long long)(a.n * sc.nbo * sc.num_n + G);
     sc.trace = a.trace;
+    sc.join = a.join_reduce ? 1 : 0;
+    if (sc.join && !a.unit_counter) throw std::runtime_error("gicc::gemm_rs (NVLS): join_reduce needs unit_counter");
+    sc.unit_counter = reinterpret_cast<unsigned long long*>(a.unit_counter);
+    sc.unit_base = (unsigned long long)(a.epoch - 1) * (unsigned long long)(sc.nbo * Q + G);
     RsNvEpi e{};
     e.trace_epi = a.trace;  // first T words
     e.N = a.N; e.nbo = sc.nbo; e.num_n = sc.num_n;

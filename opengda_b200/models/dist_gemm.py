@@ -60,6 +60,7 @@ class DistGemm:
         # more CTAs push there; at 2-4 GPUs 8 keep well ahead of the tensor cores.
         self.comm_ctas = (16 if w >= 8 else 8) if self.nvls else 32
         self.rs_reduce_ctas = 16  # RS over NVLS: CTAs whose reduce warps run multimem.ld_reduce
+        self.rs_join = False      # RS over NVLS: CTAs out of GEMM tiles join the reduction (A/B option)
         self.trace: Optional[torch.Tensor] = None
         self.diag = 0
         if w > 1 and fused:
@@ -88,6 +89,7 @@ class DistGemm:
                 if not self.slot_bufs[0].mc_ptr:
                     raise RuntimeError("DistGemm: NVLS requested but the runtime has no multicast mapping")
                 self.band_tiles = rt.signal_local(rt.signal_alloc(w * nbands))
+                self.unit_counter = rt.signal_local(rt.signal_alloc(1))
             self.C = torch.empty(*self.out_shape(), dtype=torch.bfloat16, device=self.device)
             self.launches_per_step = 1
         elif w > 1:
@@ -121,10 +123,11 @@ class DistGemm:
     def _check_frozen_settings(self) -> None:
         """The counters of a fused instance advance by amounts that depend on the grid, the
         units per band and the diag bits (tile counter: tiles + grid per call; arrival
-        counters: units per band per call, none with diag bit 0).  They are fixed by the first
-        call; changing them later would desynchronise the counters, so it is refused.
+        counters: units per band per call, none with diag bit 0; RS reduce-unit counter: only
+        with rs_join).  They are fixed by the first call; changing them later would
+        desynchronise the counters, so it is refused.
         comm_ctas, rs_reduce_ctas and trace may change freely."""
-        now = (self.grid, self.units_per_band, self.diag)
+        now = (self.grid, self.units_per_band, self.diag, self.rs_join)
         first = getattr(self, "_frozen", None)
         if first is None:
             self._frozen = now
@@ -203,7 +206,8 @@ class DistGemm:
                                 B.stride(0), [buf.ptr(q) for q in range(w)], self.arrivals, self.done, C.data_ptr(),
                                 C.stride(0), self.epoch, self.grid, self.rt.timeout_ns, buf.mc_ptr, self.band_tiles,
                                 self.tile_counter, self.rs_reduce_ctas, self.units_per_band,
-                                self.trace.data_ptr() if self.trace is not None else 0)
+                                self.trace.data_ptr() if self.trace is not None else 0, int(self.rs_join),
+                                self.unit_counter)
                 else:
                     n.k_gemm_rs(w, r, self.M, self.N, self.K // w, A.data_ptr(), A.stride(0), B.data_ptr(),
                                 B.stride(0), [buf.ptr(q) for q in range(w)], self.arrivals, self.done, C.data_ptr(),
