@@ -1,8 +1,8 @@
 // moe.cu -- expert-parallel MoE layer: routing, dispatch all-to-all fused into the first
 // grouped GEMM, SwiGLU in its epilogue, and the gate-weighted combine all-to-all fused into
-// the second grouped GEMM's epilogue.  None of this exists in the reference; it is the
-// survey's config 5 built on the same NVLink primitives (peer stores + release/acquire
-// counters, every wait bounded).
+// the second grouped GEMM's epilogue.  None of this exists in the reference; it is an
+// expert-parallel layer (e.g. 4096 tokens per GPU, hidden 7168, 256 experts, top-8) built on
+// the same NVLink primitives (peer stores + release/acquire counters, every wait bounded).
 //
 // Per call (epoch e), on every rank r of n, with El = E/n local experts:
 //  1. k_route      softmax over the E router logits of each token, top-k, per-expert counts.
