@@ -33,6 +33,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--no-baseline", action="store_true")
     ap.add_argument("--out", default=None)
+    ap.add_argument("--dispatch-ctas", type=int, default=0, help="CTAs that dispatch (0 = all; A/B option)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -48,6 +49,7 @@ def main():
     from opengda_b200.utils.timing import max_over_ranks
 
     layer = MoELayer(args.tokens, args.hidden, args.experts, args.topk, args.inter, rt=rt)
+    layer.dispatch_ctas = args.dispatch_ctas
     x, logits = make_inputs(args.tokens, args.hidden, args.experts, rank, seed=4)
 
     def timeit(fn, steps, warmup):

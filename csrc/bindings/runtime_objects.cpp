@@ -386,6 +386,8 @@ void bind_runtime_objects(py::module_& m) {
     a.ws.cum_pairs = P<uint64_t>(w["cum_pairs"].cast<uint64_t>());
     a.ws.send_pair = P<int>(w["send_pair"].cast<uint64_t>());
     a.ws.send_row = P<int>(w["send_row"].cast<uint64_t>());
+    if (w.contains("g1_tile_ctr")) a.ws.g1_tile_ctr = P<uint64_t>(w["g1_tile_ctr"].cast<uint64_t>());
+    if (d.contains("dispatch_ctas")) a.dispatch_ctas = d["dispatch_ctas"].cast<int>();
     std::vector<float> stage(6, 0.f);
     const bool timed = d.contains("stage_times") && d["stage_times"].cast<bool>();
     if (timed) a.stage_ms = stage.data();

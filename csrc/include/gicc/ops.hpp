@@ -194,6 +194,7 @@ struct MoeWorkspace {          // local device arrays
   uint64_t* cum_pairs = nullptr; // [1], zero-initialised once
   int* send_pair = nullptr;      // [T*topk]
   int* send_row = nullptr;       // [T*topk]
+  uint64_t* g1_tile_ctr = nullptr; // [2], zero-initialised once (needed with dispatch_ctas)
 };
 struct MoeArgs {
   int n = 1, r = 0, T = 0, H = 0, I = 0, E = 0, topk = 8;
@@ -218,6 +219,8 @@ struct MoeArgs {
   uint64_t timeout_ns = 0;
   MoeWorkspace ws;
   float* stage_ms = nullptr;      // optional host [6]: per-stage device time (synchronises)
+  int dispatch_ctas = 0;          // CTAs whose warps dispatch (0 = every CTA); with fewer, the
+                                  // first GEMM takes tiles dynamically (ws.g1_tile_ctr)
 };
 GICC_EXPORT void moe_route(const float* logits, int T, int E, int topk, int* topk_idx, float* topk_w, int* counts,
                            cudaStream_t s);

@@ -25,6 +25,8 @@
 //  6. k_combine    the source waits for all its rows and sums the k weighted rows per token.
 #include <cuda_runtime.h>
 
+#include <cstring>
+
 #include "gicc/device/comm.cuh"
 #include "gicc/device/gemm_core.cuh"
 #include "gicc/config.hpp"
@@ -236,10 +238,22 @@ __global__ void k_sort(const int* topk_idx, int pairs, int n, int r, int El, con
 // ---------------------------------------------------------------------------------------
 // 4. grouped GEMM 1: dispatch (comm warps) + X W1^T + SwiGLU
 // ---------------------------------------------------------------------------------------
-struct G1Sched {
+// Dyn = true: only C CTAs dispatch, and tiles come from a global counter so those CTAs take
+// fewer tiles.  The tile count changes from call to call (it follows the routing), so the
+// counter is one of a pair: call e counts on tile_ctr[e & 1] and zeroes the other one, which
+// call e+1 uses.
+template <bool Dyn>
+struct G1SchedT {
   static constexpr int kCommWarps = moe::kCommWarps;
+  static constexpr bool kDynamic = Dyn;
   int n, r, El, H, I2, num_n;  // H = hidden (K), I2 = 2*inter (N), num_n = I2 / 256
   int topk, G;
+  int C;                       // CTAs that dispatch (G when not Dyn)
+  unsigned long long* tile_ctr;  // Dyn: this call's counter
+  __device__ int next_tile() const {
+    const unsigned long long v = atomicAdd(tile_ctr, 1ull);
+    return v < (unsigned long long)num_tiles() ? (int)v : num_tiles();
+  }
   const int* mblk_prefix;      // [El+1]
   const int* expert_base;      // [El]
   const uint64_t* arrivals;    // my [n][El] row counters
@@ -302,7 +316,7 @@ struct G1Sched {
     ptx::tma_load_2d(sA, tmA, bar, kb * BK, ti.a_row);
     ptx::tma_load_2d(sB, tmB, bar, kb * BK, ti.b_row);
   }
-  // Dispatch: pairs in send order, CTA c takes pairs c, c+G, ...
+  // Dispatch: pairs in send order, dispatching CTA c takes pairs c, c+C, ...
   __device__ void comm(int cw, int lane, volatile int* abort_flag, ErrorRecord*, uint64_t) const {
     __shared__ int comm_stop;
     const int tid = cw * 32 + lane;
@@ -310,16 +324,17 @@ struct G1Sched {
     const int nvec = H / 8;  // 16-byte vectors per row
     constexpr int kBatch = 4;  // rows per fence / barrier
     constexpr int kVec = 8;    // vectors in flight per thread
-    // CTA c owns pairs c, c+G, c+2G, ... (send order, so every owner's first expert
+    if ((int)blockIdx.x >= C) return;
+    // CTA c owns pairs c, c+C, c+2C, ... (send order, so every owner's first expert
     // completes first); kBatch of them share one fence and one barrier.
-    for (int p0 = blockIdx.x; p0 < npairs; p0 += G * kBatch) {
+    for (int p0 = blockIdx.x; p0 < npairs; p0 += C * kBatch) {
       // one thread samples the CTA's abort flag; all comm threads leave together
       if (tid == 0) comm_stop = *abort_flag;
       asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
       if (comm_stop) break;
 #pragma unroll 1
       for (int j = 0; j < kBatch; ++j) {
-        const int p = p0 + j * G;
+        const int p = p0 + j * C;
         if (p >= npairs) break;
         const int pair = send_pair[p];
         const int row = send_row[p];
@@ -352,7 +367,7 @@ struct G1Sched {
       ptx::fence_acq_rel_sys();
       asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
       if (tid < kBatch) {
-        const int p = p0 + tid * G;
+        const int p = p0 + tid * C;
         if (p < npairs) {
           const int g = topk_idx[send_pair[p]];
           ptx::red_release_sys_add(arrivals_peer.p[g / El] + (size_t)r * El + (g - (g / El) * El), 1);
@@ -396,9 +411,11 @@ struct G1Epi {
   }
 };
 
+template <bool Dyn>
 __global__ void __launch_bounds__(cta_threads(kCommWarps), 1)
-    k_moe_gemm1(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, G1Sched s, G1Epi e,
-                ErrorRecord* err, uint64_t timeout_ns) {
+    k_moe_gemm1(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, G1SchedT<Dyn> s,
+                G1Epi e, ErrorRecord* err, uint64_t timeout_ns, unsigned long long* next_ctr) {
+  if (Dyn && blockIdx.x == 0 && threadIdx.x == 0) *next_ctr = 0;  // the next call's counter
   gemm_core<256>(&tmA, &tmB, s, e, err, timeout_ns, s.r);
 }
 
@@ -616,7 +633,9 @@ void moe_forward(const MoeArgs& a, cudaStream_t s) {
                                        CU_TENSOR_MAP_SWIZZLE_128B);
   const CUtensorMap tB1 = make_tmap_2d(a.w1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)El * 2 * a.I, a.H, a.H, 256,
                                        BK, CU_TENSOR_MAP_SWIZZLE_128B);
-  moe::G1Sched g1{};
+  const bool dyn = a.dispatch_ctas > 0 && a.dispatch_ctas < G;
+  if (dyn && !a.ws.g1_tile_ctr) throw std::runtime_error("gicc::moe_forward: dispatch_ctas needs ws.g1_tile_ctr");
+  moe::G1SchedT<false> g1{};
   g1.n = n;
   g1.r = r;
   g1.El = El;
@@ -625,6 +644,10 @@ void moe_forward(const MoeArgs& a, cudaStream_t s) {
   g1.num_n = 2 * a.I / 256;
   g1.topk = a.topk;
   g1.G = G;
+  g1.C = dyn ? a.dispatch_ctas : G;
+  g1.tile_ctr = dyn ? reinterpret_cast<unsigned long long*>(a.ws.g1_tile_ctr) + (a.epoch & 1) : nullptr;
+  unsigned long long* next_ctr =
+      dyn ? reinterpret_cast<unsigned long long*>(a.ws.g1_tile_ctr) + ((a.epoch + 1) & 1) : nullptr;
   g1.mblk_prefix = a.ws.mblk_prefix;
   g1.expert_base = a.ws.expert_base;
   g1.arrivals = a.arrivals[r];
@@ -646,11 +669,19 @@ void moe_forward(const MoeArgs& a, cudaStream_t s) {
   int dev = 0;
   GICC_CUDA(cudaGetDevice(&dev));
   if (!attr[dev]) {
-    GICC_CUDA(cudaFuncSetAttribute(moe::k_moe_gemm1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    GICC_CUDA(cudaFuncSetAttribute(moe::k_moe_gemm1<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    GICC_CUDA(cudaFuncSetAttribute(moe::k_moe_gemm1<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     GICC_CUDA(cudaFuncSetAttribute(moe::k_moe_gemm2, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr[dev] = true;
   }
-  moe::k_moe_gemm1<<<G, cta_threads(moe::kCommWarps), smem, s>>>(tA1, tB1, g1, e1, err, tmo);
+  if (dyn) {
+    moe::G1SchedT<true> g1d;
+    static_assert(sizeof(g1d) == sizeof(g1), "the two schedules share one layout");
+    std::memcpy(&g1d, &g1, sizeof(g1));
+    moe::k_moe_gemm1<true><<<G, cta_threads(moe::kCommWarps), smem, s>>>(tA1, tB1, g1d, e1, err, tmo, next_ctr);
+  } else {
+    moe::k_moe_gemm1<false><<<G, cta_threads(moe::kCommWarps), smem, s>>>(tA1, tB1, g1, e1, err, tmo, nullptr);
+  }
   GICC_CUDA(cudaGetLastError());
   mark(4);
   // 5. GEMM 2 (+ combine push)

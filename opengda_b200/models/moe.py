@@ -87,7 +87,11 @@ class MoELayer:
             "cum_rows": torch.zeros(n * El, dtype=torch.int64, device=dev),
             "cum_pairs": torch.zeros(1, dtype=torch.int64, device=dev),
             "send_pair": i32(pairs), "send_row": i32(pairs),
+            "g1_tile_ctr": torch.zeros(2, dtype=torch.int64, device=dev),
         }
+        # CTAs whose communication warps run the dispatch all-to-all (0 = every CTA).  With
+        # fewer, the first grouped GEMM takes its tiles dynamically so those CTAs do less math.
+        self.dispatch_ctas = 0
         self.topk_idx = i32(pairs)
         self.topk_w = torch.zeros(pairs, dtype=torch.float32, device=dev)
         self.counts = i32(E)
@@ -124,6 +128,7 @@ class MoELayer:
             "timeout_ns": self.rt.timeout_ns if self.rt is not None else 0,
             "ws": {k: v.data_ptr() for k, v in self.ws_t.items()},
             "stage_times": stage_times,
+            "dispatch_ctas": self.dispatch_ctas,
         }
         st = native().k_moe_forward(d)
         if stage_times:
