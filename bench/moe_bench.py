@@ -34,6 +34,8 @@ def main():
     ap.add_argument("--no-baseline", action="store_true")
     ap.add_argument("--out", default=None)
     ap.add_argument("--dispatch-ctas", type=int, default=0, help="CTAs that dispatch (0 = all; A/B option)")
+    ap.add_argument("--combine-ctas", type=int, default=0,
+                    help="CTAs that push the combine (0 = all, from the epilogue; A/B option)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -50,6 +52,7 @@ def main():
 
     layer = MoELayer(args.tokens, args.hidden, args.experts, args.topk, args.inter, rt=rt)
     layer.dispatch_ctas = args.dispatch_ctas
+    layer.combine_ctas = args.combine_ctas
     x, logits = make_inputs(args.tokens, args.hidden, args.experts, rank, seed=4)
 
     def timeit(fn, steps, warmup):

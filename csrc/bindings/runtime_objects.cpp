@@ -387,7 +387,11 @@ void bind_runtime_objects(py::module_& m) {
     a.ws.send_pair = P<int>(w["send_pair"].cast<uint64_t>());
     a.ws.send_row = P<int>(w["send_row"].cast<uint64_t>());
     if (w.contains("g1_tile_ctr")) a.ws.g1_tile_ctr = P<uint64_t>(w["g1_tile_ctr"].cast<uint64_t>());
+    if (w.contains("g2_ctr")) a.ws.g2_ctr = P<uint64_t>(w["g2_ctr"].cast<uint64_t>());
+    if (w.contains("g2_queue")) a.ws.g2_queue = P<uint64_t>(w["g2_queue"].cast<uint64_t>());
     if (d.contains("dispatch_ctas")) a.dispatch_ctas = d["dispatch_ctas"].cast<int>();
+    if (d.contains("combine_ctas")) a.combine_ctas = d["combine_ctas"].cast<int>();
+    if (d.contains("y_stage")) a.y_stage = P<void>(d["y_stage"].cast<uint64_t>());
     std::vector<float> stage(6, 0.f);
     const bool timed = d.contains("stage_times") && d["stage_times"].cast<bool>();
     if (timed) a.stage_ms = stage.data();

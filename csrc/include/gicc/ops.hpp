@@ -195,6 +195,8 @@ struct MoeWorkspace {          // local device arrays
   int* send_pair = nullptr;      // [T*topk]
   int* send_row = nullptr;       // [T*topk]
   uint64_t* g1_tile_ctr = nullptr; // [2], zero-initialised once (needed with dispatch_ctas)
+  uint64_t* g2_ctr = nullptr;      // [6], zero-initialised once (needed with combine_ctas)
+  uint64_t* g2_queue = nullptr;    // [cap/128 * H/256] (needed with combine_ctas)
 };
 struct MoeArgs {
   int n = 1, r = 0, T = 0, H = 0, I = 0, E = 0, topk = 8;
@@ -221,6 +223,9 @@ struct MoeArgs {
   float* stage_ms = nullptr;      // optional host [6]: per-stage device time (synchronises)
   int dispatch_ctas = 0;          // CTAs whose warps dispatch (0 = every CTA); with fewer, the
                                   // first GEMM takes tiles dynamically (ws.g1_tile_ctr)
+  int combine_ctas = 0;           // > 0: the second GEMM stages its rows in y_stage and only this
+                                  // many CTAs push them to the sources (ws.g2_ctr, ws.g2_queue)
+  void* y_stage = nullptr;        // [cap][H] bf16 local (needed with combine_ctas)
 };
 GICC_EXPORT void moe_route(const float* logits, int T, int E, int topk, int* topk_idx, float* topk_w, int* counts,
                            cudaStream_t s);

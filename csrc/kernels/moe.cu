@@ -525,6 +525,167 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------
+// 5b. grouped GEMM 2 with a staged combine (the combine_ctas option): the epilogue stores
+// the gate-scaled rows into a local staging buffer and publishes each finished tile in a
+// queue; the communication warps of `C` CTAs take tiles from the queue and push their rows
+// to the source ranks, so only those SMs issue NVLink stores.  Tiles are taken dynamically,
+// so the pushing CTAs do less math.  Counters come in parity pairs (the tile count follows
+// the routing): call e uses set e & 1 and zeroes the other set for call e+1.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t pack_tile(int e, int mb, int nb) {
+  return ((uint32_t)e << 22) | ((uint32_t)mb << 8) | (uint32_t)nb;  // e < 1024, mb < 16384, nb < 256
+}
+
+struct G2StageSched {
+  static constexpr int kCommWarps = moe::kCommWarps;
+  static constexpr bool kDynamic = true;
+  int n, El, I, H, num_n, C;
+  const int* mblk_prefix;
+  const int* expert_base;
+  const int* expert_rows;
+  unsigned long long* ctr;   // this call's set: [0] tiles taken, [1] queue tail, [2] queue head
+  uint64_t* queue;           // [max tiles] entries (epoch << 32) | packed tile
+  uint64_t epoch;
+  const int4* meta;          // my [cap] meta
+  const uint16_t* y;         // my staging [cap][H]
+  Ptrs8 comb;                // each rank's combine buffer [T*topk][H]
+  Words8 comb_arrivals;      // each rank's [1] arrival word
+
+  __device__ int num_tiles() const { return mblk_prefix[El] * num_n; }
+  __device__ int next_tile() const {
+    const unsigned long long v = atomicAdd(&ctr[0], 1ull);
+    return v < (unsigned long long)num_tiles() ? (int)v : num_tiles();
+  }
+  __device__ TileInfo tile(int t) const {
+    const int mbq = t / num_n;
+    int lo = 0, hi = El - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (mblk_prefix[mid] <= mbq) lo = mid; else hi = mid - 1;
+    }
+    const int e = lo;
+    const int rem = t - mblk_prefix[e] * num_n;
+    const int mbs = mblk_prefix[e + 1] - mblk_prefix[e];
+    const int nb = mbs ? rem / mbs : 0, mb = mbs ? rem - nb * mbs : 0;
+    TileInfo ti;
+    ti.a_row = expert_base[e] + mb * BM;
+    ti.m0 = ti.a_row;
+    ti.n0 = nb * 256;
+    ti.b_row = e * H + nb * 256;
+    ti.kb0 = 0;
+    ti.kb1 = I / BK;
+    ti.aux = e;
+    ti.aux2 = mb;
+    return ti;
+  }
+  __device__ bool producer_wait(const TileInfo&, uint64_t, volatile int*, ErrorRecord*) const { return true; }
+  __device__ void issue_loads(const TileInfo& ti, int kb, void* sA, void* sB, uint64_t* bar, const CUtensorMap* tmA,
+                              const CUtensorMap* tmB) const {
+    ptx::tma_load_2d(sA, tmA, bar, kb * BK, ti.a_row);
+    ptx::tma_load_2d(sB, tmB, bar, kb * BK, ti.b_row);
+  }
+  // Push queued tiles: one warp per row (32 lanes x 16 bytes = the tile's 256 columns).
+  __device__ void comm(int cw, int lane, volatile int* abort_flag, ErrorRecord* err, uint64_t timeout_ns) const {
+    __shared__ int comm_tile;
+    __shared__ uint32_t cnt[kMaxR];
+    const int tid = cw * 32 + lane;
+    constexpr int kT = kCommWarps * 32;
+    if ((int)blockIdx.x >= C) return;
+    if (tid < kMaxR) cnt[tid] = 0;
+    const int T = num_tiles();
+    for (;;) {
+      if (tid == 0) {
+        int packed = -1;
+        const unsigned long long idx = atomicAdd(&ctr[2], 1ull);
+        if (idx < (unsigned long long)T && !*abort_flag) {
+          const uint64_t* q = queue + idx;
+          const uint64_t t0 = ptx::globaltimer();
+          for (uint32_t i = 0;; ++i) {
+            const uint64_t v = ptx::ld_acquire_sys(q);
+            if ((v >> 32) == (epoch & 0xffffffffull)) {
+              packed = (int)(v & 0xffffffffull);
+              break;
+            }
+            if ((i & 63) == 63 && (*abort_flag || ptx::globaltimer() - t0 > timeout_ns)) {
+              if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_MOE_COUNT, -1, -1, v, epoch);
+              *abort_flag = 1;
+              break;
+            }
+          }
+        }
+        comm_tile = packed;
+      }
+      asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
+      const int packed = comm_tile;
+      if (packed < 0) break;
+      const int e = packed >> 22, mb = (packed >> 8) & 0x3fff, nb = packed & 0xff;
+      const int a_row = expert_base[e] + mb * BM;
+      const int valid = min(BM, expert_rows[e] - mb * BM);
+      for (int row = cw; row < valid; row += kCommWarps) {
+        const int4 m = meta[a_row + row];
+        const uint4 v = reinterpret_cast<const uint4*>(y + (size_t)(a_row + row) * H + nb * 256)[lane];
+        uint16_t* dst = reinterpret_cast<uint16_t*>(comb.p[m.x]) + (size_t)m.y * H + nb * 256;
+        ptx::st_v4_na(reinterpret_cast<uint4*>(dst) + lane, v);
+        if (lane == 0) atomicAdd(&cnt[m.x], 1u);
+      }
+      ptx::fence_acq_rel_sys();
+      asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
+      if (tid < n) {
+        const uint32_t c = cnt[tid];
+        cnt[tid] = 0;
+        if (c) ptx::red_release_sys_add(comb_arrivals.p[tid], c);
+      }
+      asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
+    }
+  }
+};
+
+struct G2StageEpi {
+  static constexpr bool kNeedsTileDone = true;
+  static constexpr bool kPairHalves = false;
+  int H;
+  const int* expert_rows;
+  const int4* meta;
+  uint16_t* y;               // my staging [cap][H]
+  unsigned long long* ctr;   // this call's set (queue tail at [1])
+  uint64_t* queue;
+  uint64_t epoch;
+  int valid;
+  float gate;
+  __device__ static void fence_before_done() { ptx::fence_acq_rel_sys(); }
+  __device__ void begin_tile(const TileInfo& ti, int row) {
+    valid = ti.aux2 * BM + row < expert_rows[ti.aux];
+    if (valid) gate = __int_as_float(meta[ti.a_row + row].z);
+  }
+  __device__ __forceinline__ void store(const TileInfo& ti, int row, int c, const uint32_t* acc) {
+    if (!valid) return;
+    uint16_t* p = y + (size_t)(ti.a_row + row) * H + ti.n0 + c;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 v;
+      v.x = ptx::pack_bf16x2(gate * __uint_as_float(acc[8 * j + 0]), gate * __uint_as_float(acc[8 * j + 1]));
+      v.y = ptx::pack_bf16x2(gate * __uint_as_float(acc[8 * j + 2]), gate * __uint_as_float(acc[8 * j + 3]));
+      v.z = ptx::pack_bf16x2(gate * __uint_as_float(acc[8 * j + 4]), gate * __uint_as_float(acc[8 * j + 5]));
+      v.w = ptx::pack_bf16x2(gate * __uint_as_float(acc[8 * j + 6]), gate * __uint_as_float(acc[8 * j + 7]));
+      ptx::st_v4(p + 8 * j, v);
+    }
+  }
+  __device__ void end_tile(const TileInfo&, int) {}
+  __device__ void tile_done(const TileInfo& ti) {  // last epilogue warp, after every warp's stores
+    const unsigned long long slot = atomicAdd(&ctr[1], 1ull);
+    ptx::st_release_sys(queue + slot, (epoch << 32) | pack_tile(ti.aux, ti.aux2, ti.n0 / 256));
+  }
+};
+
+__global__ void __launch_bounds__(cta_threads(kCommWarps), 1)
+    k_moe_gemm2_staged(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       G2StageSched s, G2StageEpi e, ErrorRecord* err, uint64_t timeout_ns, int rank,
+                       unsigned long long* next_ctr) {
+  if (blockIdx.x == 0 && threadIdx.x < 3) next_ctr[threadIdx.x] = 0;  // the next call's set
+  gemm_core<256>(&tmA, &tmB, s, e, err, timeout_ns, rank);
+}
+
+// ---------------------------------------------------------------------------------------
 // 6. combine: out[t] = sum_j comb[t*topk + j]
 // ---------------------------------------------------------------------------------------
 __global__ void k_combine(const uint16_t* comb, uint16_t* out, int T, int H, int topk, const uint64_t* arrivals,
@@ -699,7 +860,49 @@ void moe_forward(const MoeArgs& a, cudaStream_t s) {
     e2.comb.p[i] = a.comb[i];
     e2.comb_arrivals.p[i] = a.comb_arrivals[i];
   }
-  moe::k_moe_gemm2<<<G, kThreads, smem, s>>>(tA2, tB2, g2, e2, err, tmo, r);
+  if (a.combine_ctas > 0 && a.combine_ctas < G) {
+    if (!a.ws.g2_ctr || !a.ws.g2_queue || !a.y_stage)
+      throw std::runtime_error("gicc::moe_forward: combine_ctas needs ws.g2_ctr, ws.g2_queue and y_stage");
+    if (El > 1024 || a.cap_rows / BM > 16384 || a.H / 256 > 255)
+      throw std::runtime_error("gicc::moe_forward: combine_ctas supports El <= 1024, cap/128 <= 16384, H/256 < 256");
+    unsigned long long* cur = reinterpret_cast<unsigned long long*>(a.ws.g2_ctr) + 3 * (a.epoch & 1);
+    unsigned long long* nxt = reinterpret_cast<unsigned long long*>(a.ws.g2_ctr) + 3 * ((a.epoch + 1) & 1);
+    moe::G2StageSched gs{};
+    gs.n = n;
+    gs.El = El;
+    gs.I = a.I;
+    gs.H = a.H;
+    gs.num_n = a.H / 256;
+    gs.C = a.combine_ctas;
+    gs.mblk_prefix = a.ws.mblk_prefix;
+    gs.expert_base = a.ws.expert_base;
+    gs.expert_rows = a.ws.expert_rows;
+    gs.ctr = cur;
+    gs.queue = a.ws.g2_queue;
+    gs.epoch = a.epoch;
+    gs.meta = static_cast<const int4*>(a.meta[r]);
+    gs.y = static_cast<const uint16_t*>(a.y_stage);
+    for (int i = 0; i < n; ++i) {
+      gs.comb.p[i] = a.comb[i];
+      gs.comb_arrivals.p[i] = a.comb_arrivals[i];
+    }
+    moe::G2StageEpi es{};
+    es.H = a.H;
+    es.expert_rows = a.ws.expert_rows;
+    es.meta = static_cast<const int4*>(a.meta[r]);
+    es.y = static_cast<uint16_t*>(a.y_stage);
+    es.ctr = cur;
+    es.queue = a.ws.g2_queue;
+    es.epoch = a.epoch;
+    static bool attr2[64] = {false};
+    if (!attr2[dev]) {
+      GICC_CUDA(cudaFuncSetAttribute(moe::k_moe_gemm2_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      attr2[dev] = true;
+    }
+    moe::k_moe_gemm2_staged<<<G, cta_threads(moe::kCommWarps), smem, s>>>(tA2, tB2, gs, es, err, tmo, r, nxt);
+  } else {
+    moe::k_moe_gemm2<<<G, kThreads, smem, s>>>(tA2, tB2, g2, e2, err, tmo, r);
+  }
   GICC_CUDA(cudaGetLastError());
   mark(5);
   // 6. combine

@@ -88,10 +88,17 @@ class MoELayer:
             "cum_pairs": torch.zeros(1, dtype=torch.int64, device=dev),
             "send_pair": i32(pairs), "send_row": i32(pairs),
             "g1_tile_ctr": torch.zeros(2, dtype=torch.int64, device=dev),
+            "g2_ctr": torch.zeros(6, dtype=torch.int64, device=dev),
+            "g2_queue": torch.zeros(self.cap // 128 * (H // 256), dtype=torch.int64, device=dev),
         }
         # CTAs whose communication warps run the dispatch all-to-all (0 = every CTA).  With
         # fewer, the first grouped GEMM takes its tiles dynamically so those CTAs do less math.
         self.dispatch_ctas = 0
+        # CTAs that push the second GEMM's rows back to the sources (0 = every CTA pushes its
+        # own tiles from the epilogue).  With fewer, the rows are staged in local HBM
+        # (self.y_stage, [cap, H] bf16, allocated on first use) and queued for those CTAs.
+        self.combine_ctas = 0
+        self.y_stage = None
         self.topk_idx = i32(pairs)
         self.topk_w = torch.zeros(pairs, dtype=torch.float32, device=dev)
         self.counts = i32(E)
@@ -112,6 +119,8 @@ class MoELayer:
         p = self.epoch % 2
         n = self.n
         P = self._ptr
+        if self.combine_ctas > 0 and self.y_stage is None:
+            self.y_stage = torch.empty(self.cap, self.H, dtype=torch.bfloat16, device=self.h.device)
         d = {
             "n": n, "r": self.r, "T": self.T, "H": self.H, "I": self.I, "E": self.E, "topk": self.topk,
             "logits": logits.data_ptr(), "x": x.data_ptr(), "w1": self.w1.data_ptr(), "w2": self.w2.data_ptr(),
@@ -129,6 +138,8 @@ class MoELayer:
             "ws": {k: v.data_ptr() for k, v in self.ws_t.items()},
             "stage_times": stage_times,
             "dispatch_ctas": self.dispatch_ctas,
+            "combine_ctas": self.combine_ctas,
+            "y_stage": self.y_stage.data_ptr() if self.y_stage is not None else 0,
         }
         st = native().k_moe_forward(d)
         if stage_times:

@@ -1,5 +1,7 @@
 """MoE layer: routing kernel and the full fused forward (one GPU: every expert local)
 against an fp32 PyTorch reference."""
+import os
+
 import pytest
 import torch
 
@@ -36,4 +38,27 @@ def test_moe_forward_single_gpu(T, H, E, k, I):
         ref = reference_moe(x, logits, k, layer.w_gate, layer.w_up, layer.w2, rows)
         got = y[rows].float()
         rel = ((got - ref).norm() / ref.norm()).item()
+        assert rel < 2e-2, (call, rel)
+
+
+@pytest.mark.skipif(not os.environ.get("GICC_TEST_CONFINED_MOE"),
+                    reason="confined dispatch / staged combine options: run with GICC_TEST_CONFINED_MOE=1")
+@pytest.mark.parametrize("dispatch_ctas,combine_ctas", [(8, 0), (0, 8), (8, 8)])
+def test_moe_forward_confined_options(dispatch_ctas, combine_ctas):
+    """The A/B options that confine NVLink stores to a few CTAs (dynamic tiles in both grouped
+    GEMMs, combine rows staged locally and queued) give the same result as the reference."""
+    from opengda_b200.models.moe import MoELayer, make_inputs, reference_moe
+    from opengda_b200.ops.gemm import check_errors
+    T, H, E, k, I = 512, 1024, 32, 8, 512
+    layer = MoELayer(T, H, E, k, I, rt=None, weight_std=0.05)
+    layer.dispatch_ctas = dispatch_ctas
+    layer.combine_ctas = combine_ctas
+    for call in range(3):  # both parities of the tile counters, then the first again
+        x, logits = make_inputs(T, H, E, 0, seed=20 + call)
+        y = layer(x, logits)
+        torch.cuda.synchronize()
+        check_errors()
+        rows = torch.arange(0, T, T // 16, device="cuda")
+        ref = reference_moe(x, logits, k, layer.w_gate, layer.w_up, layer.w2, rows)
+        rel = ((y[rows].float() - ref).norm() / ref.norm()).item()
         assert rel < 2e-2, (call, rel)
