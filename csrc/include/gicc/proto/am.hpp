@@ -84,13 +84,13 @@ GICC_HD am_slot_t* slot_at(uint8_t* ring_base, int src, int nslots, uint32_t slo
   return reinterpret_cast<am_slot_t*>(ring_base + ((uint64_t)src * nslots + idx % (uint64_t)nslots) * slot_bytes);
 }
 
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD bool can_send(const AmView& v, int dst) {
   return v.head[dst] - Mem::load_acquire(&v.credit[dst]) < (uint64_t)v.nslots;
 }
 
 // Send one message; returns its sequence number (>0) or 0 on timeout (no credit).
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD uint64_t send(AmView& v, int dst, uint16_t handler, const am_args_t& args, const void* payload,
                       uint32_t len, uint8_t flags) {
   if (len > AM_MAX_PAYLOAD_SIZE || (len > 0 && v.slot_bytes < AM_SHORT_SIZE + len)) return 0;
@@ -120,14 +120,14 @@ GICC_HD uint64_t send(AmView& v, int dst, uint16_t handler, const am_args_t& arg
 }
 
 // Write the reply for request `seq` from `src` into the requester's ack words.
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD void reply(AmView& v, int src, uint64_t seq, uint64_t value) {
   Mem::store_release(&v.peer_ack_val[src][v.rank], value);
   Mem::store_release(&v.peer_ack[src][v.rank], seq);
 }
 
 // Built-in handlers.  Returns the reply value for requests.
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD uint64_t builtin_handler(AmView& v, const am_slot_t* s) {
   switch (s->hdr.handler_id) {
     case AM_HANDLER_COUNTER_ADD:
@@ -164,12 +164,12 @@ GICC_HD int poll_peer(AmView& v, int src, int max_msgs, Handler&& handler) {
   return n;
 }
 
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD int poll_peer_builtin(AmView& v, int src, int max_msgs) {
   return poll_peer<Mem>(v, src, max_msgs, [](AmView& vv, const am_slot_t* s) { return builtin_handler<Mem>(vv, s); });
 }
 
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD int poll_all_builtin(AmView& v, int max_per_peer) {
   int n = 0;
   for (int p = 0; p < v.size; ++p) n += poll_peer_builtin<Mem>(v, p, max_per_peer);  // self included
@@ -177,7 +177,7 @@ GICC_HD int poll_all_builtin(AmView& v, int max_per_peer) {
 }
 
 // Wait (bounded) for one message from src and dispatch it.  Returns 1, or 0 on timeout.
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD int wait_one(AmView& v, int src) {
   const uint64_t idx = v.tail[src];
   am_slot_t* s = slot_at(v.inbox, src, v.nslots, v.slot_bytes, idx);
@@ -187,7 +187,7 @@ GICC_HD int wait_one(AmView& v, int src) {
 }
 
 // Wait (bounded) for the reply to request `seq` sent to dst; returns true and the value.
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD bool wait_reply(AmView& v, int dst, uint64_t seq, uint64_t* value) {
   uint64_t seen = 0;
   if (!proto::wait_until<Mem>(&v.ack[dst], proto::CMP_GE, seq, v.timeout_ns, &seen)) return false;

@@ -24,7 +24,7 @@ GICC_HD int n_rounds_for(int n) {
 // waits for it runs out its bounded wait and reports GICC_ETIMEDOUT; nothing faults.
 enum Inject : int { INJECT_NONE = 0, INJECT_SKIP_SIGNAL = 1, INJECT_STALE_EPOCH = 2 };
 
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD int dissemination_barrier(int n_rounds, uint64_t* const* trigger, uint64_t* signals, uint64_t epoch,
                                   uint64_t timeout_ns, int* fail_round, uint64_t* seen, int inject = INJECT_NONE) {
   Mem::fence();  // everything before the barrier is visible before our first signal

@@ -43,7 +43,7 @@ struct CmdRingView {
 
 // Producer: enqueue command number `next` (0-based); waits (bounded) for a free slot.
 // Returns the command's sequence number (next + 1), or 0 when no slot freed in time.
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD uint64_t cmdring_push(const CmdRingView& v, uint64_t next, const Command& c, uint64_t timeout_ns) {
   if (next >= (uint64_t)v.nslots) {
     uint64_t seen = 0;
@@ -62,7 +62,7 @@ GICC_HD uint64_t cmdring_push(const CmdRingView& v, uint64_t next, const Command
 }
 
 // Consumer (one thread): wait for command `i`; returns false on idle timeout.
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD bool cmdring_next(const CmdRingView& v, uint64_t i, Command* out) {
   Command* s = &v.cmds[i % (uint64_t)v.nslots];
   uint64_t seen = 0;
@@ -79,7 +79,7 @@ GICC_HD bool cmdring_next(const CmdRingView& v, uint64_t i, Command* out) {
 }
 
 // Consumer: command `i` and everything before it are complete (their stores visible).
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD void cmdring_complete(const CmdRingView& v, uint64_t i) {
   Mem::fence();
   Mem::store_release(v.done, i + 1);

@@ -43,7 +43,7 @@ GICC_HD void litmus_delay(uint32_t n) {
 }
 
 // MP writer: data is a ring of k words in the reader's memory, flag one word there.
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD void litmus_mp_writer(uint64_t* data, uint64_t* flag, int k, int iters, uint32_t seed, uint32_t max_delay) {
   uint32_t s = seed | 1u;
   for (int i = 0; i < iters; ++i) {
@@ -55,7 +55,7 @@ GICC_HD void litmus_mp_writer(uint64_t* data, uint64_t* flag, int k, int iters, 
 
 // MP reader (local memory): counts iterations where the flag said >= i+1 but the data
 // word of iteration i still held less.  Returns GICC_OK or GICC_ETIMEDOUT.
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD int litmus_mp_reader(const uint64_t* data, const uint64_t* flag, int k, int iters, uint32_t seed,
                              uint32_t max_delay, uint64_t timeout_ns, uint64_t* violations) {
   uint32_t s = seed | 1u;
@@ -77,7 +77,7 @@ GICC_HD int litmus_mp_reader(const uint64_t* data, const uint64_t* flag, int k, 
 // a random delay, then  store 1 -> mine_remote[i];  [fence.sc];  out[i] = theirs_local[i].
 // mine_remote is the other side's copy of "my" word array, theirs_local this side's copy of
 // the other side's word array; both start zeroed.
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD int litmus_sb_side(uint64_t* ready_remote, const uint64_t* ready_local, uint64_t* mine_remote,
                            const uint64_t* theirs_local, int iters, int use_fence, uint32_t seed, uint32_t max_delay,
                            uint64_t timeout_ns, uint64_t* out) {

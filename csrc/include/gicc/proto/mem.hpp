@@ -11,8 +11,13 @@
 
 #if defined(__CUDACC__)
 #define GICC_HD __host__ __device__ __forceinline__
+// Before a protocol template: each instantiation runs on one side only (DevMem on the GPU,
+// HostMem on the CPU), so nvcc's check that a host-device function calls host-device code
+// does not apply.
+#define GICC_PROTO_TEMPLATE _Pragma("nv_exec_check_disable") template <class Mem>
 #else
 #define GICC_HD inline
+#define GICC_PROTO_TEMPLATE template <class Mem>
 #endif
 
 #if !defined(__CUDA_ARCH__)
@@ -91,7 +96,7 @@ struct HostMem {
 
 // Wait until cmp(*p, x) holds (acquire), at most timeout_ns.  Returns the last value seen
 // through *seen and true on success.
-template <class Mem>
+GICC_PROTO_TEMPLATE
 GICC_HD bool wait_until(const uint64_t* p, int cmp, uint64_t x, uint64_t timeout_ns, uint64_t* seen) {
   uint64_t v = Mem::load_acquire(p);
   if (cmp_ok(v, cmp, x)) {
