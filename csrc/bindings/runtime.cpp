@@ -2,6 +2,7 @@
 #include <torch/extension.h>
 
 #include "gicc/bootstrap.hpp"
+#include "gicc/runtime.hpp"
 
 namespace py = pybind11;
 using gicc::Bootstrap;
@@ -32,6 +33,9 @@ int litmus_run(uint64_t* shm, int rank, int test, int iters, int k, int use_fenc
 void bind_runtime(py::module_& m) {
   py::register_exception<gicc::BootstrapError>(m, "BootstrapError", PyExc_RuntimeError);
 
+  m.def("check_exchange_consistency", &gicc::check_exchange_consistency, py::arg("boot"), py::arg("kinds"),
+        py::arg("multicast"), py::call_guard<py::gil_scoped_release>(),
+        "exchange()'s collective check of the newly registered buffer tables (no GPU needed)");
   py::class_<Bootstrap, std::shared_ptr<Bootstrap>>(m, "Bootstrap")
       .def(py::init<>(), py::call_guard<py::gil_scoped_release>(), "bootstrap from the environment (blocks for all ranks)")
       .def(py::init<int, int, const std::string&, double>(), py::arg("rank"), py::arg("size"), py::arg("addr"),

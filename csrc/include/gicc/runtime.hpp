@@ -128,4 +128,11 @@ class GICC_EXPORT Runtime {
   bool finalized_ = false;
 };
 
+// The collective consistency check exchange() runs before any handle crosses a process
+// boundary: every rank registered the same number of buffers since the last exchange, with
+// the same kind and multicast flag, in the same order.  Throws BootstrapError
+// (GICC_EMISMATCH) naming the first difference on every rank; uses only the bootstrap.
+GICC_EXPORT void check_exchange_consistency(Bootstrap& boot, const std::vector<int32_t>& kinds,
+                                            const std::vector<int32_t>& multicast);
+
 }  // namespace gicc

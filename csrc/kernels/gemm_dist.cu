@@ -700,6 +700,9 @@ void ag_gemm(const AgGemmArgs& a, cudaStream_t s) {
   const CUtensorMap tB = make_tmap_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.Ns, a.K, a.ldb, BN_, BK,
                                       CU_TENSOR_MAP_SWIZZLE_128B);
   const int G = a.grid > 0 ? a.grid : num_sms();
+  // One CTA per SM (the shared-memory ring allows no second); the CTAs wait on one another's
+  // tiles and arrivals, so all of them must be resident at once.
+  if (G > num_sms()) throw std::runtime_error("gicc: a persistent distributed GEMM needs grid <= number of SMs");
   AgSched sc{};
   sc.n = a.n;
   sc.r = a.r;
@@ -788,6 +791,9 @@ void gemm_rs(const GemmRsArgs& a, cudaStream_t s) {
   const CUtensorMap tB = make_tmap_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.ldb, BN_, BK,
                                       CU_TENSOR_MAP_SWIZZLE_128B);
   const int G = a.grid > 0 ? a.grid : num_sms();
+  // One CTA per SM (the shared-memory ring allows no second); the CTAs wait on one another's
+  // tiles and arrivals, so all of them must be resident at once.
+  if (G > num_sms()) throw std::runtime_error("gicc: a persistent distributed GEMM needs grid <= number of SMs");
   if (a.staging_mc) {
     const int Q = a.units_per_band > 0 ? a.units_per_band : 4;
     if (BM % Q || !a.band_tiles || !a.tile_counter || !a.slots[a.r])

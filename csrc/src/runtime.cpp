@@ -274,18 +274,49 @@ Buffer Runtime::register_buffer(void* ptr, size_t size, bool is_device) {
 
 void Runtime::exchange() {
   NvtxRange nvtx("gicc::Runtime::exchange");
-  // collective: every rank must have registered the same number of buffers
-  const int mine = (int)regions_.size();
-  auto counts = boot_->allgather_fixed<int>(mine);
-  for (int r = 0; r < size(); ++r)
-    if (counts[r] != mine)
-      throw BootstrapError(GICC_EMISMATCH, "gicc::Runtime::exchange: rank " + std::to_string(r) + " registered " +
-                                               std::to_string(counts[r]) + " buffers, rank " + std::to_string(rank()) +
-                                               " registered " + std::to_string(mine));
+  std::vector<int32_t> kinds, mc;
+  for (size_t i = exchanged_; i < regions_.size(); ++i) {
+    kinds.push_back(regions_[i]->kind);
+    mc.push_back(regions_[i]->multicast ? 1 : 0);
+  }
+  check_exchange_consistency(*boot_, kinds, mc);
   ++exchange_epoch_;
   import_new_regions(regions_, exchanged_, exchange_epoch_ * 1024);
   exchanged_ = regions_.size();
   boot_->barrier();
+}
+
+void check_exchange_consistency(Bootstrap& boot, const std::vector<int32_t>& kinds,
+                                const std::vector<int32_t>& multicast) {
+  if (kinds.size() != multicast.size()) throw std::invalid_argument("check_exchange_consistency: table sizes differ");
+  const int mine = (int)kinds.size();
+  // Counts first: a rank with a different count must not enter an allgather of another size.
+  const auto counts = boot.allgather_fixed<int>(mine);
+  for (int r = 0; r < boot.size(); ++r)
+    if (counts[r] != mine)
+      throw BootstrapError(GICC_EMISMATCH, "gicc::Runtime::exchange: rank " + std::to_string(r) + " registered " +
+                                               std::to_string(counts[r]) + " buffers, rank " +
+                                               std::to_string(boot.rank()) + " registered " + std::to_string(mine));
+  if (mine == 0) return;
+  std::vector<int32_t> tab(2 * (size_t)mine);
+  for (int i = 0; i < mine; ++i) {
+    tab[2 * i] = kinds[i];
+    tab[2 * i + 1] = multicast[i];
+  }
+  const auto all = boot.allgather(tab.data(), (int)(tab.size() * sizeof(int32_t)));
+  for (int p = 0; p < boot.size(); ++p) {
+    if (all[p].size() != tab.size() * sizeof(int32_t))
+      throw BootstrapError(GICC_EMISMATCH, "gicc::Runtime::exchange: buffer table size differs on rank " + std::to_string(p));
+    const int32_t* q = reinterpret_cast<const int32_t*>(all[p].data());
+    for (int i = 0; i < mine; ++i) {
+      if (q[2 * i] != kinds[i])
+        throw BootstrapError(GICC_EMISMATCH, "gicc::Runtime::exchange: new buffer " + std::to_string(i) +
+                                                 " has a different kind on rank " + std::to_string(p));
+      if (q[2 * i + 1] != multicast[i])
+        throw BootstrapError(GICC_EMISMATCH, "gicc::Runtime::exchange: multicast flag of new buffer " +
+                                                 std::to_string(i) + " differs on rank " + std::to_string(p));
+    }
+  }
 }
 
 void Runtime::import_new_regions(std::vector<std::unique_ptr<Region>>& list, size_t first, int tag_base) {

@@ -34,8 +34,9 @@ def test_fd_passing(n, tmp_path):
     assert all(v == "ok" for v in res.values()), res
 
 
-def test_rank_that_leaves_is_detected(tmp_path):
-    rc, res = _run(3, "die", tmp_path, env={"GICC_BOOTSTRAP_TIMEOUT_MS": "20000"})
+@pytest.mark.parametrize("how", ["die", "kill"])
+def test_rank_that_leaves_is_detected(how, tmp_path):
+    rc, res = _run(3, how, tmp_path, env={"GICC_BOOTSTRAP_TIMEOUT_MS": "20000"})
     for r in (0, 2):
         assert res[r] is not None and res[r].startswith("err:") and "left the job" in res[r], res
         assert float(res[r].rsplit(":", 1)[1]) < 5.0, res  # well before the timeout
@@ -65,3 +66,16 @@ def test_native_host_collectives_cpu():
                        cwd=root, capture_output=True, text=True, timeout=120)
     assert p.returncode == 0, p.stdout + p.stderr
     assert p.stdout.count("PASS") == 3
+
+
+@pytest.mark.parametrize("mode,needle", [("exchange_count", "registered"), ("exchange_kind", "different kind")])
+def test_exchange_table_mismatch_fails_on_every_rank(mode, needle, tmp_path):
+    rc, res = _run(3, mode, tmp_path)
+    for r in range(3):
+        assert res[r] is not None and res[r].startswith("err:BootstrapError") and needle in res[r], res
+
+
+def test_exchange_tables_that_match_pass(tmp_path):
+    rc, res = _run(3, "exchange_ok", tmp_path)
+    assert rc == 0, res
+    assert all(v == "ok" for v in res.values()), res

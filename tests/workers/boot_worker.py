@@ -52,10 +52,14 @@ def main():
         assert data == f"rank{(r - 1) % n}", data
         b.barrier()
         res.append("ok")
-    elif mode == "die":
-        # rank 1 leaves without saying goodbye; the others must learn it at their barrier
+    elif mode in ("die", "kill"):
+        # rank 1 leaves without saying goodbye (exits, or is killed with SIGKILL); the others
+        # must learn it at their barrier
         b.barrier()
         if r == 1:
+            if mode == "kill":
+                import signal
+                os.kill(os.getpid(), signal.SIGKILL)
             os._exit(0)
         t0 = time.time()
         try:
@@ -86,9 +90,24 @@ def main():
                 res.append("no-error")
             except Exception as e:
                 res.append(f"err:{type(e).__name__}:{e}:{time.time() - t0:.2f}")
+    elif mode in ("exchange_count", "exchange_kind", "exchange_ok"):
+        # the buffer tables exchange() compares before any handle is passed: rank 1 registered
+        # one buffer more, or one of another kind; every rank must see the mismatch
+        from opengda_b200 import native
+        kinds, mc = [0, 0, 1], [0, 1, 0]
+        if r == 1 and mode == "exchange_count":
+            kinds, mc = kinds + [0], mc + [0]
+        if r == 1 and mode == "exchange_kind":
+            kinds = [0, 1, 1]
+        try:
+            native().check_exchange_consistency(b.native, kinds, mc)
+            b.barrier()
+            res.append("ok")
+        except Exception as e:
+            res.append(f"err:{type(e).__name__}:{e}")
     with open(f"{out}.{r}", "w") as f:
         f.write("\n".join(res))
-    if mode in ("die", "abort", "timeout"):
+    if mode in ("die", "kill", "abort", "timeout", "exchange_count", "exchange_kind"):
         os._exit(0)  # skip the goodbye handshake of a failed job
 
 
