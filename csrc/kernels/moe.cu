@@ -532,8 +532,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // so the pushing CTAs do less math.  Counters come in parity pairs (the tile count follows
 // the routing): call e uses set e & 1 and zeroes the other set for call e+1.
 // ---------------------------------------------------------------------------------------
+// A queued tile: expert (9 bits), m-block within the expert (14 bits), n-block (8 bits); the
+// top bit stays clear so the value is a non-negative int.
 __device__ __forceinline__ uint32_t pack_tile(int e, int mb, int nb) {
-  return ((uint32_t)e << 22) | ((uint32_t)mb << 8) | (uint32_t)nb;  // e < 1024, mb < 16384, nb < 256
+  return ((uint32_t)e << 22) | ((uint32_t)mb << 8) | (uint32_t)nb;  // e < 512, mb < 16384, nb < 256
 }
 
 struct G2StageSched {
@@ -863,8 +865,8 @@ void moe_forward(const MoeArgs& a, cudaStream_t s) {
   if (a.combine_ctas > 0 && a.combine_ctas < G) {
     if (!a.ws.g2_ctr || !a.ws.g2_queue || !a.y_stage)
       throw std::runtime_error("gicc::moe_forward: combine_ctas needs ws.g2_ctr, ws.g2_queue and y_stage");
-    if (El > 1024 || a.cap_rows / BM > 16384 || a.H / 256 > 255)
-      throw std::runtime_error("gicc::moe_forward: combine_ctas supports El <= 1024, cap/128 <= 16384, H/256 < 256");
+    if (El > 512 || a.cap_rows / BM > 16384 || a.H / 256 > 255)  // a queue entry packs (e, mb, nb) in 31 bits
+      throw std::runtime_error("gicc::moe_forward: combine_ctas supports El <= 512, cap/128 <= 16384, H/256 < 256");
     unsigned long long* cur = reinterpret_cast<unsigned long long*>(a.ws.g2_ctr) + 3 * (a.epoch & 1);
     unsigned long long* nxt = reinterpret_cast<unsigned long long*>(a.ws.g2_ctr) + 3 * ((a.epoch + 1) & 1);
     moe::G2StageSched gs{};
