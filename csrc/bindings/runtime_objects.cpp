@@ -335,6 +335,32 @@ void bind_runtime_objects(py::module_& m) {
   m.def("k_wait_count", [](uint64_t counter, uint64_t target, uint64_t timeout_ns, int rank) {
     ops::wait_count(P<const uint64_t>(counter), target, timeout_ns, rank, cur_stream());
   });
+  m.def("ring_mm_grid", &ops::ring_mm_grid, py::arg("Ns"), py::arg("push_ctas"));
+  m.def("k_ring_mm_step", [](py::dict d) {
+    ops::RingMmStep a;
+    auto u64 = [&](const char* k) { return d.contains(k) ? d[k].cast<uint64_t>() : (uint64_t)0; };
+    a.N = d["N"].cast<int>();
+    a.Ns = d["Ns"].cast<int>();
+    a.A = P<const float>(u64("A"));
+    a.Bcur = P<const float>(u64("Bcur"));
+    a.C = P<float>(u64("C"));
+    a.col_block = d["col_block"].cast<int>();
+    a.Bnext_remote = P<float>(u64("Bnext_remote"));
+    a.arrivals_remote = P<uint64_t>(u64("arrivals_remote"));
+    a.arrivals = P<const uint64_t>(u64("arrivals"));
+    a.arrivals_target = u64("arrivals_target");
+    a.consumed = P<const uint64_t>(u64("consumed"));
+    a.consumed_target = u64("consumed_target");
+    a.consumed_left = P<uint64_t>(u64("consumed_left"));
+    a.ticket = P<unsigned long long>(u64("ticket"));
+    a.ticket_target = u64("ticket_target");
+    a.push_ctas = d.contains("push_ctas") ? d["push_ctas"].cast<int>() : 0;
+    a.timeout_ns = u64("timeout_ns");
+    a.rank = d.contains("rank") ? d["rank"].cast<int>() : 0;
+    a.left = d.contains("left") ? d["left"].cast<int>() : -1;
+    a.right = d.contains("right") ? d["right"].cast<int>() : -1;
+    ops::ring_mm_step(a, cur_stream());
+  });
   m.def("k_saxpy", [](uint64_t x, uint64_t y, float a, size_t n) {
     ops::saxpy(P<const float>(x), P<float>(y), a, n, cur_stream());
   });

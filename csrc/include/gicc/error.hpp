@@ -40,6 +40,7 @@ enum Where : int {
   W_QUIET = 10,
   W_BOUNDS = 11,
   W_PINGPONG = 12,
+  W_RING_MM = 13,
 };
 
 struct ErrorRecord {

@@ -56,6 +56,34 @@ GICC_EXPORT void allreduce_bf16(int algo, const void* const* in, void* const* ou
                                 int n, int me, size_t count, float scale, bool out_f32, uint64_t* const* flag_bases,
                                 int max_blocks, uint64_t epoch, uint64_t timeout_ns, int blocks, cudaStream_t s);
 
+// ---- ring-stripe fp32 matmul (ring_mm.cu) -----------------------------------------------------
+// One step of C_s = A_s . B over a ring of n ranks: A_s [Ns][N] (my rows), B stripes [N][Ns]
+// travelling to the right, C_s [Ns][N].  Counters are monotonic over the whole job: for the
+// job's g-th step (g = 0, 1, ...) the host passes arrivals_target = (stripes received so far
+// including this one) * push_ctas, consumed_target = steps the right neighbour must have
+// finished, ticket_target = (g + 1) * grid.
+struct RingMmStep {
+  int N = 0, Ns = 0;
+  const float* A = nullptr;
+  const float* Bcur = nullptr;           // the stripe held this step (own stripe or a landing buffer)
+  float* C = nullptr;
+  int col_block = 0;                     // the stripe's index: columns [col_block*Ns, +Ns) of C
+  float* Bnext_remote = nullptr;         // right neighbour's landing buffer for the next step (null: no push)
+  uint64_t* arrivals_remote = nullptr;   // right neighbour's arrival word
+  const uint64_t* arrivals = nullptr;    // mine (null: Bcur is local)
+  uint64_t arrivals_target = 0;
+  const uint64_t* consumed = nullptr;    // mine, advanced by the right neighbour once per finished step
+  uint64_t consumed_target = 0;
+  uint64_t* consumed_left = nullptr;     // the left neighbour's consumed word (null when alone)
+  unsigned long long* ticket = nullptr;  // local count of finished CTAs (monotonic)
+  unsigned long long ticket_target = 0;
+  int push_ctas = 0;                     // CTAs that forward the stripe (kept for every step)
+  uint64_t timeout_ns = 0;
+  int rank = 0, left = -1, right = -1;
+};
+GICC_EXPORT int ring_mm_grid(int Ns, int push_ctas);
+GICC_EXPORT void ring_mm_step(const RingMmStep& a, cudaStream_t s);
+
 // ---- Jacobi (jacobi.cu) ---------------------------------------------------------------------
 struct JacobiStep {
   const float* a = nullptr;  // [rows+2][nx] read buffer

@@ -91,6 +91,7 @@ const char* where_name(int w) {
     case W_QUIET: return "quiet";
     case W_BOUNDS: return "bounds";
     case W_PINGPONG: return "pingpong";
+    case W_RING_MM: return "ring matmul";
   }
   return "?";
 }

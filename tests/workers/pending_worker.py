@@ -1,0 +1,88 @@
+"""Rank program for the multi-GPU checks of the options and kernels that have not yet run
+on a GPU (launched by opengda_b200.parallel.launch; one JSON result per rank):
+
+* the ring-stripe fp32 matmul (RingMatmul) against an fp64 product of the full matrices;
+* the fused all-gather GEMM with the copy-engine transfer (transfer="ce");
+* the reduce-scatter GEMM with the join option (rs_join);
+* the MoE layer with confined dispatch and the staged combine (dispatch_ctas, combine_ctas).
+"""
+import json
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+from opengda_b200.parallel import Bootstrap, Runtime  # noqa: E402
+
+
+def main():
+    out = sys.argv[1]
+    boot = Bootstrap.from_env()
+    rt = Runtime(boot)
+    r, n = rt.rank, rt.size
+    res = {"rank": r}
+
+    # 1. ring-stripe fp32 matmul, three calls (monotonic counters across calls)
+    from opengda_b200.models.ring_mm import RingMatmul, make_stripes
+    N = 1024
+    mm = RingMatmul(N, rt=rt, push_ctas=4)
+    worst = 0.0
+    for call in range(3):
+        A_s, B_s, A, B = make_stripes(N, n, r, seed=call)
+        C = mm(A_s, B_s).cpu().double()
+        Ns = N // n
+        ref = A[r * Ns:(r + 1) * Ns].double() @ B.double()
+        scale = A[r * Ns:(r + 1) * Ns].double().abs() @ B.double().abs()
+        worst = max(worst, float(((C - ref).abs() / scale).max()))
+    rt.check_device_errors()
+    res["ring_mm_err"] = worst
+
+    # 2. distributed GEMM options vs fp32
+    from opengda_b200.models.dist_gemm import DistGemm, make_operands
+    M = Nn = K = 2048
+    for name, mode, kw, attr in (("ag_ce", "ag", {"transfer": "ce"}, {}), ("rs_join", "rs", {}, {"rs_join": True})):
+        model = DistGemm(M, Nn, K, mode, rt=rt, fused=True, **kw)
+        for k, v in attr.items():
+            setattr(model, k, v)
+        worst = 0.0
+        for call in range(4):
+            A, B, (Af, Bf) = make_operands(M, Nn, K, mode, n, r, seed=2 + call)
+            C = model(A, B)
+            torch.cuda.synchronize()
+            full = Af.float() @ Bf.float().t()
+            ref = full[:, r * Nn // n:(r + 1) * Nn // n] if mode == "ag" else full[r * M // n:(r + 1) * M // n]
+            worst = max(worst, float(((C.float() - ref).norm() / ref.norm()).item()))
+        rt.check_device_errors()
+        res[f"gemm_{name}_relerr"] = worst
+
+    # 3. MoE with few dispatching CTAs and the staged combine
+    from opengda_b200.models.moe import MoELayer, make_inputs, reference_moe
+    T, H, E, k, I = 256, 512, 8 * n, 4, 256
+    layer = MoELayer(T, H, E, k, I, rt=rt, weight_std=0.05)
+    layer.dispatch_ctas = 8
+    layer.combine_ctas = 8
+    cat = lambda t: torch.cat([q.cuda() for q in boot.allgather_obj(t.cpu())])  # noqa: E731
+    wg, wu, w2 = cat(layer.w_gate), cat(layer.w_up), cat(layer.w2)
+    worst = 0.0
+    for call in range(3):
+        x, logits = make_inputs(T, H, E, r, seed=20 + call)
+        y = layer(x, logits)
+        torch.cuda.synchronize()
+        rows = torch.arange(0, T, 16, device="cuda")
+        ref = reference_moe(x, logits, k, wg, wu, w2, rows)
+        worst = max(worst, float(((y[rows].float() - ref).norm() / ref.norm()).item()))
+    rt.check_device_errors()
+    res["moe_confined_relerr"] = worst
+
+    boot.barrier()
+    with open(f"{out}.{r}", "w") as f:
+        json.dump(res, f)
+    del mm, layer
+    rt.finalize()
+
+
+if __name__ == "__main__":
+    main()
