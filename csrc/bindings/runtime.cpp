@@ -33,6 +33,20 @@ int litmus_run(uint64_t* shm, int rank, int test, int iters, int k, int use_fenc
 void bind_runtime(py::module_& m) {
   py::register_exception<gicc::BootstrapError>(m, "BootstrapError", PyExc_RuntimeError);
 
+  m.def("p2p_links", []() {
+    py::list out;
+    for (const auto& l : gicc::p2p_links()) {
+      py::dict d;
+      d["src"] = l.src;
+      d["dst"] = l.dst;
+      d["access"] = l.access;
+      d["native_atomics"] = l.native_atomics;
+      d["array_access"] = l.array_access;
+      d["perf_rank"] = l.perf_rank;
+      out.append(d);
+    }
+    return out;
+  }, "cudaDeviceGetP2PAttribute for every ordered pair of visible GPUs");
   m.def("check_exchange_consistency", &gicc::check_exchange_consistency, py::arg("boot"), py::arg("kinds"),
         py::arg("multicast"), py::call_guard<py::gil_scoped_release>(),
         "exchange()'s collective check of the newly registered buffer tables (no GPU needed)");

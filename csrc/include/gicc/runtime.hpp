@@ -128,6 +128,17 @@ class GICC_EXPORT Runtime {
   bool finalized_ = false;
 };
 
+// One ordered pair of visible GPUs and what cudaDeviceGetP2PAttribute reports for it.
+struct P2PLink {
+  int src = 0, dst = 0;
+  int access = 0;          // src can map dst's memory
+  int native_atomics = 0;  // atomics on dst's memory are native over the link
+  int array_access = 0;
+  int perf_rank = 0;       // the driver's relative rank (lower is faster)
+};
+// Every ordered pair of the GPUs visible to this process (no runtime needed).
+GICC_EXPORT std::vector<P2PLink> p2p_links();
+
 // The collective consistency check exchange() runs before any handle crosses a process
 // boundary: every rank registered the same number of buffers since the last exchange, with
 // the same kind and multicast flag, in the same order.  Throws BootstrapError

@@ -1,0 +1,74 @@
+"""Node topology probe: what the GPUs of this node report about one another.
+
+* ``p2p``: for every ordered pair of visible GPUs, cudaDeviceGetP2PAttribute's access,
+  native-atomics, CUDA-array and performance-rank values (native ``p2p_links``);
+* ``nvlink``: per GPU, how many NVLink links NVML reports active, and their version
+  (read-only NVML queries; skipped when NVML is not importable);
+* ``uniform``: True when every pair has access and native atomics with one performance rank
+  -- what an NVSwitch node reports, and what the runtime's peer mappings and signal atomics
+  assume.
+
+The runtime needs none of this (every peer of an NVSwitch node is equivalent); it is a
+sanity check to run on a new node.  ``python -m opengda_b200.utils.topology`` prints it as JSON.
+The NVML module and the P2P query are parameters so the logic is testable without a GPU.
+"""
+from __future__ import annotations
+
+import json
+from typing import Any, Callable, Dict, List, Optional
+
+NVLINK_MAX_LINKS = 18  # NVLink 5 on B200
+
+
+def _nvlink_state(nvml) -> List[Dict[str, Any]]:
+    out = []
+    nvml.nvmlInit()
+    try:
+        for i in range(nvml.nvmlDeviceGetCount()):
+            h = nvml.nvmlDeviceGetHandleByIndex(i)
+            name = nvml.nvmlDeviceGetName(h)
+            if isinstance(name, bytes):
+                name = name.decode()
+            active, versions = 0, set()
+            for link in range(NVLINK_MAX_LINKS):
+                try:
+                    if nvml.nvmlDeviceGetNvLinkState(h, link):
+                        active += 1
+                        try:
+                            versions.add(int(nvml.nvmlDeviceGetNvLinkVersion(h, link)))
+                        except Exception:  # version query unsupported: keep the count
+                            pass
+                except Exception:  # link index not present on this part
+                    break
+            out.append({"index": i, "name": name, "active_links": active, "versions": sorted(versions)})
+    finally:
+        nvml.nvmlShutdown()
+    return out
+
+
+def probe(nvml: Any = "import", p2p: Optional[Callable[[], List[Dict[str, int]]]] = None) -> Dict[str, Any]:
+    """The node's GPU peer matrix and NVLink state (see the module docstring)."""
+    if p2p is None:
+        from .. import native
+        p2p = native().p2p_links
+    links = list(p2p())
+    res: Dict[str, Any] = {"p2p": links}
+    if nvml == "import":
+        try:
+            import pynvml as nvml  # nvidia-ml-py
+        except ImportError:
+            nvml = None
+    res["nvlink"] = _nvlink_state(nvml) if nvml is not None else None
+    ranks = {l["perf_rank"] for l in links}
+    res["uniform"] = bool(links) and all(l["access"] and l["native_atomics"] for l in links) and len(ranks) == 1
+    missing = [(l["src"], l["dst"]) for l in links if not l["access"]]
+    res["pairs_without_access"] = missing
+    return res
+
+
+def main() -> None:
+    print(json.dumps(probe(), indent=1))
+
+
+if __name__ == "__main__":
+    main()
