@@ -27,6 +27,8 @@ def main():
     ap.add_argument("--iters", type=int, default=1000)
     ap.add_argument("--nccl-iters", type=int, default=None)
     ap.add_argument("--out", default=None)
+    ap.add_argument("--persistent", action="store_true",
+                    help="one cooperative launch for all iterations instead of one launch per iteration")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -42,7 +44,7 @@ def main():
     from opengda_b200.models.jacobi import Jacobi
     from opengda_b200.utils.timing import max_over_ranks
 
-    jac = Jacobi(args.nx, args.ny, rt=rt)
+    jac = Jacobi(args.nx, args.ny, rt=rt, persistent=args.persistent)
     jac.run(5)  # warm-up
     torch.cuda.synchronize()
     if world > 1:
@@ -56,7 +58,8 @@ def main():
     if rt:
         rt.check_device_errors()
     interior = (args.nx - 2) * (args.ny - 2)
-    res = {"metric": "jacobi_total_s", "impl": "ours-fused-halo-puts", "n_gpus": world, "nx": args.nx, "ny": args.ny,
+    res = {"metric": "jacobi_total_s", "impl": "ours-fused-halo-puts" + ("-persistent" if args.persistent else ""),
+           "n_gpus": world, "nx": args.nx, "ny": args.ny,
            "iters": args.iters, "total_s": ms / 1e3, "ms_per_iter": ms / args.iters,
            "GLUPs": interior * args.iters / (ms * 1e-3) / 1e9,
            "hbm_GBps_per_gpu": 8.0 * interior / world * args.iters / (ms * 1e-3) / 1e9}

@@ -219,6 +219,32 @@ void bind_runtime_objects(py::module_& m) {
   m.def("k_jacobi_init", [](uint64_t a, uint64_t b, int nx, int ny, int rows, int g0, uint64_t seed) {
     ops::jacobi_init(P<float>(a), P<float>(b), nx, ny, rows, g0, seed, cur_stream());
   });
+  m.def("jacobi_persistent_grid", &ops::jacobi_persistent_grid, py::arg("rows"));
+  m.def("k_jacobi_run", [](py::dict d) {
+    ops::JacobiRun r;
+    auto u64 = [&](const char* k) { return d.contains(k) ? d[k].cast<uint64_t>() : (uint64_t)0; };
+    auto two = [&](const char* k, int i) {
+      return d.contains(k) ? d[k].cast<std::vector<uint64_t>>().at(i) : (uint64_t)0;
+    };
+    for (int i = 0; i < 2; ++i) {
+      r.buf[i] = P<float>(two("buf", i));
+      r.top_dst[i] = P<float>(two("top_dst", i));
+      r.bot_dst[i] = P<float>(two("bot_dst", i));
+    }
+    r.nx = d["nx"].cast<int>();
+    r.rows = d["rows"].cast<int>();
+    r.top_sig_remote = P<uint64_t>(u64("top_sig_remote"));
+    r.bot_sig_remote = P<uint64_t>(u64("bot_sig_remote"));
+    r.top_flag = P<const uint64_t>(u64("top_flag"));
+    r.bot_flag = P<const uint64_t>(u64("bot_flag"));
+    r.iter0 = u64("iter0");
+    r.iters = d["iters"].cast<int>();
+    r.done = P<uint64_t>(u64("done"));
+    r.norm = P<double>(u64("norm"));
+    r.timeout_ns = u64("timeout_ns");
+    r.rank = d.contains("rank") ? d["rank"].cast<int>() : 0;
+    ops::jacobi_run(r, cur_stream());
+  });
   m.def("k_jacobi_step", [](uint64_t a, uint64_t b, int nx, int rows, uint64_t top_dst, uint64_t bot_dst,
                             uint64_t top_sig_remote, uint64_t bot_sig_remote, uint64_t top_flag, uint64_t bot_flag,
                             uint64_t wait_top, uint64_t wait_bot, uint64_t norm, uint64_t timeout_ns, int rank) {

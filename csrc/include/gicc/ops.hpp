@@ -103,6 +103,26 @@ struct JacobiStep {
 GICC_EXPORT void jacobi_init(float* a, float* b, int nx, int ny, int rows, int g0, uint64_t seed, cudaStream_t s);
 GICC_EXPORT void jacobi_step(const JacobiStep& st, cudaStream_t s);
 GICC_EXPORT int jacobi_ctas_per_row(int nx);
+// Many iterations in one cooperative launch (per-CTA row blocks, device-side dependencies
+// between neighbouring blocks; same halo counters as jacobi_step, so the two can be mixed).
+struct JacobiRun {
+  float* buf[2] = {nullptr, nullptr};  // [rows+2][nx]; global iteration gi reads buf[gi & 1]
+  int nx = 0, rows = 0;
+  float* top_dst[2] = {nullptr, nullptr};  // upper neighbour's bottom halo row in its buffer p
+  float* bot_dst[2] = {nullptr, nullptr};  // lower neighbour's top halo row in its buffer p
+  uint64_t* top_sig_remote = nullptr;
+  uint64_t* bot_sig_remote = nullptr;
+  const uint64_t* top_flag = nullptr;
+  const uint64_t* bot_flag = nullptr;
+  uint64_t iter0 = 0;         // global index of the first iteration (iterations done so far)
+  int iters = 0;
+  uint64_t* done = nullptr;   // [jacobi_persistent_grid(rows)] zeroed once, then monotonic
+  double* norm = nullptr;     // optional: sum of squared updates of the last iteration
+  uint64_t timeout_ns = 0;
+  int rank = 0;
+};
+GICC_EXPORT int jacobi_persistent_grid(int rows);
+GICC_EXPORT void jacobi_run(const JacobiRun& r, cudaStream_t s);
 
 // ---- distributed GEMM with fused NVLink transfers (gemm_dist.cu) ---------------------------
 // Pointer arrays are indexed by rank and hold this process's view of each rank's buffer.

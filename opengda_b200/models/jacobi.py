@@ -27,7 +27,13 @@ def split_rows(ny: int, world: int, rank: int):
 
 
 class Jacobi:
-    def __init__(self, nx: int, ny: int, rt=None, seed: int = 3, device: Optional[torch.device] = None):
+    """``persistent=True`` runs ``run(iters)`` as one cooperative launch (``k_jacobi_persistent``:
+    each CTA owns a block of rows and waits on device for its neighbouring blocks and, at the
+    ends, for the neighbour ranks' halo rows) instead of one launch per iteration; both use
+    the same buffers and counters, so ``step()`` and ``run()`` can be mixed."""
+
+    def __init__(self, nx: int, ny: int, rt=None, seed: int = 3, device: Optional[torch.device] = None,
+                 persistent: bool = False):
         if nx % 4:
             raise ValueError("nx must be a multiple of 4")
         self.nx, self.ny, self.seed = nx, ny, seed
@@ -53,6 +59,10 @@ class Jacobi:
         self.done = 0  # iterations completed (same count on every rank)
         native().k_jacobi_init(self.bufs[0].data_ptr(), self.bufs[1].data_ptr(), nx, ny, self.rows, self.g0, seed)
         self.norm_buf = torch.zeros(1, dtype=torch.float64, device=self.device)
+        self.persistent = persistent
+        if persistent:
+            grid = native().jacobi_persistent_grid(self.rows)
+            self.done_ctr = torch.zeros(grid, dtype=torch.int64, device=self.device)
 
     def step(self, norm: bool = False) -> None:
         a, b = self.bufs[self.cur], self.bufs[1 - self.cur]
@@ -76,9 +86,31 @@ class Jacobi:
         self.cur ^= 1
         self.done += 1
 
+    def _run_persistent(self, iters: int, norm: bool) -> None:
+        d = {"buf": [b.data_ptr() for b in self.bufs], "nx": self.nx, "rows": self.rows, "iter0": self.done,
+             "iters": iters, "done": self.done_ctr.data_ptr(), "norm": self.norm_buf.data_ptr() if norm else 0,
+             "rank": self.rank, "timeout_ns": self.rt.timeout_ns if self.rt is not None else 0}
+        if self.world > 1:
+            r, nx, rt = self.rank, self.nx, self.rt
+            if r > 0:  # my first row -> upper neighbour's bottom halo, in its buffer of either parity
+                d["top_dst"] = [self.sym[q].ptr(r - 1) + (self.nrows[r - 1] + 1) * nx * 4 for q in range(2)]
+                d["top_sig_remote"] = rt.signal_peer(r - 1, self.flag_off + 1)
+                d["top_flag"] = rt.signal_local(self.flag_off)
+            if r < self.world - 1:  # my last row -> lower neighbour's top halo (row 0)
+                d["bot_dst"] = [self.sym[q].ptr(r + 1) for q in range(2)]
+                d["bot_sig_remote"] = rt.signal_peer(r + 1, self.flag_off)
+                d["bot_flag"] = rt.signal_local(self.flag_off + 1)
+        native().k_jacobi_run(d)
+        self.done += iters
+        self.cur = self.done & 1
+
     def run(self, iters: int, norm_last: bool = False) -> Optional[float]:
         """Run `iters` iterations; optionally return the global L2 norm of the last update."""
-        for i in range(iters):
+        if self.persistent and iters > 0:
+            if norm_last:
+                self.norm_buf.zero_()
+            self._run_persistent(iters, norm_last)
+        for i in range(0 if self.persistent else iters):
             want = norm_last and i == iters - 1
             if want:
                 self.norm_buf.zero_()

@@ -1,7 +1,7 @@
 """GPU checks of kernels and options that compile and whose host logic is tested on CPU,
 but that have not yet run on a GPU: the ring-stripe fp32 matmul (one GPU and a ring of
 ranks), the copy-engine all-gather GEMM, the reduce-scatter join, and the MoE layer with
-confined dispatch and staged combine.  They run only with GICC_TEST_NOT_YET_RUN=1; once a
+confined dispatch and staged combine, and the persistent Jacobi kernel.  They run only with GICC_TEST_NOT_YET_RUN=1; once a
 check has passed on a B200 it moves into the regular GPU suites."""
 import json
 import os
@@ -32,6 +32,24 @@ def test_ring_mm_single_gpu_matches_fp64():
         assert err < 2e-5, (call, err)
 
 
+def test_jacobi_persistent_single_gpu_bit_exact():
+    """One cooperative launch for many iterations, mixed with per-iteration launches, gives
+    the CPU oracle's field bit for bit."""
+    import numpy as np
+    import torch
+    from opengda_b200.models.jacobi import Jacobi, jacobi_np
+    from opengda_b200.ops.gemm import check_errors
+    nx, ny = 2048, 300
+    jac = Jacobi(nx, ny, persistent=True)
+    jac.run(7)
+    jac.step()
+    jac.run(12)
+    torch.cuda.synchronize()
+    check_errors()
+    ref = jacobi_np(nx, ny, 20)[1:-1]
+    assert int((jac.owned().cpu().numpy() != ref).sum()) == 0
+
+
 @pytest.mark.multigpu
 def test_pending_options_multigpu(tmp_path):
     import torch
@@ -48,3 +66,4 @@ def test_pending_options_multigpu(tmp_path):
         assert r["ring_mm_err"] < 2e-5, r
         assert r["gemm_ag_ce_relerr"] < 1e-2 and r["gemm_rs_join_relerr"] < 1e-2, r
         assert r["moe_confined_relerr"] < 2e-2, r
+        assert r["jacobi_persistent_mismatch"] == 0, r

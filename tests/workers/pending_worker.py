@@ -4,7 +4,8 @@ on a GPU (launched by opengda_b200.parallel.launch; one JSON result per rank):
 * the ring-stripe fp32 matmul (RingMatmul) against an fp64 product of the full matrices;
 * the fused all-gather GEMM with the copy-engine transfer (transfer="ce");
 * the reduce-scatter GEMM with the join option (rs_join);
-* the MoE layer with confined dispatch and the staged combine (dispatch_ctas, combine_ctas).
+* the MoE layer with confined dispatch and the staged combine (dispatch_ctas, combine_ctas);
+* the persistent Jacobi kernel (one cooperative launch for many iterations).
 """
 import json
 import os
@@ -76,6 +77,20 @@ def main():
         worst = max(worst, float(((y[rows].float() - ref).norm() / ref.norm()).item()))
     rt.check_device_errors()
     res["moe_confined_relerr"] = worst
+
+    # 4. persistent Jacobi (one cooperative launch per run), mixed with per-iteration steps,
+    #    against the CPU oracle (bit-exact)
+    import numpy as np
+    from opengda_b200.models.jacobi import Jacobi, jacobi_np
+    jnx, jny = 1024, 4 * n + 70
+    jac = Jacobi(jnx, jny, rt=rt, persistent=True)
+    jac.run(9)
+    jac.step()
+    jac.run(15)
+    torch.cuda.synchronize()
+    rt.check_device_errors()
+    field = np.concatenate(boot.allgather_obj(jac.owned().cpu().numpy()), axis=0)
+    res["jacobi_persistent_mismatch"] = int((field != jacobi_np(jnx, jny, 25)[1:-1]).sum())
 
     boot.barrier()
     with open(f"{out}.{r}", "w") as f:
