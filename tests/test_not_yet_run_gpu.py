@@ -67,3 +67,23 @@ def test_pending_options_multigpu(tmp_path):
         assert r["gemm_ag_ce_relerr"] < 1e-2 and r["gemm_rs_join_relerr"] < 1e-2, r
         assert r["moe_confined_relerr"] < 2e-2, r
         assert r["jacobi_persistent_mismatch"] == 0, r
+
+
+@pytest.mark.parametrize("all_gpus", [False, True])
+def test_native_gicc_mm_fp32_ring_exact(all_gpus):
+    """The native example's -ring mode (the reference's fp32 ring algorithm through the C++
+    API) reproduces the exact product on sampled elements."""
+    import subprocess
+    import torch
+    from opengda_b200.parallel.launch import free_port
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    n = min(torch.cuda.device_count(), 8) if all_gpus else 1
+    if all_gpus and n < 2:
+        pytest.skip("needs 2 GPUs")
+    cmd = [sys.executable, "-m", "opengda_b200.parallel.launch", "-n", str(n), "--port", str(free_port()),
+           "--timeout", "120", os.path.join(root, "opengda_b200", "bin", "gicc_mm"), "-ring", "-n", "2048",
+           "-iters", "3", "-samples", "64"]
+    p = subprocess.run(cmd, cwd=root, capture_output=True, text=True, timeout=180,
+                       env=dict(os.environ, GICC_TIMEOUT_MS="5000"))
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert "PASS" in p.stdout
