@@ -195,26 +195,50 @@ __global__ void __launch_bounds__(256) k_plan(PlanArgs a) {
     rows_s[e] = rows;
     a.expert_rows[e] = rows;
   }
+  __shared__ int cnt_s[1024];  // this rank's pair counts per global expert (E <= 1024)
+  for (int g = t; g < E; g += blockDim.x) cnt_s[g] = a.counts[g];
   __syncthreads();
-  if (t == 0) {
-    int base = 0, mb = 0;
-    for (int e = 0; e < El; ++e) {
-      a.expert_base[e] = base;
-      a.mblk_prefix[e] = mb;
-      base += pad128(rows_s[e]);
-      mb += pad128(rows_s[e]) / 128;
-    }
-    a.mblk_prefix[El] = mb;
-    // (5) send order: key = e * n + j, j = (r - d) mod n  (local first, then r-1, r-2, ...)
-    int off = 0;
-    for (int e = 0; e < El; ++e)
-      for (int j = 0; j < n; ++j) {
-        const int d = (r - j + n) % n;
-        a.key_base[e * n + j] = off;
-        off += a.counts[d * El + e];
+  // (5) prefix sums by warp 0 (each lane scans a contiguous range from shared memory, then
+  // one shuffle scan over the lanes' totals): expert bases / m-block prefix over my experts,
+  // and the send-list offsets over keys e * n + j, j = (r - d) mod n (local first, then
+  // r-1, r-2, ...).
+  if (t < 32) {
+    const unsigned full = 0xffffffffu;
+    auto excl_scan = [&](int v, int* total) {
+      int incl = v;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(full, incl, o);
+        if (t >= o) incl += u;
       }
-    a.key_base[El * n] = off;
-    *a.cum_pairs += (uint64_t)a.pairs;
+      *total = __shfl_sync(full, incl, 31);
+      return incl - v;
+    };
+    const int pe = (El + 31) / 32, e0 = min(t * pe, El), e1 = min(e0 + pe, El);
+    int sum = 0, total = 0;
+    for (int e = e0; e < e1; ++e) sum += pad128(rows_s[e]);
+    int base = excl_scan(sum, &total);
+    for (int e = e0; e < e1; ++e) {
+      a.expert_base[e] = base;
+      a.mblk_prefix[e] = base / 128;  // every segment is a multiple of 128 rows
+      base += pad128(rows_s[e]);
+    }
+    if (t == 0) a.mblk_prefix[El] = total / 128;
+    const int K = El * n, pk = (K + 31) / 32, k0 = min(t * pk, K), k1 = min(k0 + pk, K);
+    auto key_count = [&](int key) {
+      const int e = key / n, j = key - e * n, d = (r - j + n) % n;
+      return cnt_s[d * El + e];
+    };
+    sum = 0;
+    for (int k = k0; k < k1; ++k) sum += key_count(k);
+    int off = excl_scan(sum, &total);
+    for (int k = k0; k < k1; ++k) {
+      a.key_base[k] = off;
+      off += key_count(k);
+    }
+    if (t == 0) {
+      a.key_base[K] = total;
+      *a.cum_pairs += (uint64_t)a.pairs;
+    }
   }
   for (int i = t; i < El * n; i += blockDim.x) a.key_cursor[i] = 0;
 }
@@ -743,7 +767,8 @@ void moe_forward(const MoeArgs& a, cudaStream_t s) {
   using namespace gemm;
   const int n = a.n, r = a.r, El = a.E / a.n;
   if (n < 1 || n > moe::kMaxR) throw std::runtime_error("gicc::moe: 1..8 ranks");
-  if (a.E % n || El > moe::kMaxLocalExperts) throw std::runtime_error("gicc::moe: E must split evenly, <= 256 per rank");
+  if (a.E % n || El > moe::kMaxLocalExperts || a.E > 1024)
+    throw std::runtime_error("gicc::moe: E <= 1024 must split evenly, <= 256 per rank");
   if (a.H % 256 || a.I % 128 || a.H % BK || a.I % BK) throw std::runtime_error("gicc::moe: hidden % 256, inter % 128");
   const int pairs = a.T * a.topk;
   ErrorRecord* err = device_error_record();
