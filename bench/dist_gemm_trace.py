@@ -106,6 +106,7 @@ def main() -> int:
     ap.add_argument("--mode", default="ag", choices=["ag", "rs"], help="rs: the NVLS reduce-scatter kernel")
     ap.add_argument("--transfer", default="sm", choices=["sm", "ce"], help="ag: SM pushes or copy engines")
     ap.add_argument("--join", action="store_true", help="rs: CTAs out of GEMM tiles join the reduction")
+    ap.add_argument("--raster-group", type=int, default=0, help="rs: m-blocks per raster group (0 = 16)")
     args = ap.parse_args()
 
     import numpy as np
@@ -135,6 +136,7 @@ def main() -> int:
         raise SystemExit("the trace covers the NVLS reduce-scatter kernel only")
     m.units_per_band = args.units
     m.rs_join = bool(args.join)
+    m.rs_raster_group = args.raster_group
     if args.comm_ctas:
         if args.mode == "ag":
             m.comm_ctas = args.comm_ctas
@@ -178,6 +180,7 @@ def main() -> int:
         print(json.dumps({
             "kernel": "k_ag_gemm" if args.mode == "ag" else "k_gemm_rs_nvls", "n_gpus": world, "M": M, "N": N,
             "K": K, "nvls": m.nvls, "comm_ctas": m.comm_ctas if args.mode == "ag" else m.rs_reduce_ctas,
+            "raster_group": args.raster_group,
             "units_per_band": m.units_per_band,
             "ms_per_call_max_over_ranks": round(ms, 4), "tflops": round(2.0 * M * N * K / ms / 1e9, 1),
             "relerr_vs_fp32": rel, "per_rank_trace": allsum}))

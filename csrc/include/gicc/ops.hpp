@@ -173,6 +173,9 @@ struct GemmRsArgs {
   uint64_t* trace = nullptr;   // NVLS mode diagnostics: %globaltimer stamps (layout at RsNvSched)
   int join_reduce = 0;         // NVLS: CTAs that finished their GEMM tiles join the reduction
   uint64_t* unit_counter = nullptr;  // NVLS + join_reduce: local word, zero before the first call
+  int raster_group = 0;        // NVLS: m-blocks per raster group (0 = 16).  Smaller groups finish
+                               // bands sooner (the owners can reduce them earlier); larger
+                               // ones reuse B better in L2 when B does not fit there
 };
 // Memory-model litmus tests (gicc/proto/litmus.hpp).  test 0 = MP (role 0 writes data and
 // flag into role 1's memory; role 1 checks), test 1 = SB (each role stores into the other's

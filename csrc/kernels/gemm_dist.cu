@@ -500,6 +500,7 @@ struct RsNvSched {
   int join;
   unsigned long long* unit_counter;
   unsigned long long unit_base;
+  int group;  // m-blocks per raster group
 
   __device__ int num_tiles() const { return n * nbo * num_n; }
   __device__ int num_units() const { return nbo * Q; }
@@ -517,7 +518,7 @@ struct RsNvSched {
   }
   __device__ TileInfo tile(int t) const {
     int vm, nbk;
-    raster(t, nbo * n, num_n, 16, vm, nbk);
+    raster(t, nbo * n, num_n, group, vm, nbk);
     const int b = vm / n, o = vm - b * n;
     TileInfo ti;
     ti.m0 = o * Mr + b * BM;
@@ -815,6 +816,7 @@ void gemm_rs(const GemmRsArgs& a, cudaStream_t s) {
     if (sc.join && !a.unit_counter) throw std::runtime_error("gicc::gemm_rs (NVLS): join_reduce needs unit_counter");
     sc.unit_counter = reinterpret_cast<unsigned long long*>(a.unit_counter);
     sc.unit_base = (unsigned long long)(a.epoch - 1) * (unsigned long long)(sc.nbo * Q + G);
+    sc.group = a.raster_group > 0 ? a.raster_group : 16;
     RsNvEpi e{};
     e.trace_epi = a.trace;  // first T words
     e.N = a.N; e.nbo = sc.nbo; e.num_n = sc.num_n;

@@ -61,6 +61,10 @@ class DistGemm:
         self.comm_ctas = (16 if w >= 8 else 8) if self.nvls else 32
         self.rs_reduce_ctas = 16  # RS over NVLS: CTAs whose reduce warps run multimem.ld_reduce
         self.rs_join = False      # RS over NVLS: CTAs out of GEMM tiles join the reduction (A/B option)
+        # RS over NVLS: m-blocks per raster group (0 = 16).  A band can be reduced once all its
+        # column tiles are done, so smaller groups feed the reduction sooner; when B fits in L2
+        # (small K shards) they cost no extra DRAM traffic.  A/B option.
+        self.rs_raster_group = 0
         self.trace: Optional[torch.Tensor] = None
         self.diag = 0
         if w > 1 and fused:
@@ -207,7 +211,7 @@ class DistGemm:
                                 C.stride(0), self.epoch, self.grid, self.rt.timeout_ns, buf.mc_ptr, self.band_tiles,
                                 self.tile_counter, self.rs_reduce_ctas, self.units_per_band,
                                 self.trace.data_ptr() if self.trace is not None else 0, int(self.rs_join),
-                                self.unit_counter)
+                                self.unit_counter, self.rs_raster_group)
                 else:
                     n.k_gemm_rs(w, r, self.M, self.N, self.K // w, A.data_ptr(), A.stride(0), B.data_ptr(),
                                 B.stride(0), [buf.ptr(q) for q in range(w)], self.arrivals, self.done, C.data_ptr(),
