@@ -95,6 +95,9 @@ struct PlainSched {
   int M, N, K;
   int bn;
   int num_m, num_n, group_m;
+  // L2 eviction priority of the operand loads: 0 = none (default), 1 = A kept / B streamed
+  // (A's m-blocks are reused by every column tile of a raster group), 2 = the reverse.
+  int l2hint = 0;
   __device__ int num_tiles() const { return num_m * num_n; }
   __device__ TileInfo tile(int t) const {
     int mb, nb;
@@ -114,8 +117,14 @@ struct PlainSched {
   __device__ bool producer_wait(const TileInfo&, uint64_t, volatile int*, ErrorRecord*) const { return true; }
   __device__ void issue_loads(const TileInfo& ti, int kb, void* sA, void* sB, uint64_t* bar, const CUtensorMap* tmA,
                               const CUtensorMap* tmB) const {
-    ptx::tma_load_2d(sA, tmA, bar, kb * BK, ti.a_row);
-    ptx::tma_load_2d(sB, tmB, bar, kb * BK, ti.b_row);
+    if (l2hint == 0) {
+      ptx::tma_load_2d(sA, tmA, bar, kb * BK, ti.a_row);
+      ptx::tma_load_2d(sB, tmB, bar, kb * BK, ti.b_row);
+    } else {
+      const uint64_t keep = ptx::l2_policy_evict_last(), stream = ptx::l2_policy_evict_first();
+      ptx::tma_load_2d_hint(sA, tmA, bar, kb * BK, ti.a_row, l2hint == 1 ? keep : stream);
+      ptx::tma_load_2d_hint(sB, tmB, bar, kb * BK, ti.b_row, l2hint == 1 ? stream : keep);
+    }
   }
   __device__ void comm(int, int, volatile int*, ErrorRecord*, uint64_t) const {}
 };

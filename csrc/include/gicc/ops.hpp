@@ -15,6 +15,15 @@ namespace ops {
 // bn selects the tile width (0 = default 256).
 GICC_EXPORT void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
                            long long ldc, bool out_f32, float alpha, int bn, cudaStream_t stream);
+// Process-wide tuning of gemm_bf16's 1-CTA kernel (A/B experiments; the defaults are the
+// measured configuration): m-blocks per raster group and the L2 eviction hints of the
+// operand loads (0 none, 1 keep A / stream B, 2 keep B / stream A).
+struct GemmTuning {
+  int group_m = 16;
+  int l2_hint = 0;
+};
+GICC_EXPORT void set_gemm_tuning(const GemmTuning& t);
+GICC_EXPORT GemmTuning gemm_tuning();
 // Self-test of the GEMM core's tile-done ordering: counters must hold 2*tiles+1 zeroed
 // words ([warps finished per tile][times published per tile][violations]).
 GICC_EXPORT void gemm_tile_done_selftest(const void* A, const void* B, int M, int N, int K, uint32_t* counters,

@@ -84,7 +84,9 @@ static void launch_plain(const void* A, const void* B, void* C, int M, int N, in
   s.bn = BN;
   s.num_m = (M + BM - 1) / BM;
   s.num_n = (N + BN - 1) / BN;
-  s.group_m = 16;
+  const ops::GemmTuning tune = ops::gemm_tuning();
+  s.group_m = tune.group_m;
+  s.l2hint = tune.l2_hint;
   StoreEpi e;
   e.C = C;
   e.ldc = ldc;
@@ -245,6 +247,16 @@ void gemm_tile_done_selftest(const void* A, const void* B, int M, int N, int K, 
   GICC_CUDA(cudaGetLastError());
 }
 
+
+namespace {
+GemmTuning g_tuning;
+}
+void set_gemm_tuning(const GemmTuning& t) {
+  if (t.group_m < 1 || t.l2_hint < 0 || t.l2_hint > 2)
+    throw std::runtime_error("gicc::set_gemm_tuning: group_m >= 1, l2_hint in 0..2");
+  g_tuning = t;
+}
+GemmTuning gemm_tuning() { return g_tuning; }
 
 void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
                long long ldc, bool out_f32, float alpha, int bn, cudaStream_t stream) {

@@ -18,6 +18,17 @@ def gemm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = None, alph
     return native().gemm(A, B, out, float(alpha), out_dtype == torch.float32, int(bn))
 
 
+def set_tuning(group_m: int = 16, l2_hint: int = 0) -> None:
+    """Process-wide tuning of ``gemm`` (A/B experiments; the defaults are the measured
+    configuration): m-blocks per raster group, and L2 eviction hints on the operand loads
+    (0 none, 1 keep A / stream B, 2 keep B / stream A)."""
+    native().set_gemm_tuning(int(group_m), int(l2_hint))
+
+
+def tuning() -> dict:
+    return dict(native().gemm_tuning())
+
+
 def check_errors(clear: bool = True) -> None:
     """Raise if a kernel of this library recorded a device-side error (timeout, bounds)."""
     rec = native().read_errors(clear)

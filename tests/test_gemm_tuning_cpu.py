@@ -1,0 +1,18 @@
+"""The GEMM tuning knobs (raster group, L2 hints) are validated and restored on the host."""
+import pytest
+
+from opengda_b200.ops.gemm import set_tuning, tuning
+
+
+def test_tuning_roundtrip_and_validation():
+    assert tuning() == {"group_m": 16, "l2_hint": 0}
+    try:
+        set_tuning(group_m=8, l2_hint=2)
+        assert tuning() == {"group_m": 8, "l2_hint": 2}
+        for bad in ({"group_m": 0}, {"l2_hint": 3}, {"l2_hint": -1}):
+            with pytest.raises(RuntimeError):
+                set_tuning(**bad)
+        assert tuning() == {"group_m": 8, "l2_hint": 2}  # a rejected call changes nothing
+    finally:
+        set_tuning()
+    assert tuning() == {"group_m": 16, "l2_hint": 0}
