@@ -58,7 +58,11 @@ def probe(nvml: Any = "import", p2p: Optional[Callable[[], List[Dict[str, int]]]
             import pynvml as nvml  # nvidia-ml-py
         except ImportError:
             nvml = None
-    res["nvlink"] = _nvlink_state(nvml) if nvml is not None else None
+    try:
+        res["nvlink"] = _nvlink_state(nvml) if nvml is not None else None
+    except Exception as e:  # NVML present but not usable here (driver or permissions)
+        res["nvlink"] = None
+        res["nvml_error"] = f"{type(e).__name__}: {e}"
     ranks = {l["perf_rank"] for l in links}
     res["uniform"] = bool(links) and all(l["access"] and l["native_atomics"] for l in links) and len(ranks) == 1
     missing = [(l["src"], l["dst"]) for l in links if not l["access"]]

@@ -52,6 +52,14 @@ def test_non_uniform_and_missing_access_are_reported():
     assert not res["uniform"] and res["pairs_without_access"] == [(0, 1), (1, 0)]
 
 
+def test_unusable_nvml_is_reported_not_raised():
+    class Broken(FakeNvml):
+        def nvmlInit(self):
+            raise RuntimeError("no permission")
+    res = probe(nvml=Broken([18]), p2p=_pairs(2))
+    assert res["nvlink"] is None and "no permission" in res["nvml_error"] and res["uniform"]
+
+
 def test_single_gpu_is_not_called_uniform():
     assert probe(nvml=None, p2p=_pairs(1))["uniform"] is False
 
