@@ -104,3 +104,18 @@ def test_native_put_bw_two_ranks():
                        env=dict(os.environ, GICC_TIMEOUT_MS="5000"))
     assert p.returncode == 0, p.stdout + p.stderr
     assert p.stdout.strip().endswith("PASS") and ",FAIL" not in p.stdout
+
+
+def test_native_am_pingpong_two_ranks():
+    import subprocess
+    import torch
+    from opengda_b200.parallel.launch import free_port
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cmd = [sys.executable, "-m", "opengda_b200.parallel.launch", "-n", "2", "--port", str(free_port()),
+           "--timeout", "120", os.path.join(root, "opengda_b200", "bin", "gicc_am_pingpong"), "20", "2"]
+    p = subprocess.run(cmd, cwd=root, capture_output=True, text=True, timeout=180,
+                       env=dict(os.environ, GICC_TIMEOUT_MS="5000"))
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert "request/reply" in p.stdout and "request/request" in p.stdout
