@@ -70,8 +70,60 @@ def probe(nvml: Any = "import", p2p: Optional[Callable[[], List[Dict[str, int]]]
     return res
 
 
+def environment() -> Dict[str, Any]:
+    """Versions of what this package runs on (the reference's scripts check their module
+    environment the same way before a run): Python, torch and its CUDA / NCCL, the driver
+    (NVML), nvcc, the visible GPUs and whether the native library loads."""
+    import platform
+    import shutil
+    import subprocess
+
+    env: Dict[str, Any] = {"python": platform.python_version()}
+    try:
+        import torch
+        env["torch"] = torch.__version__
+        env["torch_cuda"] = torch.version.cuda
+        env["cuda_available"] = torch.cuda.is_available()
+        if torch.cuda.is_available():
+            env["gpus"] = [torch.cuda.get_device_name(i) for i in range(torch.cuda.device_count())]
+            try:
+                env["nccl"] = ".".join(map(str, torch.cuda.nccl.version()))
+            except Exception as e:  # NCCL not bundled
+                env["nccl"] = f"unavailable: {e}"
+    except ImportError:
+        env["torch"] = None
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            v = pynvml.nvmlSystemGetDriverVersion()
+            env["driver"] = v.decode() if isinstance(v, bytes) else v
+        finally:
+            pynvml.nvmlShutdown()
+    except Exception as e:
+        env["driver"] = f"unavailable: {type(e).__name__}"
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    try:
+        out = subprocess.run([nvcc, "--version"], capture_output=True, text=True, timeout=30).stdout
+        env["nvcc"] = out.strip().splitlines()[-1] if out.strip() else None
+    except (OSError, subprocess.SubprocessError):
+        env["nvcc"] = None
+    try:
+        from .. import native
+        native()
+        env["native_library"] = "loaded"
+    except Exception as e:
+        env["native_library"] = f"not loadable: {e}"
+    return env
+
+
 def main() -> None:
-    print(json.dumps(probe(), indent=1))
+    res: Dict[str, Any] = {"environment": environment()}
+    try:
+        res["topology"] = probe()
+    except Exception as e:  # no GPU here
+        res["topology"] = f"unavailable: {type(e).__name__}: {e}"
+    print(json.dumps(res, indent=1))
 
 
 if __name__ == "__main__":

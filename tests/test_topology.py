@@ -77,3 +77,9 @@ def test_probe_on_this_node():
         assert res["uniform"], res  # an NVSwitch node: every pair equal
     if res["nvlink"] is not None:
         assert len(res["nvlink"]) >= n
+
+
+def test_environment_summary_runs_without_gpu():
+    from opengda_b200.utils.topology import environment
+    env = environment()
+    assert env["python"] and env["native_library"] == "loaded"
