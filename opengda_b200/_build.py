@@ -57,7 +57,7 @@ def _ninja_file(debug_checks: bool) -> str:
     checks = " -DGICC_CHECKS=1" if debug_checks else ""
     nvflags = (
         f"-std=c++17 -O3 {' '.join(ARCH)} -lineinfo -Xcompiler -fPIC,-fvisibility=hidden "
-        f"--expt-relaxed-constexpr -Xptxas -v {inc}{checks}"
+        f"--expt-relaxed-constexpr -diag-suppress=177 -Xptxas -v {inc}{checks}"
     )
     cxxflags = f"-std=c++17 -O2 -fPIC -fvisibility=hidden -Wall -Wno-unused-function {inc}{checks}"
     tcflags, tldflags = _torch_flags()
