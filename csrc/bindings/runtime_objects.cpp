@@ -205,7 +205,7 @@ void bind_runtime_objects(py::module_& m) {
   m.def("k_allreduce_bf16", [](int algo, std::vector<uint64_t> in, std::vector<uint64_t> out, uint64_t mc_in,
                                uint64_t mc_out, int n, int me, size_t count, float scale, bool out_f32,
                                std::vector<uint64_t> flags, int max_blocks, uint64_t epoch, uint64_t timeout_ns,
-                               int blocks) {
+                               int blocks, uint64_t epoch_dev, uint64_t ticket) {
     std::vector<const void*> ip;
     std::vector<void*> op;
     std::vector<uint64_t*> fp;
@@ -214,8 +214,10 @@ void bind_runtime_objects(py::module_& m) {
     for (auto a : flags) fp.push_back(P<uint64_t>(a));
     ops::allreduce_bf16(algo, ip.empty() ? nullptr : ip.data(), op.empty() ? nullptr : op.data(), P<const void>(mc_in),
                         P<void>(mc_out), n, me, count, scale, out_f32, fp.data(), max_blocks, epoch, timeout_ns, blocks,
-                        cur_stream());
-  });
+                        cur_stream(), P<uint64_t>(epoch_dev), P<unsigned int>(ticket));
+  }, py::arg("algo"), py::arg("in_ptrs"), py::arg("out_ptrs"), py::arg("mc_in"), py::arg("mc_out"), py::arg("n"),
+     py::arg("me"), py::arg("count"), py::arg("scale"), py::arg("out_f32"), py::arg("flags"), py::arg("max_blocks"),
+     py::arg("epoch"), py::arg("timeout_ns"), py::arg("blocks"), py::arg("epoch_dev") = 0, py::arg("ticket") = 0);
   m.def("k_jacobi_init", [](uint64_t a, uint64_t b, int nx, int ny, int rows, int g0, uint64_t seed) {
     ops::jacobi_init(P<float>(a), P<float>(b), nx, ny, rows, g0, seed, cur_stream());
   });

@@ -61,9 +61,13 @@ GICC_EXPORT void reduce_bf16(const void* const* srcs, int nsrc, void* out, size_
 // Allreduce of `count` bf16 elements held in symmetric memory.  in/out: per-rank addresses
 // (this process's view); mc_in/mc_out: multicast addresses (NVLS only); flag_bases: per-rank
 // base of a [2][max_blocks][n] signal-word area; epoch: call counter (same on all ranks).
+// With epoch_dev (a local word, zero before the first call) and ticket (a local 32-bit word,
+// zero), the epoch is kept on the device instead: each call uses *epoch_dev + 1 and stores it
+// back when its last CTA finishes, so the call can be captured in a CUDA graph and replayed.
 GICC_EXPORT void allreduce_bf16(int algo, const void* const* in, void* const* out, const void* mc_in, void* mc_out,
                                 int n, int me, size_t count, float scale, bool out_f32, uint64_t* const* flag_bases,
-                                int max_blocks, uint64_t epoch, uint64_t timeout_ns, int blocks, cudaStream_t s);
+                                int max_blocks, uint64_t epoch, uint64_t timeout_ns, int blocks, cudaStream_t s,
+                                uint64_t* epoch_dev = nullptr, unsigned int* ticket = nullptr);
 
 // ---- ring-stripe fp32 matmul (ring_mm.cu) -----------------------------------------------------
 // One step of C_s = A_s . B over a ring of n ranks: A_s [Ns][N] (my rows), B stripes [N][Ns]

@@ -36,6 +36,29 @@ struct PeerOut {
 struct FlagPtrs {
   uint64_t* p[kMaxRanks];  // each rank's flag area base (this rank's view)
 };
+// Where a call's epoch comes from.  dev == null: the host passes it (value).  Otherwise the
+// epoch is *dev + 1, read by every CTA at its start, and the last CTA to finish stores it
+// back (and re-arms the ticket): a captured CUDA graph then uses a new epoch on every replay.
+struct EpochRef {
+  uint64_t value;
+  uint64_t* dev;
+  unsigned int* ticket;
+};
+
+__device__ __forceinline__ uint64_t call_epoch(const EpochRef& e) {
+  __shared__ uint64_t ep;
+  if (threadIdx.x == 0) ep = e.dev ? *reinterpret_cast<volatile uint64_t*>(e.dev) + 1 : e.value;
+  __syncthreads();
+  return ep;
+}
+__device__ __forceinline__ void finish_epoch(const EpochRef& e, uint64_t ep) {
+  if (!e.dev) return;
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(e.ticket, 1u) + 1 == gridDim.x) {
+    *e.ticket = 0;  // every CTA of this call has counted; the next call starts after this kernel
+    *reinterpret_cast<volatile uint64_t*>(e.dev) = ep;
+  }
+}
 
 __device__ __forceinline__ void add_bf16x8(float* acc, const uint4& v) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -117,25 +140,31 @@ __device__ __forceinline__ void reduce_range(const PeerPtrs& in, int n, size_t l
 // One-shot: every rank reads all inputs and writes the whole result locally.
 __global__ void __launch_bounds__(256) k_allreduce_oneshot(PeerPtrs in, void* out, size_t nvec, int n, int me,
                                                            float scale, int out_f32, FlagPtrs flags, int max_blocks,
-                                                           uint64_t epoch, uint64_t timeout_ns, ErrorRecord* err) {
-  if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) != GICC_OK) return;
-  reduce_range(in, n, 0, nvec, [&](size_t v, const float* acc) { store8(out, v, acc, scale, out_f32); });
-  cta_handshake(flags, n, me, 1, max_blocks, epoch, timeout_ns, err);
+                                                           EpochRef er, uint64_t timeout_ns, ErrorRecord* err) {
+  const uint64_t epoch = call_epoch(er);
+  if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) == GICC_OK) {
+    reduce_range(in, n, 0, nvec, [&](size_t v, const float* acc) { store8(out, v, acc, scale, out_f32); });
+    cta_handshake(flags, n, me, 1, max_blocks, epoch, timeout_ns, err);
+  }
+  finish_epoch(er, epoch);
 }
 
 // Two-shot: rank r reduces chunk r from all inputs and pushes it into every rank's output.
 __global__ void __launch_bounds__(256) k_allreduce_twoshot(PeerPtrs in, PeerOut out, size_t nvec, int n, int me,
                                                            float scale, int out_f32, FlagPtrs flags, int max_blocks,
-                                                           uint64_t epoch, uint64_t timeout_ns, ErrorRecord* err) {
-  if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) != GICC_OK) return;
-  const size_t per = (nvec + n - 1) / n;
-  const size_t lo = per * me, hi = lo + per < nvec ? lo + per : nvec;
-  reduce_range(in, n, lo, hi, [&](size_t v, const float* acc) {
+                                                           EpochRef er, uint64_t timeout_ns, ErrorRecord* err) {
+  const uint64_t epoch = call_epoch(er);
+  if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) == GICC_OK) {
+    const size_t per = (nvec + n - 1) / n;
+    const size_t lo = per * me, hi = lo + per < nvec ? lo + per : nvec;
+    reduce_range(in, n, lo, hi, [&](size_t v, const float* acc) {
 #pragma unroll
-    for (int p = 0; p < kMaxRanks; ++p)
-      if (p < n) store8(out.p[(me + p) % n], v, acc, scale, out_f32);
-  });
-  cta_handshake(flags, n, me, 1, max_blocks, epoch, timeout_ns, err);
+      for (int p = 0; p < kMaxRanks; ++p)
+        if (p < n) store8(out.p[(me + p) % n], v, acc, scale, out_f32);
+    });
+    cta_handshake(flags, n, me, 1, max_blocks, epoch, timeout_ns, err);
+  }
+  finish_epoch(er, epoch);
 }
 
 __device__ __forceinline__ void nvls_emit(void* mc_out, size_t v, uint4 s, float scale, int out_f32) {
@@ -168,8 +197,12 @@ __device__ __forceinline__ void nvls_emit(void* mc_out, size_t v, uint4 s, float
 // NVLS: rank r reduces chunk r inside the switch and multicasts the result.
 __global__ void __launch_bounds__(512) k_allreduce_nvls(const void* mc_in, void* mc_out, size_t nvec, int n, int me,
                                                         float scale, int out_f32, FlagPtrs flags, int max_blocks,
-                                                        uint64_t epoch, uint64_t timeout_ns, ErrorRecord* err) {
-  if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) != GICC_OK) return;
+                                                        EpochRef er, uint64_t timeout_ns, ErrorRecord* err) {
+  const uint64_t epoch = call_epoch(er);
+  if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) != GICC_OK) {
+    finish_epoch(er, epoch);
+    return;
+  }
   const size_t per = (nvec + n - 1) / n;
   const size_t lo = per * me, hi = lo + per < nvec ? lo + per : nvec;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -185,6 +218,7 @@ __global__ void __launch_bounds__(512) k_allreduce_nvls(const void* mc_in, void*
   }
   for (; v < hi; v += stride) nvls_emit(mc_out, v, ptx::multimem_ld_reduce_bf16x8(src + v), scale, out_f32);
   cta_handshake(flags, n, me, 1, max_blocks, epoch, timeout_ns, err);
+  finish_epoch(er, epoch);
 }
 
 // Plain multi-source reduction (callers order it with barriers): out = scale * sum(src).
@@ -214,7 +248,9 @@ void reduce_bf16(const void* const* srcs, int nsrc, void* out, size_t count, flo
 
 void allreduce_bf16(int algo, const void* const* in, void* const* out, const void* mc_in, void* mc_out, int n, int me,
                     size_t count, float scale, bool out_f32, uint64_t* const* flag_bases, int max_blocks,
-                    uint64_t epoch, uint64_t timeout_ns, int blocks, cudaStream_t s) {
+                    uint64_t epoch, uint64_t timeout_ns, int blocks, cudaStream_t s, uint64_t* epoch_dev,
+                    unsigned int* ticket) {
+  if (epoch_dev && !ticket) throw std::runtime_error("gicc::allreduce: a device epoch needs a ticket word");
   NvtxRange nvtx("gicc::ops::allreduce_bf16");
   if (n < 1 || n > kMaxRanks) throw std::runtime_error("gicc::allreduce: 1..8 ranks (one NVSwitch node)");
   if (count % 8) throw std::runtime_error("gicc::allreduce: element count must be a multiple of 8");
@@ -242,18 +278,19 @@ void allreduce_bf16(int algo, const void* const* in, void* const* out, const voi
   }
   if (blocks > max_blocks) blocks = max_blocks;
   ErrorRecord* err = device_error_record();
+  const EpochRef er{epoch, epoch_dev, ticket};
   switch (algo) {
     case ALLREDUCE_ONESHOT:
-      k_allreduce_oneshot<<<blocks, 256, 0, s>>>(ip, op.p[me], nvec, n, me, scale, out_f32, fp, max_blocks, epoch,
+      k_allreduce_oneshot<<<blocks, 256, 0, s>>>(ip, op.p[me], nvec, n, me, scale, out_f32, fp, max_blocks, er,
                                                  timeout_ns, err);
       break;
     case ALLREDUCE_TWOSHOT:
-      k_allreduce_twoshot<<<blocks, 256, 0, s>>>(ip, op, nvec, n, me, scale, out_f32, fp, max_blocks, epoch,
+      k_allreduce_twoshot<<<blocks, 256, 0, s>>>(ip, op, nvec, n, me, scale, out_f32, fp, max_blocks, er,
                                                  timeout_ns, err);
       break;
     case ALLREDUCE_NVLS:
       if (!mc_in || !mc_out) throw std::runtime_error("gicc::allreduce: NVLS needs multicast-bound buffers");
-      k_allreduce_nvls<<<blocks, 512, 0, s>>>(mc_in, mc_out, nvec, n, me, scale, out_f32, fp, max_blocks, epoch,
+      k_allreduce_nvls<<<blocks, 512, 0, s>>>(mc_in, mc_out, nvec, n, me, scale, out_f32, fp, max_blocks, er,
                                               timeout_ns, err);
       break;
     default:

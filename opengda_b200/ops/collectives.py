@@ -31,11 +31,16 @@ class Allreduce:
     ``inp`` is a symmetric bf16 buffer (write the data into ``allreduce.input(count)``),
     the result goes to a symmetric output buffer (bf16 or f32).  ``algo``: "oneshot",
     "twoshot", "nvls" or "auto" (one-shot <= 256 KiB, NVLS when available, else two-shot).
+
+    ``graph_safe=True`` keeps the call counter on the device (each kernel reads it and its
+    last CTA advances it), so calls can be captured in a CUDA graph (``torch.cuda.graph``)
+    and replayed; every rank must replay the same calls in the same order.  Without it the
+    host passes the counter, and capturing a call is refused (a replay would reuse it).
     """
 
     MAX_BLOCKS = 1024
 
-    def __init__(self, rt, max_count: int, out_dtype: torch.dtype = torch.bfloat16):
+    def __init__(self, rt, max_count: int, out_dtype: torch.dtype = torch.bfloat16, graph_safe: bool = False):
         self.rt = rt
         self.n, self.me = rt.size, rt.rank
         self.max_count = (max_count + 7) // 8 * 8
@@ -48,6 +53,9 @@ class Allreduce:
         self.epoch = 0
         self.in_ptrs = [self.inp.ptr(p) for p in range(self.n)]
         self.out_ptrs = [self.out.ptr(p) for p in range(self.n)]
+        self.graph_safe = graph_safe
+        if graph_safe:  # [0] epoch (u64), [1] low half: the CTA ticket (u32)
+            self._dev_words = torch.zeros(2, dtype=torch.int64, device=self.inp.local.device)
 
     def input(self, count: Optional[int] = None) -> torch.Tensor:
         return self.inp.local[: (count or self.max_count)]
@@ -68,9 +76,15 @@ class Allreduce:
         a = self.pick(count) if algo == "auto" else ALGOS[algo]
         if a == NVLS and not self.rt.multicast_supported:
             raise RuntimeError("NVLS allreduce needs multicast support")
+        dev = tick = 0
+        if self.graph_safe:
+            dev = self._dev_words.data_ptr()
+            tick = dev + 8
+        elif torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("Allreduce: capturing a call in a CUDA graph needs Allreduce(..., graph_safe=True)")
         self.epoch += 1
         native().k_allreduce_bf16(a, self.in_ptrs, self.out_ptrs, self.inp.mc_ptr if a == NVLS else 0,
                                   self.out.mc_ptr if a == NVLS else 0, self.n, self.me, count, float(scale),
                                   self.out_dtype == torch.float32, self.flags, self.MAX_BLOCKS, self.epoch,
-                                  self.rt.timeout_ns, blocks)
+                                  self.rt.timeout_ns, blocks, dev, tick)
         return self.output(count)

@@ -1,7 +1,8 @@
 """GPU checks of kernels and options that compile and whose host logic is tested on CPU,
 but that have not yet run on a GPU: the ring-stripe fp32 matmul (one GPU and a ring of
 ranks), the copy-engine all-gather GEMM, the reduce-scatter join, and the MoE layer with
-confined dispatch and staged combine, and the persistent Jacobi kernel.  They run only with GICC_TEST_NOT_YET_RUN=1; once a
+confined dispatch and staged combine, the persistent Jacobi kernel, and allreduce
+replayed from a CUDA graph.  They run only with GICC_TEST_NOT_YET_RUN=1; once a
 check has passed on a B200 it moves into the regular GPU suites."""
 import json
 import os
@@ -30,6 +31,41 @@ def test_ring_mm_single_gpu_matches_fp64():
         scale = A.double().abs() @ B.double().abs()
         err = float(((C.cpu().double() - ref).abs() / scale).max())
         assert err < 2e-5, (call, err)
+
+
+def test_allreduce_graph_capture_single_gpu():
+    """Allreduce(graph_safe=True) captured in a CUDA graph gives the right result on every
+    replay (the call counter advances on the device); capturing without it is refused."""
+    import torch
+    from opengda_b200.ops.collectives import Allreduce
+    from opengda_b200.ops.gemm import check_errors
+    from opengda_b200.parallel import Bootstrap, Runtime
+    rt = Runtime(Bootstrap.create(0, 1, "127.0.0.1:0"))
+    try:
+        count = 1 << 16
+        ar = Allreduce(rt, count, graph_safe=True)
+        src = torch.zeros(count, dtype=torch.bfloat16, device="cuda")
+        ar.input(count).copy_(src)
+        ar(count, algo="oneshot", scale=2.0)  # warm-up outside the graph
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            ar.input(count).copy_(src)
+            ar(count, algo="oneshot", scale=2.0)
+        for k in range(3):
+            src.copy_(torch.randn(count, device="cuda").to(torch.bfloat16))
+            g.replay()
+            torch.cuda.synchronize()
+            check_errors()
+            torch.testing.assert_close(ar.output(count).float(), 2.0 * src.float(), rtol=1e-2, atol=1e-2)
+        plain = Allreduce(rt, count)
+        with pytest.raises(RuntimeError, match="graph_safe"):
+            with torch.cuda.graph(torch.cuda.CUDAGraph()):
+                plain(count)
+        del g
+    finally:
+        torch.cuda.synchronize()
+        rt.finalize()
 
 
 def test_jacobi_persistent_single_gpu_bit_exact():
@@ -67,6 +103,8 @@ def test_pending_options_multigpu(tmp_path):
         assert r["gemm_ag_ce_relerr"] < 1e-2 and r["gemm_rs_join_relerr"] < 1e-2, r
         assert r["moe_confined_relerr"] < 2e-2, r
         assert r["jacobi_persistent_mismatch"] == 0, r
+        for k, v in r["allreduce_graph_maxerr"].items():
+            assert v < 0.05 * n, (k, v)
 
 
 @pytest.mark.parametrize("all_gpus", [False, True])

@@ -5,7 +5,8 @@ on a GPU (launched by opengda_b200.parallel.launch; one JSON result per rank):
 * the fused all-gather GEMM with the copy-engine transfer (transfer="ce");
 * the reduce-scatter GEMM with the join option (rs_join);
 * the MoE layer with confined dispatch and the staged combine (dispatch_ctas, combine_ctas);
-* the persistent Jacobi kernel (one cooperative launch for many iterations).
+* the persistent Jacobi kernel (one cooperative launch for many iterations);
+* allreduce with a device-side call counter, captured in a CUDA graph and replayed.
 """
 import json
 import os
@@ -91,6 +92,38 @@ def main():
     rt.check_device_errors()
     field = np.concatenate(boot.allgather_obj(jac.owned().cpu().numpy()), axis=0)
     res["jacobi_persistent_mismatch"] = int((field != jacobi_np(jnx, jny, 25)[1:-1]).sum())
+
+    # 5. allreduce captured in a CUDA graph (device-side call counter), every algorithm,
+    #    three replays with new inputs each
+    from opengda_b200.ops.collectives import Allreduce
+    count = 1 << 18
+    errs = {}
+    for algo in (["oneshot", "twoshot"] + (["nvls"] if rt.multicast_supported else [])):
+        ar = Allreduce(rt, count, graph_safe=True)
+        src = torch.zeros(count, dtype=torch.bfloat16, device="cuda")
+        ar.input(count).copy_(src)
+        ar(count, algo=algo)
+        torch.cuda.synchronize()
+        boot.barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            ar.input(count).copy_(src)
+            ar(count, algo=algo, scale=0.5)
+        worst = 0.0
+        for k in range(3):
+            gen = torch.Generator(device="cuda").manual_seed(500 + k)
+            allx = [torch.randn(count, generator=gen, device="cuda").to(torch.bfloat16) for _ in range(n)]
+            src.copy_(allx[r])
+            boot.barrier()
+            graph.replay()
+            torch.cuda.synchronize()
+            ref = 0.5 * torch.stack([x.float() for x in allx]).sum(0)
+            worst = max(worst, float((ar.output(count).float() - ref).abs().max().item()))
+            boot.barrier()
+        errs[algo] = worst
+        del graph, ar
+    rt.check_device_errors()
+    res["allreduce_graph_maxerr"] = errs
 
     boot.barrier()
     with open(f"{out}.{r}", "w") as f:
