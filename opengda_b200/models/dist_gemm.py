@@ -20,6 +20,7 @@ from typing import Optional
 import torch
 
 from ..ops.gemm import gemm
+from ..utils.graphs import refuse_capture
 
 
 class DistGemm:
@@ -165,6 +166,7 @@ class DistGemm:
         w, r = self.world, self.rank
         if w == 1:
             return gemm(A, B, out=out)
+        refuse_capture("DistGemm")
         if self.fused:
             from .. import native
 

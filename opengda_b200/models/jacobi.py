@@ -16,6 +16,7 @@ import numpy as np
 import torch
 
 from .. import native
+from ..utils.graphs import refuse_capture
 
 
 def split_rows(ny: int, world: int, rank: int):
@@ -65,6 +66,8 @@ class Jacobi:
             self.done_ctr = torch.zeros(grid, dtype=torch.int64, device=self.device)
 
     def step(self, norm: bool = False) -> None:
+        if self.world > 1:
+            refuse_capture("Jacobi.step on several ranks")
         a, b = self.bufs[self.cur], self.bufs[1 - self.cur]
         top_dst = bot_dst = top_sig = bot_sig = top_flag = bot_flag = 0
         wait = 0
@@ -107,6 +110,7 @@ class Jacobi:
     def run(self, iters: int, norm_last: bool = False) -> Optional[float]:
         """Run `iters` iterations; optionally return the global L2 norm of the last update."""
         if self.persistent and iters > 0:
+            refuse_capture("Jacobi.run (persistent)")
             if norm_last:
                 self.norm_buf.zero_()
             self._run_persistent(iters, norm_last)

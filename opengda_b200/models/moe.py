@@ -23,6 +23,7 @@ from typing import Optional
 import torch
 
 from .. import native
+from ..utils.graphs import refuse_capture
 
 
 def interleave_w1(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
@@ -113,6 +114,7 @@ class MoELayer:
         """x [T, H] bf16, logits [T, E] fp32 -> y [T, H] bf16 (this rank's tokens).
         stage_times=True also records per-kernel device times into ``self.last_stage_ms``
         (synchronises; profiling only)."""
+        refuse_capture("MoELayer")
         assert x.shape == (self.T, self.H) and x.dtype == torch.bfloat16 and x.is_contiguous()
         assert logits.shape == (self.T, self.E) and logits.dtype == torch.float32 and logits.is_contiguous()
         self.epoch += 1

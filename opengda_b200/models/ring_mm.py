@@ -22,6 +22,7 @@ from typing import Optional
 import torch
 
 from .. import native
+from ..utils.graphs import refuse_capture
 
 
 class RingMatmul:
@@ -50,6 +51,8 @@ class RingMatmul:
     def forward(self, A_s: torch.Tensor, B_s: torch.Tensor, C_s: Optional[torch.Tensor] = None) -> torch.Tensor:
         """A_s [Ns, N] and B_s [N, Ns] fp32 (this rank's stripes) -> C_s [Ns, N] = A_s . B."""
         N, Ns, n, r = self.N, self.Ns, self.n, self.r
+        if n > 1:
+            refuse_capture("RingMatmul")
         assert A_s.shape == (Ns, N) and A_s.dtype == torch.float32 and A_s.is_contiguous()
         assert B_s.shape == (N, Ns) and B_s.dtype == torch.float32 and B_s.is_contiguous()
         if C_s is None:
