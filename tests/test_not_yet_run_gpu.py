@@ -157,3 +157,27 @@ def test_native_am_pingpong_two_ranks():
                        env=dict(os.environ, GICC_TIMEOUT_MS="5000"))
     assert p.returncode == 0, p.stdout + p.stderr
     assert "request/reply" in p.stdout and "request/request" in p.stdout
+
+
+@pytest.mark.multigpu
+def test_rank_loss_between_steps_is_detected_on_the_host(tmp_path):
+    """A rank that leaves between steps (no kernel or collective of it in flight) is seen by
+    the others at their next host-side bootstrap barrier, before they launch anything that
+    would wait on it.  Multicast is off (GICC_DISABLE_NVLS=1, NCCL_NVLS_ENABLE=0) and the
+    kernels use plain peer stores."""
+    import torch
+    from opengda_b200.parallel.launch import launch
+    n = min(torch.cuda.device_count(), 4)
+    if n < 2:
+        pytest.skip("needs 2 GPUs")
+    out = str(tmp_path / "loss")
+    worker = os.path.join(os.path.dirname(__file__), "workers", "rank_loss_worker.py")
+    launch(n, [sys.executable, worker, out, "1", "2"], timeout=180,
+           extra_env={"GICC_DISABLE_NVLS": "1", "NCCL_NVLS_ENABLE": "0", "GICC_TIMEOUT_MS": "2000",
+                      "GICC_BOOTSTRAP_TIMEOUT_MS": "20000"})
+    for r in range(n):
+        if r == 1:
+            assert not os.path.exists(f"{out}.1")
+            continue
+        res = json.load(open(f"{out}.{r}"))
+        assert res["steps_done"] == 2 and res["detected"] and "left the job" in res["detected"], res
