@@ -391,6 +391,9 @@ void bind_runtime_objects(py::module_& m) {
     a.right = d.contains("right") ? d["right"].cast<int>() : -1;
     ops::ring_mm_step(a, cur_stream());
   });
+  m.def("k_put_tile", [](uint64_t dst, int tiles, uint32_t tile_bytes, uint32_t seed, uint64_t sig) {
+    ops::put_tile_test(P<void>(dst), tiles, tile_bytes, seed, P<uint64_t>(sig), cur_stream());
+  }, py::arg("dst"), py::arg("tiles"), py::arg("tile_bytes"), py::arg("seed"), py::arg("sig") = 0);
   m.def("k_saxpy", [](uint64_t x, uint64_t y, float a, size_t n) {
     ops::saxpy(P<const float>(x), P<float>(y), a, n, cur_stream());
   });

@@ -91,6 +91,24 @@ __device__ __forceinline__ void get(void* dst, const void* src_remote, size_t n)
 }
 __device__ __forceinline__ void quiet() { ptx::fence_acq_rel_sys(); }
 
+// Bulk put of a tile staged in this CTA's shared memory: one thread issues a cp.async.bulk
+// shared -> global store (no multicast) straight into the peer's memory, so the copy needs
+// no registers and no further instructions of the CTA.  Addresses 16-byte aligned, bytes a
+// multiple of 16.  Before it: the threads that wrote the tile run fence_tile_for_put() and
+// the CTA synchronises.  put_tile_wait_read(): the tile's shared memory may be rewritten;
+// put_tile_wait(): the stores are complete, after which quiet() + a release signal publish
+// them like any other put.
+__device__ __forceinline__ void fence_tile_for_put() { ptx::fence_proxy_async_smem(); }
+__device__ __forceinline__ void put_tile(void* dst_remote, const void* src_smem, uint32_t bytes) {
+  ptx::bulk_store(dst_remote, src_smem, bytes);
+  ptx::bulk_commit();
+}
+__device__ __forceinline__ void put_tile_wait_read() { ptx::bulk_wait_read_all(); }
+__device__ __forceinline__ void put_tile_wait() {
+  ptx::bulk_wait_all();
+  ptx::fence_proxy_async_global();  // the async-proxy writes are ordered with what follows
+}
+
 enum SignalOp : int { SIGNAL_SET = 0, SIGNAL_ADD = 1 };
 
 // Put n bytes, then publish `value` on the peer's signal word once the data is visible.

@@ -223,6 +223,10 @@ GICC_EXPORT void saxpy_put(const float* x, float* y, float a, size_t n, float* d
                            int blocks, cudaStream_t s);
 GICC_EXPORT void wait_count(const uint64_t* counter, uint64_t target, uint64_t timeout_ns, int rank, cudaStream_t s);
 GICC_EXPORT void saxpy(const float* x, float* y, float a, size_t n, cudaStream_t s);
+// `tiles` CTAs each put one pattern tile from shared memory with the bulk tile put
+// (device put_tile) to dst + i * tile_bytes (dst may be a peer's memory), then add 1 to sig.
+GICC_EXPORT void put_tile_test(void* dst, int tiles, uint32_t tile_bytes, uint32_t seed, uint64_t* sig,
+                               cudaStream_t s);
 // Copy-engine transfer for ag_gemm (the A/B alternative to SM pushes): on stream `s`, for
 // each peer d in the consumption order (r-1, r-2, ...): wait (stream memory operation)
 // until d finished the call that last used this parity, copy this rank's shard into d's

@@ -85,6 +85,25 @@ __global__ void k_wait_count(const uint64_t* counter, uint64_t target, uint64_t 
     report_error(err, GICC_ETIMEDOUT, W_SIGNAL_WAIT, rank, -1, seen, target);
 }
 
+// Bulk tile put: each CTA writes a `tile_bytes` pattern tile into shared memory, one thread
+// puts it to dst + blockIdx.x * tile_bytes with put_tile, waits, and releases `sig` (+1).
+__global__ void __launch_bounds__(256) k_put_tile(uint8_t* dst, uint32_t tile_bytes, uint32_t seed, uint64_t* sig) {
+  extern __shared__ __align__(16) uint8_t tile[];
+  const size_t base = (size_t)blockIdx.x * tile_bytes;
+  for (uint32_t j = threadIdx.x; j < tile_bytes; j += blockDim.x) {  // the byte pattern of k_fill / k_check
+    const size_t i = base + j;
+    tile[j] = (uint8_t)((seed * 2654435761u + (uint32_t)i * 40503u + (uint32_t)(i >> 16)) >> 13);
+  }
+  fence_tile_for_put();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    put_tile(dst + base, tile, tile_bytes);
+    put_tile_wait();
+    quiet();
+    if (sig) signal_add(sig, 1);
+  }
+}
+
 __global__ void k_saxpy(const float* x, float* y, float a, size_t n) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
     y[i] = a * x[i] + y[i];
@@ -110,6 +129,15 @@ void saxpy_put(const float* x, float* y, float a, size_t n, float* dst_remote, u
 
 void wait_count(const uint64_t* counter, uint64_t target, uint64_t timeout_ns, int rank, cudaStream_t s) {
   k_wait_count<<<1, 1, 0, s>>>(counter, target, timeout_ns, device_error_record(), rank);
+  GICC_CUDA(cudaGetLastError());
+}
+
+void put_tile_test(void* dst, int tiles, uint32_t tile_bytes, uint32_t seed, uint64_t* sig, cudaStream_t s) {
+  if (tile_bytes == 0 || tile_bytes % 16 || tile_bytes > 96 * 1024 || (reinterpret_cast<uintptr_t>(dst) & 15))
+    throw std::runtime_error("gicc::put_tile_test: 16-byte aligned dst, tile_bytes a multiple of 16 up to 96 KiB");
+  if (tile_bytes > 48 * 1024)
+    GICC_CUDA(cudaFuncSetAttribute(k_put_tile, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tile_bytes));
+  k_put_tile<<<tiles, 256, tile_bytes, s>>>(static_cast<uint8_t*>(dst), tile_bytes, seed, sig);
   GICC_CUDA(cudaGetLastError());
 }
 

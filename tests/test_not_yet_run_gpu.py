@@ -68,6 +68,23 @@ def test_allreduce_graph_capture_single_gpu():
         rt.finalize()
 
 
+def test_bulk_tile_put_single_gpu():
+    """put_tile (cp.async.bulk shared -> global, one thread per tile) delivers every byte and
+    its release signal counts one per tile."""
+    import torch
+    from opengda_b200 import native
+    from opengda_b200.ops.gemm import check_errors
+    tiles, tile_bytes = 296, 32 * 1024
+    dst = torch.zeros(tiles * tile_bytes, dtype=torch.uint8, device="cuda")
+    sig = torch.zeros(1, dtype=torch.int64, device="cuda")
+    native().k_put_tile(dst.data_ptr(), tiles, tile_bytes, 77, sig.data_ptr())
+    bad = torch.zeros(1, dtype=torch.int64, device="cuda")
+    native().k_check_pattern(dst.data_ptr(), dst.numel(), 77, bad.data_ptr())
+    torch.cuda.synchronize()
+    check_errors()
+    assert int(bad.item()) == 0 and int(sig.item()) == tiles
+
+
 def test_jacobi_persistent_single_gpu_bit_exact():
     """One cooperative launch for many iterations, mixed with per-iteration launches, gives
     the CPU oracle's field bit for bit."""
