@@ -9,10 +9,12 @@ It offers the capabilities and API of GICC/OpenGDA (lwshanbd/OpenGDA), rebuilt f
 * ``opengda_b200.ops`` -- the sm_100a kernels (tcgen05 GEMM, put/get, barrier,
   allreduce, Jacobi, MoE routing/dispatch/combine) as torch-facing functions;
 * ``opengda_b200.models`` -- the workloads: distributed GEMM (AG->GEMM, GEMM->RS),
-  Jacobi with fused halo puts, the MoE expert-parallel layer, the CPU matmul;
+  the fp32 ring-stripe matmul, Jacobi with fused halo puts (per-iteration or persistent),
+  the MoE expert-parallel layer, the CPU matmul;
 * ``opengda_b200.baselines`` -- NCCL(+cuBLAS) and host-driven restatements used as the
   comparison arm;
-* ``opengda_b200.utils`` -- config, logging, device timing, result records.
+* ``opengda_b200.utils`` -- config, logging, device timing, clock sampling, result
+  records, litmus tests, the topology / environment probe, the CUDA-graph capture guard.
 
 The native code lives in ``lib/libgicc.so`` (no torch dependency) and the binding
 ``_C``; ``python -m opengda_b200._build`` compiles both in place.
