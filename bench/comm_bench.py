@@ -9,6 +9,8 @@
 * quiet latency: one 8-byte NVLink store + fence.acq_rel.sys.
 * barrier: 10000 barriers in one kernel (continuous mode), dissemination and NVLS;
   NCCL arm: dist.barrier() and a 1-element all_reduce (both in a CUDA graph-free loop).
+* with --rs-ag: reduce-scatter and all-gather (NVLS and direct) against NCCL's
+  reduce_scatter_tensor / all_gather_into_tensor, bus bandwidth (n-1)/n * S / t;
 * allreduce bf16 N(0,1), 1 KiB .. 1 GiB: bus bandwidth 2(n-1)/n * S / t for every
   algorithm (one-shot, two-shot, NVLS, auto) and NCCL.
 
@@ -55,6 +57,7 @@ def main():
     ap.add_argument("--out", default=None)
     ap.add_argument("--max-put", type=int, default=28)  # 2^28 = 256 MiB
     ap.add_argument("--max-ar", type=int, default=30)   # 2^30 = 1 GiB
+    ap.add_argument("--rs-ag", action="store_true", help="also time reduce-scatter and all-gather vs NCCL")
     args = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -193,6 +196,39 @@ def main():
         arr.append(row)
     results["allreduce_bf16"] = arr
     rt.check_device_errors()
+
+    # ---------------- reduce-scatter / all-gather (bus bandwidth (n-1)/n * S / t) ----------
+    if args.rs_ag:
+        from opengda_b200.ops.collectives import AllGather, ReduceScatter
+        del ar
+        torch.cuda.empty_cache()
+        rs = ReduceScatter(rt, max_count)
+        rs.input().copy_(torch.randn(max_count, generator=g, device="cuda").to(torch.bfloat16))
+        ag = AllGather(rt, max_count * 2 // n)
+        rows = []
+        for k in range(16, args.max_ar + 1, 2):
+            nbytes = 1 << k
+            count = nbytes // 2
+            if count % (8 * n):
+                continue
+            reps = max(3, min(100, (256 << 20) // nbytes))
+            row = {"bytes": nbytes}
+            for nv in ([True, False] if rs.nvls else [False]):
+                tag = "nvls" if nv else "direct"
+                ms = timed(lambda: rs(count, nvls=nv), reps)
+                row[f"rs_{tag}"] = {"us": ms * 1e3, "busbw_GBps": (n - 1) / n * nbytes / (ms * 1e-3) / 1e9}
+                ms = timed(lambda: ag(nbytes // n, nvls=nv), reps)
+                row[f"ag_{tag}"] = {"us": ms * 1e3, "busbw_GBps": (n - 1) / n * nbytes / (ms * 1e-3) / 1e9}
+            full = nccl_buf[:count]
+            part = torch.empty(count // n, dtype=torch.bfloat16, device="cuda")
+            ms = timed(lambda: dist.reduce_scatter_tensor(part, full), reps)
+            row["rs_nccl"] = {"us": ms * 1e3, "busbw_GBps": (n - 1) / n * nbytes / (ms * 1e-3) / 1e9}
+            ms = timed(lambda: dist.all_gather_into_tensor(full, part), reps)
+            row["ag_nccl"] = {"us": ms * 1e3, "busbw_GBps": (n - 1) / n * nbytes / (ms * 1e-3) / 1e9}
+            rows.append(row)
+        results["reduce_scatter_all_gather"] = rows
+        rt.check_device_errors()
+        ar = None
     if r == 0:
         js = json.dumps(results)
         print(js)

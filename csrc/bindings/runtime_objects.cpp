@@ -218,6 +218,37 @@ void bind_runtime_objects(py::module_& m) {
   }, py::arg("algo"), py::arg("in_ptrs"), py::arg("out_ptrs"), py::arg("mc_in"), py::arg("mc_out"), py::arg("n"),
      py::arg("me"), py::arg("count"), py::arg("scale"), py::arg("out_f32"), py::arg("flags"), py::arg("max_blocks"),
      py::arg("epoch"), py::arg("timeout_ns"), py::arg("blocks"), py::arg("epoch_dev") = 0, py::arg("ticket") = 0);
+  m.def("k_reduce_scatter_bf16", [](bool nvls, std::vector<uint64_t> in, uint64_t mc_in, uint64_t out, int n, int me,
+                                    size_t count, float scale, bool out_f32, std::vector<uint64_t> flags,
+                                    int max_blocks, uint64_t epoch, uint64_t timeout_ns, int blocks, uint64_t epoch_dev,
+                                    uint64_t ticket) {
+    std::vector<const void*> ip;
+    std::vector<uint64_t*> fp;
+    for (auto a : in) ip.push_back(P<const void>(a));
+    for (auto a : flags) fp.push_back(P<uint64_t>(a));
+    if ((int)fp.size() != n || (!nvls && (int)ip.size() != n))
+      throw std::runtime_error("k_reduce_scatter_bf16: one flag base (and, without NVLS, one input) per rank");
+    ops::reduce_scatter_bf16(nvls, ip.empty() ? nullptr : ip.data(), P<const void>(mc_in), P<void>(out), n, me, count,
+                             scale, out_f32, fp.data(), max_blocks, epoch, timeout_ns, blocks, cur_stream(),
+                             P<uint64_t>(epoch_dev), P<unsigned int>(ticket));
+  }, py::arg("nvls"), py::arg("in_ptrs"), py::arg("mc_in"), py::arg("out"), py::arg("n"), py::arg("me"),
+     py::arg("count"), py::arg("scale"), py::arg("out_f32"), py::arg("flags"), py::arg("max_blocks"), py::arg("epoch"),
+     py::arg("timeout_ns"), py::arg("blocks") = 0, py::arg("epoch_dev") = 0, py::arg("ticket") = 0);
+  m.def("k_all_gather", [](bool nvls, uint64_t shard, std::vector<uint64_t> out, uint64_t mc_out, int n, int me,
+                           size_t shard_bytes, std::vector<uint64_t> flags, int max_blocks, uint64_t epoch,
+                           uint64_t timeout_ns, int blocks, uint64_t epoch_dev, uint64_t ticket) {
+    std::vector<void*> op;
+    std::vector<uint64_t*> fp;
+    for (auto a : out) op.push_back(P<void>(a));
+    for (auto a : flags) fp.push_back(P<uint64_t>(a));
+    if ((int)fp.size() != n || (!nvls && (int)op.size() != n))
+      throw std::runtime_error("k_all_gather: one flag base (and, without NVLS, one output) per rank");
+    ops::all_gather(nvls, P<const void>(shard), op.empty() ? nullptr : op.data(), P<void>(mc_out), n, me, shard_bytes,
+                    fp.data(), max_blocks, epoch, timeout_ns, blocks, cur_stream(), P<uint64_t>(epoch_dev),
+                    P<unsigned int>(ticket));
+  }, py::arg("nvls"), py::arg("shard"), py::arg("out_ptrs"), py::arg("mc_out"), py::arg("n"), py::arg("me"),
+     py::arg("shard_bytes"), py::arg("flags"), py::arg("max_blocks"), py::arg("epoch"), py::arg("timeout_ns"),
+     py::arg("blocks") = 0, py::arg("epoch_dev") = 0, py::arg("ticket") = 0);
   m.def("k_jacobi_init", [](uint64_t a, uint64_t b, int nx, int ny, int rows, int g0, uint64_t seed) {
     ops::jacobi_init(P<float>(a), P<float>(b), nx, ny, rows, g0, seed, cur_stream());
   });

@@ -69,6 +69,22 @@ GICC_EXPORT void allreduce_bf16(int algo, const void* const* in, void* const* ou
                                 int max_blocks, uint64_t epoch, uint64_t timeout_ns, int blocks, cudaStream_t s,
                                 uint64_t* epoch_dev = nullptr, unsigned int* ticket = nullptr);
 
+// Reduce-scatter of `count` bf16 elements (count % (8 * n) == 0): rank r receives chunk r of
+// the sum (count / n elements, bf16 or f32, scaled) in `out` (local).  nvls: the switch adds
+// the copies (mc_in = the input's multicast address); otherwise every rank's input is read
+// over NVLink.  Flags, epochs and the device-epoch option as for allreduce_bf16.
+GICC_EXPORT void reduce_scatter_bf16(bool nvls, const void* const* in, const void* mc_in, void* out, int n, int me,
+                                     size_t count, float scale, bool out_f32, uint64_t* const* flag_bases,
+                                     int max_blocks, uint64_t epoch, uint64_t timeout_ns, int blocks, cudaStream_t s,
+                                     uint64_t* epoch_dev = nullptr, unsigned int* ticket = nullptr);
+// All-gather: this rank's `shard_bytes` (16-byte multiple, local) land at offset
+// me * shard_bytes of every rank's symmetric output.  nvls: one multimem store per vector
+// (mc_out = the output's multicast address); otherwise one store per rank.
+GICC_EXPORT void all_gather(bool nvls, const void* shard, void* const* out, void* mc_out, int n, int me,
+                            size_t shard_bytes, uint64_t* const* flag_bases, int max_blocks, uint64_t epoch,
+                            uint64_t timeout_ns, int blocks, cudaStream_t s, uint64_t* epoch_dev = nullptr,
+                            unsigned int* ticket = nullptr);
+
 // ---- ring-stripe fp32 matmul (ring_mm.cu) -----------------------------------------------------
 // One step of C_s = A_s . B over a ring of n ranks: A_s [Ns][N] (my rows), B stripes [N][Ns]
 // travelling to the right, C_s [Ns][N].  Counters are monotonic over the whole job: for the

@@ -221,6 +221,84 @@ __global__ void __launch_bounds__(512) k_allreduce_nvls(const void* mc_in, void*
   finish_epoch(er, epoch);
 }
 
+// Reduce-scatter: rank r ends with chunk r of the sum, out[v - lo] for v in [lo, hi).
+// Direct: CTAs read every rank's input over NVLink; NVLS: the switch adds the copies.
+__global__ void __launch_bounds__(256) k_reduce_scatter(PeerPtrs in, void* out, size_t nvec, int n, int me,
+                                                        float scale, int out_f32, FlagPtrs flags, int max_blocks,
+                                                        EpochRef er, uint64_t timeout_ns, ErrorRecord* err) {
+  const uint64_t epoch = call_epoch(er);
+  if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) == GICC_OK) {
+    const size_t per = nvec / n, lo = per * me;
+    reduce_range(in, n, lo, lo + per, [&](size_t v, const float* acc) { store8(out, v - lo, acc, scale, out_f32); });
+    cta_handshake(flags, n, me, 1, max_blocks, epoch, timeout_ns, err);  // inputs may be rewritten after this
+  }
+  finish_epoch(er, epoch);
+}
+
+__global__ void __launch_bounds__(512) k_reduce_scatter_nvls(const void* mc_in, void* out, size_t nvec, int n, int me,
+                                                             float scale, int out_f32, FlagPtrs flags, int max_blocks,
+                                                             EpochRef er, uint64_t timeout_ns, ErrorRecord* err) {
+  const uint64_t epoch = call_epoch(er);
+  if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) == GICC_OK) {
+    const size_t per = nvec / n, lo = per * me;
+    const uint4* src = reinterpret_cast<const uint4*>(mc_in);
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    constexpr int U = 2 * kU;
+    for (; v + (U - 1) * stride < per; v += U * stride) {
+      uint4 t[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) t[u] = ptx::multimem_ld_reduce_bf16x8(src + lo + v + u * stride);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        add_bf16x8(acc, t[u]);
+        store8(out, v + u * stride, acc, scale, out_f32);
+      }
+    }
+    for (; v < per; v += stride) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      add_bf16x8(acc, ptx::multimem_ld_reduce_bf16x8(src + lo + v));
+      store8(out, v, acc, scale, out_f32);
+    }
+    cta_handshake(flags, n, me, 1, max_blocks, epoch, timeout_ns, err);
+  }
+  finish_epoch(er, epoch);
+}
+
+// All-gather of 16-byte vectors: rank r's shard goes to [r*per, (r+1)*per) of every rank's
+// output.  Direct: one store per peer; NVLS: one multimem store reaches every GPU.
+__global__ void __launch_bounds__(256) k_all_gather(const uint4* shard, PeerOut out, size_t per, int n, int me,
+                                                    FlagPtrs flags, int max_blocks, EpochRef er, uint64_t timeout_ns,
+                                                    ErrorRecord* err) {
+  const uint64_t epoch = call_epoch(er);
+  if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) == GICC_OK) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < per; v += stride) {
+      const uint4 x = shard[v];
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p)
+        if (p < n) reinterpret_cast<uint4*>(out.p[(me + p) % n])[(size_t)me * per + v] = x;
+    }
+    cta_handshake(flags, n, me, 1, max_blocks, epoch, timeout_ns, err);  // every shard has landed here
+  }
+  finish_epoch(er, epoch);
+}
+
+__global__ void __launch_bounds__(512) k_all_gather_nvls(const uint4* shard, void* mc_out, size_t per, int n, int me,
+                                                         FlagPtrs flags, int max_blocks, EpochRef er,
+                                                         uint64_t timeout_ns, ErrorRecord* err) {
+  const uint64_t epoch = call_epoch(er);
+  if (cta_handshake(flags, n, me, 0, max_blocks, epoch, timeout_ns, err) == GICC_OK) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    uint4* dst = reinterpret_cast<uint4*>(mc_out) + (size_t)me * per;
+    for (size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < per; v += stride)
+      ptx::multimem_st_v4(dst + v, shard[v]);
+    cta_handshake(flags, n, me, 1, max_blocks, epoch, timeout_ns, err);
+  }
+  finish_epoch(er, epoch);
+}
+
 // Plain multi-source reduction (callers order it with barriers): out = scale * sum(src).
 __global__ void __launch_bounds__(256) k_reduce(PeerPtrs src, int nsrc, void* out, size_t nvec, float scale,
                                                 int out_f32) {
@@ -295,6 +373,77 @@ void allreduce_bf16(int algo, const void* const* in, void* const* out, const voi
       break;
     default:
       throw std::runtime_error("gicc::allreduce: unknown algorithm");
+  }
+  GICC_CUDA(cudaGetLastError());
+}
+
+namespace {
+int resident_blocks(const void* fn, int threads, size_t work) {
+  int per_sm = 1;
+  GICC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0));
+  const size_t resident = (size_t)std::max(per_sm, 1) * num_sms();
+  return (int)std::min<size_t>(std::max<size_t>((work + threads * kU - 1) / (threads * kU), 1), resident);
+}
+}  // namespace
+
+void reduce_scatter_bf16(bool nvls, const void* const* in, const void* mc_in, void* out, int n, int me, size_t count,
+                         float scale, bool out_f32, uint64_t* const* flag_bases, int max_blocks, uint64_t epoch,
+                         uint64_t timeout_ns, int blocks, cudaStream_t s, uint64_t* epoch_dev, unsigned int* ticket) {
+  NvtxRange nvtx("gicc::ops::reduce_scatter_bf16");
+  if (n < 1 || n > kMaxRanks) throw std::runtime_error("gicc::reduce_scatter: 1..8 ranks");
+  if (count % (8 * (size_t)n)) throw std::runtime_error("gicc::reduce_scatter: count must be a multiple of 8 * ranks");
+  if (epoch_dev && !ticket) throw std::runtime_error("gicc::reduce_scatter: a device epoch needs a ticket word");
+  const size_t nvec = count / 8;
+  PeerPtrs ip{};
+  FlagPtrs fp{};
+  for (int i = 0; i < n; ++i) {
+    ip.p[i] = in ? in[i] : nullptr;
+    fp.p[i] = flag_bases[i];
+  }
+  const EpochRef er{epoch, epoch_dev, ticket};
+  ErrorRecord* err = device_error_record();
+  if (nvls) {
+    if (!mc_in) throw std::runtime_error("gicc::reduce_scatter: NVLS needs a multicast-bound input");
+    if (blocks <= 0) blocks = resident_blocks((const void*)k_reduce_scatter_nvls, 512, nvec / n);
+    blocks = std::min(blocks, max_blocks);
+    k_reduce_scatter_nvls<<<blocks, 512, 0, s>>>(mc_in, out, nvec, n, me, scale, out_f32, fp, max_blocks, er,
+                                                 timeout_ns, err);
+  } else {
+    if (blocks <= 0) blocks = resident_blocks((const void*)k_reduce_scatter, 256, nvec / n);
+    blocks = std::min(blocks, max_blocks);
+    k_reduce_scatter<<<blocks, 256, 0, s>>>(ip, out, nvec, n, me, scale, out_f32, fp, max_blocks, er, timeout_ns,
+                                            err);
+  }
+  GICC_CUDA(cudaGetLastError());
+}
+
+void all_gather(bool nvls, const void* shard, void* const* out, void* mc_out, int n, int me, size_t shard_bytes,
+                uint64_t* const* flag_bases, int max_blocks, uint64_t epoch, uint64_t timeout_ns, int blocks,
+                cudaStream_t s, uint64_t* epoch_dev, unsigned int* ticket) {
+  NvtxRange nvtx("gicc::ops::all_gather");
+  if (n < 1 || n > kMaxRanks) throw std::runtime_error("gicc::all_gather: 1..8 ranks");
+  if (shard_bytes % 16 || (reinterpret_cast<uintptr_t>(shard) & 15))
+    throw std::runtime_error("gicc::all_gather: 16-byte aligned shard of a multiple of 16 bytes");
+  if (epoch_dev && !ticket) throw std::runtime_error("gicc::all_gather: a device epoch needs a ticket word");
+  const size_t per = shard_bytes / 16;
+  PeerOut op{};
+  FlagPtrs fp{};
+  for (int i = 0; i < n; ++i) {
+    op.p[i] = out ? out[i] : nullptr;
+    fp.p[i] = flag_bases[i];
+  }
+  const EpochRef er{epoch, epoch_dev, ticket};
+  ErrorRecord* err = device_error_record();
+  const uint4* src = static_cast<const uint4*>(shard);
+  if (nvls) {
+    if (!mc_out) throw std::runtime_error("gicc::all_gather: NVLS needs a multicast-bound output");
+    if (blocks <= 0) blocks = resident_blocks((const void*)k_all_gather_nvls, 512, per);
+    blocks = std::min(blocks, max_blocks);
+    k_all_gather_nvls<<<blocks, 512, 0, s>>>(src, mc_out, per, n, me, fp, max_blocks, er, timeout_ns, err);
+  } else {
+    if (blocks <= 0) blocks = resident_blocks((const void*)k_all_gather, 256, per * n);
+    blocks = std::min(blocks, max_blocks);
+    k_all_gather<<<blocks, 256, 0, s>>>(src, op, per, n, me, fp, max_blocks, er, timeout_ns, err);
   }
   GICC_CUDA(cudaGetLastError());
 }

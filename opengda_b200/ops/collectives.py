@@ -88,3 +88,99 @@ class Allreduce:
                                   self.out_dtype == torch.float32, self.flags, self.MAX_BLOCKS, self.epoch,
                                   self.rt.timeout_ns, blocks, dev, tick)
         return self.output(count)
+
+
+class _Collective:
+    """Shared state of the symmetric-buffer collectives: flag area, call counter (host or,
+    with graph_safe, device-resident) and the capture guard."""
+
+    MAX_BLOCKS = 1024
+
+    def __init__(self, rt, graph_safe: bool):
+        self.rt = rt
+        self.n, self.me = rt.size, rt.rank
+        off = rt.signal_alloc(2 * self.MAX_BLOCKS * self.n)
+        self.flags = [rt.signal_peer(p, off) for p in range(self.n)]
+        self.epoch = 0
+        self.graph_safe = graph_safe
+        self._dev_words = torch.zeros(2, dtype=torch.int64, device="cuda") if graph_safe else None
+
+    def _next(self, name: str):
+        if self.graph_safe:
+            dev = self._dev_words.data_ptr()
+            return dev, dev + 8
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError(f"{name}: capturing a call in a CUDA graph needs graph_safe=True")
+        self.epoch += 1
+        return 0, 0
+
+
+class ReduceScatter(_Collective):
+    """Reduce-scatter of bf16 vectors: write up to ``max_count`` elements into
+    ``input(count)`` (symmetric), call; rank r gets chunk r of the sum (count / n elements,
+    scaled, bf16 or f32) in ``output(count)``.  NVLS (sum inside the switch) when the node
+    has it, else every rank's input is read over NVLink.  ``graph_safe`` as for Allreduce."""
+
+    def __init__(self, rt, max_count: int, out_dtype: torch.dtype = torch.bfloat16, graph_safe: bool = False):
+        super().__init__(rt, graph_safe)
+        q = 8 * self.n
+        self.max_count = (max_count + q - 1) // q * q
+        self.nvls = bool(rt.multicast_supported and self.n > 1)
+        self.inp = rt.alloc_tensor((self.max_count,), torch.bfloat16, multicast=self.nvls)
+        self.out = torch.empty(self.max_count // self.n, dtype=out_dtype, device=self.inp.local.device)
+        self.out_dtype = out_dtype
+        self.in_ptrs = [self.inp.ptr(p) for p in range(self.n)]
+
+    def input(self, count: Optional[int] = None) -> torch.Tensor:
+        return self.inp.local[: (count or self.max_count)]
+
+    def output(self, count: Optional[int] = None) -> torch.Tensor:
+        return self.out[: (count or self.max_count) // self.n]
+
+    def __call__(self, count: int, scale: float = 1.0, blocks: int = 0, nvls: Optional[bool] = None) -> torch.Tensor:
+        if count % (8 * self.n) or count > self.max_count:
+            raise ValueError("count must be a multiple of 8 * ranks and <= max_count")
+        use_nvls = self.nvls if nvls is None else bool(nvls)
+        if use_nvls and not self.nvls:
+            raise RuntimeError("NVLS reduce-scatter needs multicast support")
+        dev, tick = self._next("ReduceScatter")
+        native().k_reduce_scatter_bf16(use_nvls, self.in_ptrs, self.inp.mc_ptr if use_nvls else 0,
+                                       self.out.data_ptr(), self.n, self.me, count, float(scale),
+                                       self.out_dtype == torch.float32, self.flags, self.MAX_BLOCKS, self.epoch,
+                                       self.rt.timeout_ns, blocks, dev, tick)
+        return self.output(count)
+
+
+class AllGather(_Collective):
+    """All-gather: write this rank's shard (up to ``max_shard_bytes``, a multiple of 16)
+    into ``shard(nbytes)``, call; every rank's ``output(nbytes)`` then holds all shards in
+    rank order (n * nbytes bytes, symmetric).  NVLS multicast stores when the node has them,
+    else one store per rank.  ``graph_safe`` as for Allreduce."""
+
+    def __init__(self, rt, max_shard_bytes: int, graph_safe: bool = False):
+        super().__init__(rt, graph_safe)
+        self.max_shard_bytes = (max_shard_bytes + 15) // 16 * 16
+        self.nvls = bool(rt.multicast_supported and self.n > 1)
+        self.out = rt.alloc_tensor((self.n * self.max_shard_bytes,), torch.uint8, multicast=self.nvls)
+        self._shard = torch.empty(self.max_shard_bytes, dtype=torch.uint8, device=self.out.local.device)
+        self.out_ptrs = [self.out.ptr(p) for p in range(self.n)]
+
+    def shard(self, nbytes: Optional[int] = None) -> torch.Tensor:
+        return self._shard[: (nbytes or self.max_shard_bytes)]
+
+    def output(self, nbytes: Optional[int] = None) -> torch.Tensor:
+        """[n, nbytes]: row r is rank r's shard (the gathered bytes are contiguous)."""
+        b = nbytes or self.max_shard_bytes
+        return self.out.local[: self.n * b].view(self.n, b)
+
+    def __call__(self, nbytes: int, blocks: int = 0, nvls: Optional[bool] = None) -> torch.Tensor:
+        if nbytes % 16 or nbytes > self.max_shard_bytes:
+            raise ValueError("nbytes must be a multiple of 16 and <= max_shard_bytes")
+        use_nvls = self.nvls if nvls is None else bool(nvls)
+        if use_nvls and not self.nvls:
+            raise RuntimeError("NVLS all-gather needs multicast support")
+        dev, tick = self._next("AllGather")
+        native().k_all_gather(use_nvls, self._shard.data_ptr(), self.out_ptrs, self.out.mc_ptr if use_nvls else 0,
+                              self.n, self.me, nbytes, self.flags, self.MAX_BLOCKS, self.epoch, self.rt.timeout_ns,
+                              blocks, dev, tick)
+        return self.output(nbytes)

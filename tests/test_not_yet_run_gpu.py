@@ -122,6 +122,9 @@ def test_pending_options_multigpu(tmp_path):
         assert r["jacobi_persistent_mismatch"] == 0, r
         for k, v in r["allreduce_graph_maxerr"].items():
             assert v < 0.05 * n, (k, v)
+        for k, v in r["reduce_scatter_maxerr"].items():
+            assert v < 0.05 * n, (k, v)
+        assert r["all_gather_bad"] == 0, r
 
 
 @pytest.mark.parametrize("all_gpus", [False, True])

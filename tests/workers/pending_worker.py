@@ -125,6 +125,35 @@ def main():
     rt.check_device_errors()
     res["allreduce_graph_maxerr"] = errs
 
+    # 6. standalone reduce-scatter (NVLS when available, and direct) and all-gather
+    from opengda_b200.ops.collectives import AllGather, ReduceScatter
+    count = 8 * n * 4096
+    rs = ReduceScatter(rt, count, out_dtype=torch.float32)
+    gen = torch.Generator(device="cuda").manual_seed(900)
+    allx = [torch.randn(count, generator=gen, device="cuda").to(torch.bfloat16) for _ in range(n)]
+    ref = torch.stack([x.float() for x in allx]).sum(0)[r * count // n:(r + 1) * count // n]
+    errs = {}
+    for nv in ([True, False] if rs.nvls else [False]):
+        rs.input(count).copy_(allx[r])
+        boot.barrier()
+        y = rs(count, scale=1.0, nvls=nv)
+        torch.cuda.synchronize()
+        errs["nvls" if nv else "direct"] = float((y - ref).abs().max().item())
+        boot.barrier()
+    res["reduce_scatter_maxerr"] = errs
+    ag = AllGather(rt, 1 << 16)
+    bad = 0
+    for nv in ([True, False] if ag.nvls else [False]):
+        ag.shard(1 << 16).copy_(torch.full((1 << 16,), 10 + r, dtype=torch.uint8, device="cuda"))
+        boot.barrier()
+        out_ag = ag(1 << 16, nvls=nv)
+        torch.cuda.synchronize()
+        want = torch.arange(n, device="cuda", dtype=torch.uint8).view(n, 1) + 10
+        bad += int((out_ag != want).sum().item())
+        boot.barrier()
+    rt.check_device_errors()
+    res["all_gather_bad"] = bad
+
     boot.barrier()
     with open(f"{out}.{r}", "w") as f:
         json.dump(res, f)
