@@ -34,6 +34,8 @@ def main():
     ap.add_argument("--no-baseline", action="store_true")
     ap.add_argument("--out", default=None)
     ap.add_argument("--dispatch-ctas", type=int, default=0, help="CTAs that dispatch (0 = all; A/B option)")
+    ap.add_argument("--comm-only", action="store_true",
+                    help="time the dispatch + combine round trip alone (identity experts), vs NCCL all_to_all")
     ap.add_argument("--combine-ctas", type=int, default=0,
                     help="CTAs that push the combine (0 = all, from the epilogue; A/B option)")
     args = ap.parse_args()
@@ -69,6 +71,37 @@ def main():
         torch.cuda.synchronize()
         return max_over_ranks(s.elapsed_time(e) / steps)
 
+    if args.comm_only:
+        ms = timeit(lambda: layer.dispatch_combine(x, logits), args.steps, args.warmup)
+        if rt:
+            rt.check_device_errors()
+        res = {"metric": "moe_dispatch_combine_us", "impl": "ours-fused", "n_gpus": world,
+               "tokens_per_gpu": args.tokens, "hidden": args.hidden, "experts": args.experts, "topk": args.topk,
+               "us": ms * 1e3}
+        layer.dispatch_combine(x, logits, stage_times=True)
+        res["stage_us_rank0"] = {k: round(v * 1e3, 1) for k, v in layer.last_stage_ms.items()}
+        y = layer.dispatch_combine(x, logits).float()
+        prob = torch.softmax(logits, dim=-1)
+        wsum = torch.topk(prob, args.topk, dim=-1).values.sum(-1, keepdim=True)
+        ref = x.float() * wsum
+        res["rel_err_vs_identity_reference"] = float(((y - ref).norm() / ref.norm()).item())
+        if not args.no_baseline:
+            from opengda_b200.baselines.moe_nccl import NcclMoE
+            base = NcclMoE(layer)
+            ms_b = timeit(lambda: base.dispatch_combine(x, logits), max(2, args.steps // 2), 1)
+            res["nccl_torch"] = {"us": ms_b * 1e3}
+        if rank == 0:
+            print(json.dumps(res))
+            if args.out:
+                with open(args.out, "w") as f:
+                    f.write(json.dumps(res) + "\n")
+        if world > 1:
+            del layer
+            torch.cuda.synchronize()
+            rt.finalize()
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     ms = timeit(lambda: layer(x, logits), args.steps, args.warmup)
     if rt:
         rt.check_device_errors()

@@ -481,6 +481,7 @@ void bind_runtime_objects(py::module_& m) {
     if (w.contains("g2_queue")) a.ws.g2_queue = P<uint64_t>(w["g2_queue"].cast<uint64_t>());
     if (d.contains("dispatch_ctas")) a.dispatch_ctas = d["dispatch_ctas"].cast<int>();
     if (d.contains("combine_ctas")) a.combine_ctas = d["combine_ctas"].cast<int>();
+    if (d.contains("comm_only")) a.comm_only = d["comm_only"].cast<int>();
     if (d.contains("y_stage")) a.y_stage = P<void>(d["y_stage"].cast<uint64_t>());
     std::vector<float> stage(6, 0.f);
     const bool timed = d.contains("stage_times") && d["stage_times"].cast<bool>();

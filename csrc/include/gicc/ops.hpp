@@ -310,6 +310,8 @@ struct MoeArgs {
   int combine_ctas = 0;           // > 0: the second GEMM stages its rows in y_stage and only this
                                   // many CTAs push them to the sources (ws.g2_ctr, ws.g2_queue)
   void* y_stage = nullptr;        // [cap][H] bf16 local (needed with combine_ctas)
+  int comm_only = 0;              // 1: identity experts -- route, dispatch, return, combine only
+                                  // (out[t] = sum_j w_j * x[t]), to time the all-to-all round trip
 };
 GICC_EXPORT void moe_route(const float* logits, int T, int E, int topk, int* topk_idx, float* topk_w, int* counts,
                            cudaStream_t s);

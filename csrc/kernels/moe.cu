@@ -714,6 +714,86 @@ __global__ void __launch_bounds__(cta_threads(kCommWarps), 1)
 // ---------------------------------------------------------------------------------------
 // 6. combine: out[t] = sum_j comb[t*topk + j]
 // ---------------------------------------------------------------------------------------
+// ---------------------------------------------------------------------------------------
+// Communication only (MoeArgs::comm_only): the same dispatch and combine with identity
+// experts, to time the all-to-all round trip by itself.  k_moe_dispatch runs the first
+// grouped GEMM's dispatch warps alone; k_moe_return sends every received row, scaled by its
+// gate, back to its source (counting H/256 per row, as the second GEMM's epilogue does), so
+// k_combine then sums sum_j w_j * x[t] for every token.
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kCommWarps * 32) k_moe_dispatch(G1SchedT<false> s, ErrorRecord* err,
+                                                                   uint64_t timeout_ns) {
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) abort_flag = 0;
+  __syncthreads();
+  s.comm((int)threadIdx.x / 32, (int)threadIdx.x % 32, &abort_flag, err, timeout_ns);
+}
+
+struct ReturnArgs {
+  int n, r, El, H;
+  const int* mblk_prefix;
+  const int* expert_base;
+  const int* expert_rows;
+  const uint64_t* arrivals;  // my [n][El] row counters
+  const uint64_t* cum_rows;  // [n][El] targets
+  const uint16_t* recv;      // my [cap][H]
+  const int4* meta;          // my [cap]
+  Ptrs8 comb;
+  Words8 comb_arrivals;
+};
+
+__global__ void __launch_bounds__(256) k_moe_return(ReturnArgs a, ErrorRecord* err, uint64_t timeout_ns) {
+  __shared__ int ok;
+  __shared__ uint32_t cnt[kMaxR];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nwarps = blockDim.x / 32;
+  if (threadIdx.x < kMaxR) cnt[threadIdx.x] = 0;
+  const int blocks = a.mblk_prefix[a.El];
+  for (int u = blockIdx.x; u < blocks; u += gridDim.x) {
+    int lo = 0, hi = a.El - 1;  // the expert of m-block u
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (a.mblk_prefix[mid] <= u) lo = mid; else hi = mid - 1;
+    }
+    const int e = lo, mb = u - a.mblk_prefix[e];
+    if (threadIdx.x == 0) {
+      ok = 1;
+      for (int src = 0; src < a.n && ok; ++src)
+        if (!wait_ge(a.arrivals + (size_t)src * a.El + e, a.cum_rows[(size_t)src * a.El + e], timeout_ns, nullptr)) {
+          report_error(err, GICC_ETIMEDOUT, W_MOE_COUNT, a.r, src, 0, a.cum_rows[(size_t)src * a.El + e]);
+          ok = 0;
+        }
+    }
+    __syncthreads();
+    if (!ok) return;
+    const int rows = min(BM, a.expert_rows[e] - mb * BM);
+    const int row0 = a.expert_base[e] + mb * BM;
+    for (int i = warp; i < rows; i += nwarps) {
+      const int4 m = a.meta[row0 + i];
+      const float gate = __int_as_float(m.z);
+      const uint4* src = reinterpret_cast<const uint4*>(a.recv + (size_t)(row0 + i) * a.H);
+      uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.comb.p[m.x]) + (size_t)m.y * a.H);
+      for (int c = lane; c < a.H / 8; c += 32) {
+        const uint4 v = src[c];
+        uint4 o;
+        o.x = ptx::pack_bf16x2(gate * ptx::bf16_lo(v.x), gate * ptx::bf16_hi(v.x));
+        o.y = ptx::pack_bf16x2(gate * ptx::bf16_lo(v.y), gate * ptx::bf16_hi(v.y));
+        o.z = ptx::pack_bf16x2(gate * ptx::bf16_lo(v.z), gate * ptx::bf16_hi(v.z));
+        o.w = ptx::pack_bf16x2(gate * ptx::bf16_lo(v.w), gate * ptx::bf16_hi(v.w));
+        ptx::st_v4_na(dst + c, o);
+      }
+      if (lane == 0) atomicAdd(&cnt[m.x], (uint32_t)(a.H / 256));
+    }
+    ptx::fence_acq_rel_sys();
+    __syncthreads();
+    if (threadIdx.x < a.n) {
+      const uint32_t c = cnt[threadIdx.x];
+      cnt[threadIdx.x] = 0;
+      if (c) ptx::red_release_sys_add(a.comb_arrivals.p[threadIdx.x], c);
+    }
+    __syncthreads();
+  }
+}
+
 __global__ void k_combine(const uint16_t* comb, uint16_t* out, int T, int H, int topk, const uint64_t* arrivals,
                           uint64_t target, ErrorRecord* err, uint64_t timeout_ns, int rank) {
   __shared__ int ok;
@@ -817,6 +897,60 @@ void moe_forward(const MoeArgs& a, cudaStream_t s) {
   mark(3);
   // 4. GEMM 1 (+ dispatch)
   const int G = num_sms();
+  if (a.comm_only) {  // identity experts: dispatch, return, combine
+    moe::G1SchedT<false> d{};
+    d.n = n;
+    d.r = r;
+    d.El = El;
+    d.H = a.H;
+    d.topk = a.topk;
+    d.G = G;
+    d.C = G;
+    d.npairs = pairs;
+    d.send_pair = a.ws.send_pair;
+    d.send_row = a.ws.send_row;
+    d.topk_idx = a.topk_idx;
+    d.topk_w = a.topk_w;
+    d.x = static_cast<const uint16_t*>(a.x);
+    for (int i = 0; i < n; ++i) {
+      d.recv.p[i] = a.recv[i];
+      d.meta.p[i] = a.meta[i];
+      d.arrivals_peer.p[i] = a.arrivals[i];
+    }
+    moe::k_moe_dispatch<<<G, moe::kCommWarps * 32, 0, s>>>(d, err, tmo);
+    GICC_CUDA(cudaGetLastError());
+    mark(4);
+    moe::ReturnArgs ra{};
+    ra.n = n;
+    ra.r = r;
+    ra.El = El;
+    ra.H = a.H;
+    ra.mblk_prefix = a.ws.mblk_prefix;
+    ra.expert_base = a.ws.expert_base;
+    ra.expert_rows = a.ws.expert_rows;
+    ra.arrivals = a.arrivals[r];
+    ra.cum_rows = a.ws.cum_rows;
+    ra.recv = static_cast<const uint16_t*>(a.recv[r]);
+    ra.meta = static_cast<const int4*>(a.meta[r]);
+    for (int i = 0; i < n; ++i) {
+      ra.comb.p[i] = a.comb[i];
+      ra.comb_arrivals.p[i] = a.comb_arrivals[i];
+    }
+    moe::k_moe_return<<<2 * G, 256, 0, s>>>(ra, err, tmo);
+    GICC_CUDA(cudaGetLastError());
+    mark(5);
+    const uint64_t target = a.epoch * (uint64_t)pairs * (uint64_t)(a.H / 256);
+    moe::k_combine<<<4 * G, 256, 0, s>>>(static_cast<const uint16_t*>(a.comb[r]), static_cast<uint16_t*>(a.out), a.T,
+                                          a.H, a.topk, a.comb_arrivals[r], target, err, tmo, r);
+    GICC_CUDA(cudaGetLastError());
+    mark(6);
+    if (a.stage_ms) {
+      GICC_CUDA(cudaEventSynchronize(ev[6]));
+      for (int i = 0; i < 6; ++i) GICC_CUDA(cudaEventElapsedTime(&a.stage_ms[i], ev[i], ev[i + 1]));
+      for (auto& e : ev) cudaEventDestroy(e);
+    }
+    return;
+  }
   const CUtensorMap tA1 = make_tmap_2d(a.recv[r], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.cap_rows, a.H, a.H, BM, BK,
                                        CU_TENSOR_MAP_SWIZZLE_128B);
   const CUtensorMap tB1 = make_tmap_2d(a.w1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)El * 2 * a.I, a.H, a.H, 256,

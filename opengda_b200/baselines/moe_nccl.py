@@ -68,4 +68,28 @@ class NcclMoE:
         y = (y.view(T, k, self.H) * w.unsqueeze(-1)).sum(1)
         return y.to(x.dtype)
 
+    def dispatch_combine(self, x: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
+        """The all-to-all round trip alone (identity experts): route, all_to_all_single of the
+        rows to their owners and back, gate-weighted sum on the source."""
+        T, k, El, n = self.T, self.topk, self.El, self.n
+        prob = torch.softmax(logits, dim=-1)
+        w, idx = torch.topk(prob, k, dim=-1)
+        flat = idx.flatten()
+        order = torch.argsort(flat, stable=True)
+        send = x[order // k]
+        counts = torch.bincount(flat, minlength=self.E)
+        if n > 1:
+            recv_counts = torch.empty_like(counts)
+            dist.all_to_all_single(recv_counts, counts)
+            ss, rs = counts.view(n, El).sum(1).tolist(), recv_counts.view(n, El).sum(1).tolist()
+            recv = torch.empty(sum(rs), self.H, dtype=x.dtype, device=x.device)
+            dist.all_to_all_single(recv, send, rs, ss)
+            back = torch.empty_like(send)
+            dist.all_to_all_single(back, recv, ss, rs)
+        else:
+            back = send
+        y = torch.zeros(T * k, self.H, dtype=torch.float32, device=x.device)
+        y[order] = back.float()
+        return (y.view(T, k, self.H) * w.unsqueeze(-1)).sum(1).to(x.dtype)
+
     __call__ = forward

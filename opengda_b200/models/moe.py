@@ -109,8 +109,16 @@ class MoELayer:
         self.launches_per_step = 7  # memset + route + plan + sort + gemm1 + gemm2 + combine
 
     STAGES = ("route", "plan", "sort", "gemm1+dispatch", "gemm2+combine_push", "combine")
+    COMM_STAGES = ("route", "plan", "sort", "dispatch", "return", "combine")
 
-    def forward(self, x: torch.Tensor, logits: torch.Tensor, stage_times: bool = False) -> torch.Tensor:
+    def dispatch_combine(self, x: torch.Tensor, logits: torch.Tensor, stage_times: bool = False) -> torch.Tensor:
+        """The all-to-all round trip alone, with identity experts: routing, dispatch of every
+        (token, expert) row to its owner, return of the row scaled by its gate, combine.
+        Returns y[t] = sum_j w_j * x[t]; the counters advance exactly as in ``forward``."""
+        return self.forward(x, logits, stage_times=stage_times, comm_only=True)
+
+    def forward(self, x: torch.Tensor, logits: torch.Tensor, stage_times: bool = False,
+                comm_only: bool = False) -> torch.Tensor:
         """x [T, H] bf16, logits [T, E] fp32 -> y [T, H] bf16 (this rank's tokens).
         stage_times=True also records per-kernel device times into ``self.last_stage_ms``
         (synchronises; profiling only)."""
@@ -141,11 +149,12 @@ class MoELayer:
             "stage_times": stage_times,
             "dispatch_ctas": self.dispatch_ctas,
             "combine_ctas": self.combine_ctas,
+            "comm_only": int(comm_only),
             "y_stage": self.y_stage.data_ptr() if self.y_stage is not None else 0,
         }
         st = native().k_moe_forward(d)
         if stage_times:
-            self.last_stage_ms = dict(zip(self.STAGES, st))
+            self.last_stage_ms = dict(zip(self.COMM_STAGES if comm_only else self.STAGES, st))
         return self.out
 
     __call__ = forward

@@ -85,6 +85,30 @@ def test_bulk_tile_put_single_gpu():
     assert int(bad.item()) == 0 and int(sig.item()) == tiles
 
 
+def test_moe_dispatch_combine_identity_single_gpu():
+    """The communication-only MoE round trip returns sum_j w_j * x[t]; normal forwards before
+    and after it still match the reference (the counters stay consistent)."""
+    import torch
+    from opengda_b200.models.moe import MoELayer, make_inputs, reference_moe
+    from opengda_b200.ops.gemm import check_errors
+    T, H, E, k, I = 256, 512, 16, 4, 256
+    layer = MoELayer(T, H, E, k, I, rt=None, weight_std=0.05)
+    for call in range(4):
+        x, logits = make_inputs(T, H, E, 0, seed=40 + call)
+        if call % 2:
+            y = layer.dispatch_combine(x, logits).float()
+            wsum = torch.topk(torch.softmax(logits, -1), k, dim=-1).values.sum(-1, keepdim=True)
+            ref = x.float() * wsum
+        else:
+            y = layer(x, logits).float()
+            rows = torch.arange(0, T, 16, device="cuda")
+            ref = reference_moe(x, logits, k, layer.w_gate, layer.w_up, layer.w2, rows)
+            y = y[rows]
+        torch.cuda.synchronize()
+        check_errors()
+        assert ((y - ref).norm() / ref.norm()).item() < 2e-2, call
+
+
 def test_jacobi_persistent_single_gpu_bit_exact():
     """One cooperative launch for many iterations, mixed with per-iteration launches, gives
     the CPU oracle's field bit for bit."""
@@ -125,6 +149,7 @@ def test_pending_options_multigpu(tmp_path):
         for k, v in r["reduce_scatter_maxerr"].items():
             assert v < 0.05 * n, (k, v)
         assert r["all_gather_bad"] == 0, r
+        assert r["moe_dispatch_combine_relerr"] < 2e-2, r
 
 
 @pytest.mark.parametrize("all_gpus", [False, True])

@@ -154,6 +154,19 @@ def main():
     rt.check_device_errors()
     res["all_gather_bad"] = bad
 
+    # 7. MoE all-to-all round trip alone (identity experts)
+    layer2 = MoELayer(T, H, E, k, I, rt=rt, weight_std=0.05)
+    worst = 0.0
+    for call in range(3):
+        x, logits = make_inputs(T, H, E, r, seed=60 + call)
+        y = layer2.dispatch_combine(x, logits).float()
+        torch.cuda.synchronize()
+        wsum = torch.topk(torch.softmax(logits, -1), k, dim=-1).values.sum(-1, keepdim=True)
+        ref = x.float() * wsum
+        worst = max(worst, float(((y - ref).norm() / ref.norm()).item()))
+    rt.check_device_errors()
+    res["moe_dispatch_combine_relerr"] = worst
+
     boot.barrier()
     with open(f"{out}.{r}", "w") as f:
         json.dump(res, f)
