@@ -226,3 +226,23 @@ def test_rank_loss_between_steps_is_detected_on_the_host(tmp_path):
             continue
         res = json.load(open(f"{out}.{r}"))
         assert res["steps_done"] == 2 and res["detected"] and "left the job" in res["detected"], res
+
+
+@pytest.mark.parametrize("all_gpus", [False, True])
+def test_native_queued_put(all_gpus):
+    """Host-queued puts (put_no_db, prepare_trigger, device flush, host wait) in the native
+    example: every stream's per-iteration pattern arrives intact."""
+    import subprocess
+    import torch
+    from opengda_b200.parallel.launch import free_port
+    n = min(torch.cuda.device_count(), 8) if all_gpus else 1
+    if all_gpus and n < 2:
+        pytest.skip("needs 2 GPUs")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cmd = [sys.executable, "-m", "opengda_b200.parallel.launch", "-n", str(n), "--port", str(free_port()),
+           "--timeout", "120", os.path.join(root, "opengda_b200", "bin", "gicc_queued_put"), "-size", "65536",
+           "-iters", "5"]
+    p = subprocess.run(cmd, cwd=root, capture_output=True, text=True, timeout=180,
+                       env=dict(os.environ, GICC_TIMEOUT_MS="5000"))
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert "PASS" in p.stdout
