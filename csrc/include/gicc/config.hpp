@@ -25,6 +25,8 @@ struct GICC_EXPORT Config {
   bool disable_nvls = false;             // GICC_DISABLE_NVLS: never bind multicast objects
   bool debug_puts = false;               // GICC_DEBUG: log every host-initiated transfer
   size_t signal_heap_bytes = 0;          // GICC_SIGNAL_HEAP_BYTES: 0 = the RuntimeOptions value [64 KiB, 1 GiB]
+  int gemm_group_m = 16;                 // GICC_GEMM_GROUP_M: m-blocks per raster group of gemm_bf16 [1, 1024]
+  int gemm_l2_hint = 0;                  // GICC_GEMM_L2_HINT: 0 none, 1 keep A / stream B, 2 the reverse
 
   // Parses the environment now; throws std::invalid_argument naming the bad variable.
   static Config from_env();

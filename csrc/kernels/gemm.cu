@@ -250,13 +250,23 @@ void gemm_tile_done_selftest(const void* A, const void* B, int M, int N, int K, 
 
 namespace {
 GemmTuning g_tuning;
+bool g_tuning_set = false;  // set_gemm_tuning() wins over the environment
 }
 void set_gemm_tuning(const GemmTuning& t) {
   if (t.group_m < 1 || t.l2_hint < 0 || t.l2_hint > 2)
     throw std::runtime_error("gicc::set_gemm_tuning: group_m >= 1, l2_hint in 0..2");
   g_tuning = t;
+  g_tuning_set = true;
 }
-GemmTuning gemm_tuning() { return g_tuning; }
+GemmTuning gemm_tuning() {
+  if (!g_tuning_set) {  // GICC_GEMM_GROUP_M / GICC_GEMM_L2_HINT, read once
+    const Config c = config();
+    g_tuning.group_m = c.gemm_group_m;
+    g_tuning.l2_hint = c.gemm_l2_hint;
+    g_tuning_set = true;
+  }
+  return g_tuning;
+}
 
 void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
                long long ldc, bool out_f32, float alpha, int bn, cudaStream_t stream) {

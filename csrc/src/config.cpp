@@ -71,6 +71,9 @@ Config Config::from_env() {
   parse_bool("GICC_DEBUG", &c.debug_puts);
   uint64_t heap = 0;
   if (parse_u64("GICC_SIGNAL_HEAP_BYTES", 64ull << 10, 1ull << 30, &heap)) c.signal_heap_bytes = heap;
+  uint64_t v = 0;
+  if (parse_u64("GICC_GEMM_GROUP_M", 1, 1024, &v)) c.gemm_group_m = (int)v;
+  if (parse_u64("GICC_GEMM_L2_HINT", 0, 2, &v)) c.gemm_l2_hint = (int)v;
   return c;
 }
 
@@ -78,11 +81,12 @@ std::string Config::summary() const {
   char buf[512];
   std::snprintf(buf, sizeof(buf),
                 "gicc config: GICC_TIMEOUT_MS=%llu GICC_BOOTSTRAP_TIMEOUT_MS=%llu%s GICC_LOG_LEVEL=%s GICC_CHECKS=%d "
-                "GICC_DISABLE_NVLS=%d GICC_DEBUG=%d GICC_SIGNAL_HEAP_BYTES=%zu%s",
+                "GICC_DISABLE_NVLS=%d GICC_DEBUG=%d GICC_SIGNAL_HEAP_BYTES=%zu%s GICC_GEMM_GROUP_M=%d "
+                "GICC_GEMM_L2_HINT=%d",
                 (unsigned long long)timeout_ms, (unsigned long long)bootstrap_timeout_ms,
                 bootstrap_timeout_ms ? "" : " (default 120 s)", level_name(log_level), checks ? 1 : 0,
                 disable_nvls ? 1 : 0, debug_puts ? 1 : 0, signal_heap_bytes,
-                signal_heap_bytes ? "" : " (RuntimeOptions value)");
+                signal_heap_bytes ? "" : " (RuntimeOptions value)", gemm_group_m, gemm_l2_hint);
   return buf;
 }
 

@@ -16,3 +16,16 @@ def test_tuning_roundtrip_and_validation():
     finally:
         set_tuning()
     assert tuning() == {"group_m": 16, "l2_hint": 0}
+
+
+def test_tuning_from_environment():
+    import os
+    import subprocess
+    import sys
+    code = "from opengda_b200.ops.gemm import tuning; print(tuning())"
+    env = dict(os.environ, GICC_GEMM_GROUP_M="8", GICC_GEMM_L2_HINT="1")
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=120)
+    assert "'group_m': 8" in out.stdout and "'l2_hint': 1" in out.stdout, out.stdout + out.stderr
+    env["GICC_GEMM_L2_HINT"] = "5"
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=120)
+    assert out.returncode != 0 and "GICC_GEMM_L2_HINT" in out.stderr
