@@ -2,24 +2,36 @@
 //
 // all-gather -> GEMM (AG):  C[:, cols_r] = A_full[M,K] * B_r[Ns,K]^T
 //   A is row-sharded; rank r's shard already sits in rows [r*Ms, (r+1)*Ms) of its
-//   symmetric A_full buffer.  Four communication warps per CTA push that shard, in
-//   128-row bands, straight into every peer's A_full (16-byte NVLink stores), then bump
-//   the peer's per-(source, band) arrival counter with a release add.  The TMA producer
-//   of each CTA walks the tiles in "local shard first, then shard r+1, r+2, ..." order and
-//   waits (bounded, acquire) on the band's counter before loading it -- so the transfer of
-//   band b+1 overlaps the MMAs on band b.  Pushes go to rank r-1 first, r-2 next, ...
-//   which is exactly the order in which each receiver consumes them.
+//   symmetric A_full buffer.  The communication warps of `comm_ctas` CTAs move that shard
+//   in 128-row bands (units of a band spread over those CTAs):
+//   * NVLS (default when the node has it): each unit is written once through the landing
+//     buffer's multicast view (multimem.st) and one multimem.red bumps the (source, band)
+//     arrival counter on every GPU; all shards arrive at once, band by band, so consumers
+//     take the local shard first and then go band-major over the other sources;
+//   * unicast: 16-byte stores into every peer's A_full, release add on that peer's
+//     counter; pushes go to rank r-1 first, r-2 next, ..., the order in which each receiver
+//     consumes them (local shard first, then shard r+1, r+2, ...);
+//   * copy engines (ops::ag_transfer_ce, an option): a side stream copies the bands and
+//     writes the counters with stream memory operations, and the kernel only waits.
+//   Tiles come from a global counter (dynamic schedule), so the CTAs that push take fewer
+//   tiles; an SM whose warps store to NVLink also slows its own TMA loads.  The TMA producer
+//   waits (bounded, acquire) on a band's counter before loading it, so band b+1 travels
+//   while the tensor cores work on band b.
 //
-// GEMM -> reduce-scatter (RS): rank r owns output rows [r*Mr, (r+1)*Mr)
-//   K is sharded.  Tiles are walked owner by owner (r+1, r+2, ..., own rows last).  The
-//   epilogue stores a remote owner's tile as bf16 into that owner's slot for source r
-//   (peer memory) and releases a per-(source, band) counter; for its own rows it waits for
-//   every source's tiles of the band, adds them (f32) to its TMEM accumulator and writes the
-//   bf16 result.
+// GEMM -> reduce-scatter (RS): rank r owns output rows [r*Mr, (r+1)*Mr); K is sharded.
+//   * NVLS (default when available): every rank stores its bf16 partial of the whole output
+//     in its own staging buffer; when the last tile of band (o, b) is stored, rank r tells
+//     owner o; the owner's reduce warps (in `comm_ctas` CTAs, or -- with the join option --
+//     in every CTA that has run out of tiles) sum the band of all ranks inside the switch
+//     with multimem.ld_reduce once all ranks reported it, and write the result;
+//   * unicast: tiles walked owner by owner (r+1, r+2, ..., own rows last); the epilogue
+//     stores a remote owner's tile into that owner's slot for source r and releases a
+//     (source, band) counter; for its own rows it waits for every source's tiles, adds them
+//     to its TMEM accumulator and writes the bf16 result.
 //
-// Both use epoch counters (one epoch per call) and double-buffered landing areas; a rank
-// writes into a peer's area of parity p only after that peer reported (per-CTA done
-// counters) that it finished the call that last used parity p.
+// Both use epoch counters (one epoch per call) and double-buffered landing / staging areas;
+// a rank writes an area of parity p only after every rank that reads it reported (per-CTA
+// done counters) that it finished the call that last used parity p.
 //
 // The reference's distributed matmul (examples/gicc/mm.cu:116-225) rotates fp32 B stripes
 // around a ring with one <<<1,1>>> put per step and a SIMT atomicAdd kernel; this is the
