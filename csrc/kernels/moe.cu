@@ -23,6 +23,13 @@
 //                  the source rank's combine buffer (slot t*k+j), then release-adds the
 //                  per-source arrival count (rows x column tiles).
 //  6. k_combine    the source waits for all its rows and sums the k weighted rows per token.
+//
+// Options (MoeArgs): dispatch_ctas confines step 4's NVLink stores to a few CTAs and lets
+// the first GEMM take tiles dynamically; combine_ctas makes step 5 stage its rows locally
+// (k_moe_gemm2_staged) and queue each finished tile for a few pushing CTAs; comm_only runs
+// steps 1-3, then k_moe_dispatch (step 4's dispatch alone), k_moe_return (each received row
+// back to its source, scaled by its gate) and step 6 -- the all-to-all round trip with
+// identity experts.
 #include <cuda_runtime.h>
 
 #include <cstring>
