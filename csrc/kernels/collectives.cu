@@ -1,5 +1,7 @@
-// collectives.cu -- allreduce (one-shot, two-shot, NVLS) fused with scale/cast, and a
-// multi-source reduction used by GEMM->reduce-scatter.
+// collectives.cu -- allreduce (one-shot, two-shot, NVLS) fused with scale/cast, standalone
+// reduce-scatter and all-gather (NVLS or direct NVLink), and a multi-source reduction used
+// by GEMM->reduce-scatter.  Every call's epoch is either a kernel argument or, for CUDA-graph
+// capture, a device word that the call reads and its last CTA advances.
 //
 // None of these exists in the reference (its only reduction is the host scalar
 // coll::allreduce_sum over MPI, src/gicc/coll.hpp:15-21).  Design:
