@@ -25,6 +25,7 @@ def main():
     ap.add_argument("--sizes", type=int, nargs="+", default=[8192, 16384])
     ap.add_argument("--groups", type=int, nargs="+", default=[4, 8, 16, 32])
     ap.add_argument("--hints", type=int, nargs="+", default=[0, 1, 2])
+    ap.add_argument("--pair-groups", type=int, nargs="+", default=[4, 8, 16])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--out", default=None)
@@ -62,9 +63,12 @@ def main():
             err = float(((C.float() - ref.float()).norm() / ref.float().norm()).item())
             rows.append({"size": S, "impl": "tcgen05", "group_m": g, "l2_hint": h, "ms": ms,
                          "tflops": flop / ms / 1e9, "rel_err": err, "clocks": clk})
+        for pg in args.pair_groups:
+            set_tuning(pair_group_m=pg)
+            ms, clk = timed(lambda: native().gemm(A, B, out=C, bn=512))
+            rows.append({"size": S, "impl": "tcgen05_pair", "pair_group_m": pg, "ms": ms, "tflops": flop / ms / 1e9,
+                         "clocks": clk})
         set_tuning()
-        ms, clk = timed(lambda: native().gemm(A, B, out=C, bn=512))
-        rows.append({"size": S, "impl": "tcgen05_pair", "ms": ms, "tflops": flop / ms / 1e9, "clocks": clk})
         check_errors()
         del A, B, C, ref
         torch.cuda.empty_cache()

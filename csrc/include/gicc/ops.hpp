@@ -19,8 +19,9 @@ GICC_EXPORT void gemm_bf16(const void* A, const void* B, void* C, int M, int N, 
 // measured configuration): m-blocks per raster group and the L2 eviction hints of the
 // operand loads (0 none, 1 keep A / stream B, 2 keep B / stream A).
 struct GemmTuning {
-  int group_m = 16;
+  int group_m = 16;       // 1-CTA kernel: 128-row m-blocks per raster group
   int l2_hint = 0;
+  int pair_group_m = 8;   // CTA-pair kernel (bn = 512): 256-row m-blocks per raster group
 };
 GICC_EXPORT void set_gemm_tuning(const GemmTuning& t);
 GICC_EXPORT GemmTuning gemm_tuning();

@@ -149,7 +149,7 @@ static void launch_pair(const void* A, const void* B, void* C, int M, int N, int
   s.K = K;
   s.num_m = (M + 2 * BM - 1) / (2 * BM);
   s.num_n = (N + pair::BN2 - 1) / pair::BN2;
-  s.group_m = 8;
+  s.group_m = ops::gemm_tuning().pair_group_m;
   StoreEpi e;
   e.C = C;
   e.ldc = ldc;
@@ -253,8 +253,8 @@ GemmTuning g_tuning;
 bool g_tuning_set = false;  // set_gemm_tuning() wins over the environment
 }
 void set_gemm_tuning(const GemmTuning& t) {
-  if (t.group_m < 1 || t.l2_hint < 0 || t.l2_hint > 2)
-    throw std::runtime_error("gicc::set_gemm_tuning: group_m >= 1, l2_hint in 0..2");
+  if (t.group_m < 1 || t.l2_hint < 0 || t.l2_hint > 2 || t.pair_group_m < 1)
+    throw std::runtime_error("gicc::set_gemm_tuning: group_m >= 1, l2_hint in 0..2, pair_group_m >= 1");
   g_tuning = t;
   g_tuning_set = true;
 }
@@ -263,6 +263,7 @@ GemmTuning gemm_tuning() {
     const Config c = config();
     g_tuning.group_m = c.gemm_group_m;
     g_tuning.l2_hint = c.gemm_l2_hint;
+    g_tuning.pair_group_m = c.gemm_pair_group_m;
     g_tuning_set = true;
   }
   return g_tuning;

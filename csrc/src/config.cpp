@@ -74,6 +74,7 @@ Config Config::from_env() {
   uint64_t v = 0;
   if (parse_u64("GICC_GEMM_GROUP_M", 1, 1024, &v)) c.gemm_group_m = (int)v;
   if (parse_u64("GICC_GEMM_L2_HINT", 0, 2, &v)) c.gemm_l2_hint = (int)v;
+  if (parse_u64("GICC_GEMM_PAIR_GROUP_M", 1, 1024, &v)) c.gemm_pair_group_m = (int)v;
   return c;
 }
 

@@ -5,17 +5,17 @@ from opengda_b200.ops.gemm import set_tuning, tuning
 
 
 def test_tuning_roundtrip_and_validation():
-    assert tuning() == {"group_m": 16, "l2_hint": 0}
+    assert tuning() == {"group_m": 16, "l2_hint": 0, "pair_group_m": 8}
     try:
-        set_tuning(group_m=8, l2_hint=2)
-        assert tuning() == {"group_m": 8, "l2_hint": 2}
-        for bad in ({"group_m": 0}, {"l2_hint": 3}, {"l2_hint": -1}):
+        set_tuning(group_m=8, l2_hint=2, pair_group_m=4)
+        assert tuning() == {"group_m": 8, "l2_hint": 2, "pair_group_m": 4}
+        for bad in ({"group_m": 0}, {"l2_hint": 3}, {"l2_hint": -1}, {"pair_group_m": 0}):
             with pytest.raises(RuntimeError):
                 set_tuning(**bad)
-        assert tuning() == {"group_m": 8, "l2_hint": 2}  # a rejected call changes nothing
+        assert tuning() == {"group_m": 8, "l2_hint": 2, "pair_group_m": 4}  # a rejected call changes nothing
     finally:
         set_tuning()
-    assert tuning() == {"group_m": 16, "l2_hint": 0}
+    assert tuning() == {"group_m": 16, "l2_hint": 0, "pair_group_m": 8}
 
 
 def test_tuning_from_environment():
