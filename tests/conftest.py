@@ -25,3 +25,21 @@ def pytest_collection_modifyitems(config, items):
             item.add_marker(pytest.mark.skip(reason="no CUDA device"))
         if "multigpu" in item.keywords and ngpu < 2:
             item.add_marker(pytest.mark.skip(reason="needs >= 2 GPUs"))
+
+
+def run_native(n, prog, *args, timeout=180, env=None):
+    """Run opengda_b200/bin/<prog> on n ranks under the local launcher; returns the
+    CompletedProcess (stdout/stderr captured)."""
+    import subprocess
+
+    from opengda_b200.parallel.launch import free_port
+    cmd = [sys.executable, "-m", "opengda_b200.parallel.launch", "-n", str(n), "--port", str(free_port()),
+           "--timeout", str(max(30, timeout - 60)), os.path.join(ROOT, "opengda_b200", "bin", prog)]
+    cmd += [str(a) for a in args]
+    return subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=timeout,
+                          env=dict(os.environ, GICC_TIMEOUT_MS="5000", **(env or {})))
+
+
+@pytest.fixture
+def native_app():
+    return run_native

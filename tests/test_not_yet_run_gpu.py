@@ -153,53 +153,33 @@ def test_pending_options_multigpu(tmp_path):
 
 
 @pytest.mark.parametrize("all_gpus", [False, True])
-def test_native_gicc_mm_fp32_ring_exact(all_gpus):
+def test_native_gicc_mm_fp32_ring_exact(all_gpus, native_app):
     """The native example's -ring mode (the reference's fp32 ring algorithm through the C++
     API) reproduces the exact product on sampled elements."""
-    import subprocess
     import torch
-    from opengda_b200.parallel.launch import free_port
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     n = min(torch.cuda.device_count(), 8) if all_gpus else 1
     if all_gpus and n < 2:
         pytest.skip("needs 2 GPUs")
-    cmd = [sys.executable, "-m", "opengda_b200.parallel.launch", "-n", str(n), "--port", str(free_port()),
-           "--timeout", "120", os.path.join(root, "opengda_b200", "bin", "gicc_mm"), "-ring", "-n", "2048",
-           "-iters", "3", "-samples", "64"]
-    p = subprocess.run(cmd, cwd=root, capture_output=True, text=True, timeout=180,
-                       env=dict(os.environ, GICC_TIMEOUT_MS="5000"))
+    p = native_app(n, "gicc_mm", "-ring", "-n", 2048, "-iters", 3, "-samples", 64)
     assert p.returncode == 0, p.stdout + p.stderr
     assert "PASS" in p.stdout
 
 
-def test_native_put_bw_two_ranks():
+def test_native_put_bw_two_ranks(native_app):
     """The native put/get bandwidth sweep verifies every byte it moves."""
-    import subprocess
     import torch
-    from opengda_b200.parallel.launch import free_port
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    cmd = [sys.executable, "-m", "opengda_b200.parallel.launch", "-n", "2", "--port", str(free_port()),
-           "--timeout", "120", os.path.join(root, "opengda_b200", "bin", "gicc_put_bw"), "-max", str(16 << 20),
-           "-iters", "3", "-csv"]
-    p = subprocess.run(cmd, cwd=root, capture_output=True, text=True, timeout=180,
-                       env=dict(os.environ, GICC_TIMEOUT_MS="5000"))
+    p = native_app(2, "gicc_put_bw", "-max", 16 << 20, "-iters", 3, "-csv")
     assert p.returncode == 0, p.stdout + p.stderr
     assert p.stdout.strip().endswith("PASS") and ",FAIL" not in p.stdout
 
 
-def test_native_am_pingpong_two_ranks():
-    import subprocess
+def test_native_am_pingpong_two_ranks(native_app):
     import torch
-    from opengda_b200.parallel.launch import free_port
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    cmd = [sys.executable, "-m", "opengda_b200.parallel.launch", "-n", "2", "--port", str(free_port()),
-           "--timeout", "120", os.path.join(root, "opengda_b200", "bin", "gicc_am_pingpong"), "20", "2"]
-    p = subprocess.run(cmd, cwd=root, capture_output=True, text=True, timeout=180,
-                       env=dict(os.environ, GICC_TIMEOUT_MS="5000"))
+    p = native_app(2, "gicc_am_pingpong", 20, 2)
     assert p.returncode == 0, p.stdout + p.stderr
     assert "request/reply" in p.stdout and "request/request" in p.stdout
 
@@ -229,20 +209,13 @@ def test_rank_loss_between_steps_is_detected_on_the_host(tmp_path):
 
 
 @pytest.mark.parametrize("all_gpus", [False, True])
-def test_native_queued_put(all_gpus):
+def test_native_queued_put(all_gpus, native_app):
     """Host-queued puts (put_no_db, prepare_trigger, device flush, host wait) in the native
     example: every stream's per-iteration pattern arrives intact."""
-    import subprocess
     import torch
-    from opengda_b200.parallel.launch import free_port
     n = min(torch.cuda.device_count(), 8) if all_gpus else 1
     if all_gpus and n < 2:
         pytest.skip("needs 2 GPUs")
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    cmd = [sys.executable, "-m", "opengda_b200.parallel.launch", "-n", str(n), "--port", str(free_port()),
-           "--timeout", "120", os.path.join(root, "opengda_b200", "bin", "gicc_queued_put"), "-size", "65536",
-           "-iters", "5"]
-    p = subprocess.run(cmd, cwd=root, capture_output=True, text=True, timeout=180,
-                       env=dict(os.environ, GICC_TIMEOUT_MS="5000"))
+    p = native_app(n, "gicc_queued_put", "-size", 65536, "-iters", 5)
     assert p.returncode == 0, p.stdout + p.stderr
     assert "PASS" in p.stdout
