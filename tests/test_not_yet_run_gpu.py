@@ -150,6 +150,8 @@ def test_pending_options_multigpu(tmp_path):
             assert v < 0.05 * n, (k, v)
         assert r["all_gather_bad"] == 0, r
         assert r["moe_dispatch_combine_relerr"] < 2e-2, r
+        fe = r["functional_maxerr"]
+        assert fe["all_reduce"] < 0.05 * n and fe["reduce_scatter"] < 0.05 * n and fe["all_gather"] == 0, fe
 
 
 @pytest.mark.parametrize("all_gpus", [False, True])

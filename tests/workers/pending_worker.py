@@ -167,6 +167,29 @@ def main():
     rt.check_device_errors()
     res["moe_dispatch_combine_relerr"] = worst
 
+    # 8. torch.distributed-style calls on ordinary tensors
+    from opengda_b200.parallel.functional import Collectives
+    col = Collectives(rt)
+    gen = torch.Generator(device="cuda").manual_seed(1234)
+    xs = [torch.randn(1000, 37, generator=gen, device="cuda").to(torch.bfloat16) for _ in range(n)]
+    t = xs[r].clone()
+    col.all_reduce(t)
+    ref = torch.stack([x.float() for x in xs]).sum(0)
+    errs = {"all_reduce": float((t.float() - ref).abs().max().item())}
+    big = [torch.randn(8 * n * 300, generator=gen, device="cuda").to(torch.bfloat16) for _ in range(n)]
+    o = torch.empty(8 * 300, dtype=torch.float32, device="cuda")
+    col.reduce_scatter_tensor(o, big[r])
+    ref = torch.stack([x.float() for x in big]).sum(0)[r * 2400:(r + 1) * 2400]
+    errs["reduce_scatter"] = float((o - ref).abs().max().item())
+    shard = torch.full((4, 8), float(r), dtype=torch.float32, device="cuda")
+    g_out = torch.empty(4 * n, 8, dtype=torch.float32, device="cuda")
+    col.all_gather_into_tensor(g_out, shard)
+    want = torch.arange(n, device="cuda", dtype=torch.float32).repeat_interleave(4).view(-1, 1).expand(-1, 8)
+    errs["all_gather"] = float((g_out - want).abs().max().item())
+    torch.cuda.synchronize()
+    rt.check_device_errors()
+    res["functional_maxerr"] = errs
+
     boot.barrier()
     with open(f"{out}.{r}", "w") as f:
         json.dump(res, f)
