@@ -162,6 +162,15 @@ class DistGemm:
             return self.A_bufs[p].local[self.rank * Ms:(self.rank + 1) * Ms]
         return self.A_full.local[self.rank * Ms:(self.rank + 1) * Ms]
 
+    def _peer_ptrs(self, buf, parity: int):
+        """Every rank's address of a symmetric buffer (fixed for the object's life; cached so
+        a call does not rebuild the list)."""
+        cache = self.__dict__.setdefault("_ptr_cache", {})
+        key = (id(buf), parity)
+        if key not in cache:
+            cache[key] = [buf.ptr(q) for q in range(self.world)]
+        return cache[key]
+
     def forward(self, A: torch.Tensor, B: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         w, r = self.world, self.rank
         if w == 1:
@@ -180,7 +189,7 @@ class DistGemm:
                 if A.data_ptr() != slot.data_ptr():
                     slot.copy_(A)
                 buf = self.A_bufs[p]
-                ptrs = [buf.ptr(q) for q in range(w)]
+                ptrs = self._peer_ptrs(buf, p)
                 diag = self.diag
                 done_ev = None
                 if self.transfer == "ce":
@@ -209,14 +218,14 @@ class DistGemm:
                 buf = self.slot_bufs[p]
                 if self.nvls:
                     n.k_gemm_rs(w, r, self.M, self.N, self.K // w, A.data_ptr(), A.stride(0), B.data_ptr(),
-                                B.stride(0), [buf.ptr(q) for q in range(w)], self.arrivals, self.done, C.data_ptr(),
+                                B.stride(0), self._peer_ptrs(buf, p), self.arrivals, self.done, C.data_ptr(),
                                 C.stride(0), self.epoch, self.grid, self.rt.timeout_ns, buf.mc_ptr, self.band_tiles,
                                 self.tile_counter, self.rs_reduce_ctas, self.units_per_band,
                                 self.trace.data_ptr() if self.trace is not None else 0, int(self.rs_join),
                                 self.unit_counter, self.rs_raster_group)
                 else:
                     n.k_gemm_rs(w, r, self.M, self.N, self.K // w, A.data_ptr(), A.stride(0), B.data_ptr(),
-                                B.stride(0), [buf.ptr(q) for q in range(w)], self.arrivals, self.done, C.data_ptr(),
+                                B.stride(0), self._peer_ptrs(buf, p), self.arrivals, self.done, C.data_ptr(),
                                 C.stride(0), self.epoch, self.grid, self.rt.timeout_ns)
             return C
         if self.mode == "ag":
