@@ -155,7 +155,7 @@ def main() -> int:
             a_dev = feeder.next()
             out = model(a_dev, B)
             feeder.release()
-            out.float().sum().item()
+            out.sum(dtype=torch.float32).item()  # 4-byte device->host read of a checksum
 
     e2e_run(2)
     torch.cuda.synchronize()
