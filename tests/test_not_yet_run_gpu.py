@@ -139,6 +139,8 @@ def test_pending_options_multigpu(tmp_path):
                 extra_env={"GICC_TIMEOUT_MS": "5000", "GICC_BOOTSTRAP_TIMEOUT_MS": "120000"})
     res = [json.load(open(f"{out}.{r}")) for r in range(n)]
     assert rc == 0, res
+    errors = {k: v for r in res for k, v in r.items() if k.endswith("_error")}
+    assert not errors, errors
     for r in res:
         assert r["ring_mm_err"] < 2e-5, r
         assert r["gemm_ag_ce_relerr"] < 1e-2 and r["gemm_rs_join_relerr"] < 1e-2, r
