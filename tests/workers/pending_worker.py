@@ -49,7 +49,9 @@ def main():
     try:
         from opengda_b200.models.dist_gemm import DistGemm, make_operands
         M = Nn = K = 2048
-        for name, mode, kw, attr in (("ag_ce", "ag", {"transfer": "ce"}, {}), ("rs_join", "rs", {}, {"rs_join": True})):
+        for name, mode, kw, attr in (("ag_ce", "ag", {"transfer": "ce"}, {}), ("rs_join", "rs", {}, {"rs_join": True}),
+                                     ("rs_group2", "rs", {}, {"rs_raster_group": 2}),
+                                     ("ag_unicast", "ag", {"nvls": False}, {}), ("rs_unicast", "rs", {"nvls": False}, {})):
             model = DistGemm(M, Nn, K, mode, rt=rt, fused=True, **kw)
             for k, v in attr.items():
                 setattr(model, k, v)
