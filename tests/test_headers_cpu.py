@@ -1,0 +1,35 @@
+"""The umbrella headers under the reference's names compile: <gicc/gicc.hpp> with the host
+compiler and <gicc/gicc_device.cuh> in an sm_100a translation unit, so a program written for
+the reference finds its includes."""
+import os
+import shutil
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+INC = os.path.join(ROOT, "csrc", "include")
+NVCC = "/usr/local/cuda/bin/nvcc"
+
+
+def test_host_umbrella_header(tmp_path):
+    if shutil.which("g++") is None:
+        pytest.skip("no g++")
+    src = tmp_path / "h.cpp"
+    src.write_text("#include <gicc/gicc.hpp>\nint main() { return gicc::config().timeout_ms == 0; }\n")
+    p = subprocess.run(["g++", "-std=c++17", f"-I{INC}", "-I/usr/local/cuda/include", "-fsyntax-only", str(src)],
+                       capture_output=True, text=True, timeout=300)
+    assert p.returncode == 0, p.stderr[-3000:]
+
+
+def test_device_umbrella_header(tmp_path):
+    if not os.path.exists(NVCC):
+        pytest.skip("no nvcc")
+    src = tmp_path / "d.cu"
+    src.write_text("#include <gicc/gicc.hpp>\n#include <gicc/gicc_device.cuh>\n"
+                   "__global__ void k(gicc::DeviceCtx* c, uint64_t l, uint32_t lk, uint64_t r, uint32_t rk) {\n"
+                   "  gicc::put(c, l, lk, r, rk, 64);\n  gicc::flush(c);\n  gicc::quiet(c);\n}\n")
+    p = subprocess.run([NVCC, "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", f"-I{INC}",
+                        "--expt-relaxed-constexpr", "-c", str(src), "-o", str(tmp_path / "d.o")],
+                       capture_output=True, text=True, timeout=600)
+    assert p.returncode == 0, p.stderr[-3000:]
