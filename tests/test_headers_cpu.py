@@ -16,7 +16,8 @@ def test_host_umbrella_header(tmp_path):
     if shutil.which("g++") is None:
         pytest.skip("no g++")
     src = tmp_path / "h.cpp"
-    src.write_text("#include <gicc/gicc.hpp>\nint main() { return gicc::config().timeout_ms == 0; }\n")
+    src.write_text("#include <gicc/gicc.hpp>\n#include <gicc/bootstrap/bootstrap.hpp>\n#include <gicc/coll.hpp>\n"
+                   "int main() { return gicc::config().timeout_ms == 0; }\n")
     p = subprocess.run(["g++", "-std=c++17", f"-I{INC}", "-I/usr/local/cuda/include", "-fsyntax-only", str(src)],
                        capture_output=True, text=True, timeout=300)
     assert p.returncode == 0, p.stderr[-3000:]
