@@ -34,3 +34,45 @@ def test_device_umbrella_header(tmp_path):
                         "--expt-relaxed-constexpr", "-c", str(src), "-o", str(tmp_path / "d.o")],
                        capture_output=True, text=True, timeout=600)
     assert p.returncode == 0, p.stderr[-3000:]
+
+
+def test_reference_style_program_compiles(tmp_path):
+    """A program written against the reference's documented API (Runtime register_buffer /
+    exchange / prepare / remote_buffer / reset, device put / flush / quiet on a DeviceCtx,
+    Barrier continuous mode) compiles unchanged against these headers."""
+    if not os.path.exists(NVCC):
+        pytest.skip("no nvcc")
+    src = tmp_path / "app.cu"
+    src.write_text(r"""
+#include <gicc/gicc.hpp>
+#include <gicc/gicc_device.cuh>
+__global__ void kernel(gicc::DeviceCtx* ctx, uint64_t laddr, uint32_t lkey, uint64_t raddr, uint32_t rkey,
+                       uint32_t size, gicc::BarrierCtx* bar) {
+  gicc::put(ctx, laddr, lkey, raddr, rkey, size);
+  gicc::quiet(ctx);
+  gicc::flush(ctx);
+  gicc::barrier(bar);
+  bar->expected_signal++;
+}
+int main() {
+  gicc::Runtime rt;
+  void* d = nullptr;
+  cudaMalloc(&d, 1 << 20);
+  auto buf = rt.register_buffer(d, 1 << 20, true);
+  rt.exchange();
+  const int peer = (rt.rank() + 1) % rt.size();
+  auto remote = rt.remote_buffer(peer, buf.index);
+  gicc::DeviceCtx* ctx = rt.prepare(peer, buf.index);
+  gicc::Barrier barrier(rt);
+  barrier.setup();
+  kernel<<<1, 32>>>(ctx, buf.addr, buf.lkey, remote.addr, remote.rkey, 4096, barrier.device_ctx());
+  barrier.wait_completion();
+  rt.barrier();
+  rt.reset();
+  return 0;
+}
+""")
+    p = subprocess.run([NVCC, "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", f"-I{INC}",
+                        "--expt-relaxed-constexpr", "-c", str(src), "-o", str(tmp_path / "app.o")],
+                       capture_output=True, text=True, timeout=600)
+    assert p.returncode == 0, p.stderr[-3000:]
