@@ -67,6 +67,19 @@ int main() {
   barrier.setup();
   kernel<<<1, 32>>>(ctx, buf.addr, buf.lkey, remote.addr, remote.rkey, 4096, barrier.device_ctx());
   barrier.wait_completion();
+  // OFI-style host queue: put_no_db -> Token, prepare_trigger, device flush, host wait
+  gicc::Token t = rt.put_no_db(buf, peer, buf.index, 4096, 0, 0);
+  gicc::DeviceCtx* tctx = rt.prepare_trigger(t);
+  kernel<<<1, 32>>>(tctx, buf.addr, buf.lkey, remote.addr, remote.rkey, 0, barrier.device_ctx());
+  rt.wait(t);
+  // continuous barrier mode
+  barrier.start_continuous(100);
+  barrier.wait_continuous();
+  // active messages
+  gicc::am::Am am(rt);
+  gicc::am::am_args_t args{};
+  am.send_handle(peer, 1, args);
+  am.poll_once();
   rt.barrier();
   rt.reset();
   return 0;
