@@ -46,6 +46,14 @@ def test_reference_style_program_compiles(tmp_path):
     src.write_text(r"""
 #include <gicc/gicc.hpp>
 #include <gicc/gicc_device.cuh>
+#include <gicc/gicc_types.hpp>
+__global__ void simple(gicc::GiccContext* ctx, float* x, size_t n, int peer) {
+  float* dst = static_cast<float*>(gicc::remote_ptr(ctx, x, peer));
+  gicc::put(ctx, dst, x, (uint32_t)(n * sizeof(float)), peer);
+  gicc::put_no_db(ctx, dst, x, (uint32_t)(n * sizeof(float)), peer);
+  gicc::flush(ctx, peer);
+  gicc::quiet(ctx, peer);
+}
 __global__ void kernel(gicc::DeviceCtx* ctx, uint64_t laddr, uint32_t lkey, uint64_t raddr, uint32_t rkey,
                        uint32_t size, gicc::BarrierCtx* bar) {
   gicc::put(ctx, laddr, lkey, raddr, rkey, size);
@@ -82,6 +90,13 @@ int main() {
   am.poll_once();
   rt.barrier();
   rt.reset();
+  // NVSHMEM-style simplified API
+  gicc::init();
+  float* x = static_cast<float*>(gicc::malloc(1 << 20));
+  simple<<<1, 32>>>(gicc::context(), x, 1024, (gicc::my_pe() + 1) % gicc::n_pes());
+  gicc::barrier();
+  gicc::free(x);
+  gicc::finalize();
   return 0;
 }
 """)
