@@ -104,3 +104,15 @@ int main() {
                         "--expt-relaxed-constexpr", "-c", str(src), "-o", str(tmp_path / "app.o")],
                        capture_output=True, text=True, timeout=600)
     assert p.returncode == 0, p.stderr[-3000:]
+
+
+def test_c_api_headers_under_reference_names(tmp_path):
+    """Programs include "gda.h" / "gda_barrier_proxy.h" with include/ and include/gda on the
+    path (the CMake target exports both), as the reference's C API programs do."""
+    if shutil.which("g++") is None:
+        pytest.skip("no g++")
+    src = tmp_path / "c.cpp"
+    src.write_text('#include "gda.h"\n#include "gda_barrier_proxy.h"\nint main() { return gda_rank() < -1; }\n')
+    p = subprocess.run(["g++", "-std=c++17", f"-I{INC}", f"-I{os.path.join(INC, 'gda')}", "-I/usr/local/cuda/include",
+                        "-fsyntax-only", str(src)], capture_output=True, text=True, timeout=300)
+    assert p.returncode == 0, p.stderr[-3000:]
