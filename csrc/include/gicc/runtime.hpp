@@ -42,6 +42,10 @@ class GICC_EXPORT Runtime {
  public:
   Runtime();  // bootstrap from the environment
   explicit Runtime(std::shared_ptr<Bootstrap> boot, RuntimeOptions opt = RuntimeOptions());
+  // Over a Bootstrap the caller owns and keeps alive (the reference's OFI programs build
+  // their transport this way: gicc::Fabric comm(boot)).
+  explicit Runtime(Bootstrap& boot, RuntimeOptions opt = RuntimeOptions());
+  Runtime& fabric() { return *this; }  // the reference's accessor of its transport object
   ~Runtime();
   Runtime(const Runtime&) = delete;
   Runtime& operator=(const Runtime&) = delete;
@@ -138,6 +142,10 @@ struct P2PLink {
 };
 // Every ordered pair of the GPUs visible to this process (no runtime needed).
 GICC_EXPORT std::vector<P2PLink> p2p_links();
+
+// The reference's OFI programs name their transport object gicc::Fabric; here the Runtime
+// is that object.
+using Fabric = Runtime;
 
 // The collective consistency check exchange() runs before any handle crosses a process
 // boundary: every rank registered the same number of buffers since the last exchange, with

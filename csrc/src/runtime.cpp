@@ -63,6 +63,8 @@ Runtime::Runtime() : Runtime(std::make_shared<Bootstrap>()) {}
 
 Runtime::Runtime(std::shared_ptr<Bootstrap> boot, RuntimeOptions opt) : boot_(std::move(boot)) { init(opt); }
 
+Runtime::Runtime(Bootstrap& boot, RuntimeOptions opt) : boot_(&boot, [](Bootstrap*) {}) { init(opt); }
+
 void Runtime::init(RuntimeOptions opt) {
   NvtxRange nvtx("gicc::Runtime::init");
   const Config cfg = config();  // validates every GICC_* variable (throws on a bad one)

@@ -83,6 +83,13 @@ int main() {
   // continuous barrier mode
   barrier.start_continuous(100);
   barrier.wait_continuous();
+  // the OFI programs' spelling: a transport over a caller-owned bootstrap
+  {
+    gicc::Bootstrap boot;
+    gicc::Fabric comm(boot);
+    gicc::Barrier b2(comm.fabric());
+    (void)comm.gpu_id();
+  }
   // active messages
   gicc::am::Am am(rt);
   gicc::am::am_args_t args{};
