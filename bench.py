@@ -38,6 +38,76 @@ def reference_unavailable(args) -> None:
     }))
 
 
+def check_numerics(model, A, B, Afull, Bfull, mode, world, rank) -> float:
+    """One call, then a 256-row block of this rank's output against fp32.  AG mode with
+    several ranks checks rows of the NEXT rank's shard (data that crossed NVLink); RS mode
+    checks this rank's rows (every rank's partial is in them).  Max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    C = model(A, B)
+    torch.cuda.synchronize()
+    if mode == "ag":
+        Ms, Ns = Afull.shape[0] // world, Bfull.shape[0] // world
+        r0 = ((rank + 1) % world) * Ms + (Ms // 2 if world > 1 else 0)
+        rows = slice(r0, r0 + 256)
+        ref = Afull[rows].float() @ Bfull[rank * Ns:(rank + 1) * Ns].float().t()
+        got = C[rows].float()
+    else:
+        Mr = Afull.shape[0] // world
+        ref = Afull[rank * Mr:rank * Mr + 256].float() @ Bfull.float().t()
+        got = C[0:256].float()
+    rel = torch.tensor([((got - ref).norm() / ref.norm()).item()], device=A.device)
+    if world > 1:
+        dist.all_reduce(rel, op=dist.ReduceOp.MAX)
+    return float(rel.item())
+
+
+def timed_run(step, steps, warmup, world, local_rank):
+    """W untimed steps, then K steps between a barrier + synchronize on both sides, timed
+    with CUDA events on the launching stream (one event per step boundary, which adds no
+    synchronisation).  Returns (ms per step, max over ranks; per-step ms summary of the
+    slowest rank; clock record during the timed steps, all ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from opengda_b200.utils.clocks import ClockSampler
+    from opengda_b200.utils.timing import max_over_ranks
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    with ClockSampler([local_rank]) as cs:
+        ev[0].record()
+        for i in range(steps):
+            step()
+            ev[i + 1].record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    per = sorted(ev[i].elapsed_time(ev[i + 1]) for i in range(steps))
+    total = ev[0].elapsed_time(ev[steps]) / steps
+    ms = max_over_ranks(total)
+    summ = {"min": round(per[0], 4), "p50": round(per[len(per) // 2], 4), "max": round(per[-1], 4)}
+    clocks = cs.summary()
+    if world > 1:
+        allc = [None] * world
+        dist.all_gather_object(allc, (clocks, total, summ))
+        slowest = max(range(world), key=lambda q: allc[q][1])
+        summ = dict(allc[slowest][2], rank=slowest)
+        cl = [c[0] for c in allc]
+        sm = [c["sm_mhz"] for c in cl if c.get("sm_mhz")]
+        reasons = sorted({r for c in cl for r in c.get("reasons", [])})
+        clocks = {"sm_mhz": min(sm) if sm else None, "sm_max_mhz": cl[0].get("sm_max_mhz"), "reasons": reasons,
+                  "per_rank_sm_mhz": sm}
+    return ms, summ, clocks
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -49,6 +119,7 @@ def main() -> int:
     ap.add_argument("--size", type=int, default=16384)
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--unfused", action="store_true", help="decomposed path: copy kernels + GEMM (A/B only)")
+    ap.add_argument("--no-nccl-arm", action="store_true", help="skip the same-run NCCL(+cuBLAS) comparison arm")
     ap.add_argument("--transfer", default="sm", choices=["sm", "ce"],
                     help="fused AG: SM pushes (NVLS multicast or unicast) or copy engines (A/B option)")
     args = ap.parse_args()
@@ -78,7 +149,6 @@ def main() -> int:
         rt = Runtime()
 
     from opengda_b200.models.dist_gemm import DistGemm, make_operands
-    from opengda_b200.utils.clocks import ClockSampler
 
     M = N = K = args.size
     if args.impl == "nccl":
@@ -89,19 +159,7 @@ def main() -> int:
         model = DistGemm(M, N, K, args.mode, rt=rt, device=dev, fused=not args.unfused,
                          transfer=args.transfer if args.mode == "ag" else "sm")
     A, B, (Afull, Bfull) = make_operands(M, N, K, args.mode, world, rank, seed=2, device=dev)
-    # numerics spot check (one row block) before timing
-    C = model(A, B)
-    torch.cuda.synchronize()
-    rows = slice(0, 256)
-    if args.mode == "ag":
-        Ns = N // world
-        ref = Afull[rows].float() @ Bfull[rank * Ns:(rank + 1) * Ns].float().t()
-        got = C[rows].float()
-    else:
-        Mr = M // world
-        ref = Afull[rank * Mr:rank * Mr + 256].float() @ Bfull.float().t()
-        got = C[rows].float()
-    rel = ((got - ref).norm() / ref.norm()).item()
+    rel = check_numerics(model, A, B, Afull, Bfull, args.mode, world, rank)
     del Afull, Bfull
     torch.cuda.empty_cache()
     zero_copy = world > 1 and args.mode == "ag" and args.impl == "ours"
@@ -112,28 +170,9 @@ def main() -> int:
     def step():
         model(model.a_slot() if zero_copy else A, B)
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler([local_rank]) as cs:
-        s.record()
-        for _ in range(args.steps):
-            step()
-        e.record()
-        torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / args.steps
+    ms, step_ms, clocks = timed_run(step, args.steps, args.warmup, world, local_rank)
     if rt is not None:
         rt.check_device_errors()
-    from opengda_b200.utils.timing import max_over_ranks
-
-    ms = max_over_ranks(ms)
     flops = 2.0 * M * N * K
     value = flops / (ms * 1e-3) / 1e12
 
@@ -168,14 +207,24 @@ def main() -> int:
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(es.elapsed_time(ee) / e2e_steps)
 
-    clocks = cs.summary()
-    if world > 1:
-        allc = [None] * world
-        dist.all_gather_object(allc, clocks)
-        sm = [c["sm_mhz"] for c in allc if c.get("sm_mhz")]
-        reasons = sorted({r for c in allc for r in c.get("reasons", [])})
-        clocks = {"sm_mhz": min(sm) if sm else None, "sm_max_mhz": allc[0].get("sm_max_mhz"), "reasons": reasons,
-                  "per_rank_sm_mhz": sm}
+    # ---- the NCCL (+cuBLAS) arm, same process, same shapes, steps, warm-up and clock record
+    arm = None
+    if args.impl == "ours" and not args.no_nccl_arm:
+        from opengda_b200.baselines.gemm_nccl import NcclDistGemm
+
+        del feeder, A_host
+        base = NcclDistGemm(M, N, K, args.mode, device=dev)
+        base_rel = check_numerics(base, A, B, *make_operands(M, N, K, args.mode, world, rank, seed=2, device=dev)[2],
+                                  args.mode, world, rank)
+        torch.cuda.empty_cache()
+        b_ms, b_step_ms, b_clocks = timed_run(lambda: base(A, B), args.steps, args.warmup, world, local_rank)
+        arm = {"impl": "nccl+cublas", "what": ("all_gather_into_tensor + torch.matmul" if args.mode == "ag"
+                                               else "torch.matmul + reduce_scatter_tensor") if world > 1
+               else "torch.matmul (cuBLAS)",
+               "value": round(flops / (b_ms * 1e-3) / 1e12, 2), "ms_per_step": round(b_ms, 4),
+               "step_ms": b_step_ms, "clocks": b_clocks, "numerics_rel_err_vs_fp32": round(base_rel, 6)}
+        del base
+        torch.cuda.empty_cache()
     if rank == 0:
         out = {
             "metric": METRIC,
@@ -188,7 +237,9 @@ def main() -> int:
             "ms_per_step": round(ms, 4),
             "higher_is_better": True,
             "scaling": "strong",
-            "vs_baseline": None,
+            # same-run NCCL(+cuBLAS) arm: its time / ours (> 1: this framework is faster)
+            "vs_baseline": round(value / arm["value"], 4) if arm else None,
+            "vs_baseline_of": "same-run NCCL+cuBLAS arm (nccl_arm)" if arm else None,
             "dtype": "bf16",
             "data": "synthetic: A, B ~ N(0, 1/sqrt(K)) from seed 2, random-init (no dataset)",
             "config": {
@@ -200,6 +251,9 @@ def main() -> int:
                              model.transfer + ("-nvls" if model.nvls else "")),
                 "l2": "inputs exceed L2 (A_full 512 MiB > 126 MB), no flush",
                 "numerics_rel_err_vs_fp32": round(rel, 6),
+                "numerics_rows": ("256 rows of the next rank's shard (gathered data), max over ranks"
+                                  if args.mode == "ag" and world > 1 else "256 rows of each rank's output, max over ranks"),
+                "step_ms": step_ms,
             },
             "impl": args.impl,
             "clocks": clocks,
@@ -208,6 +262,7 @@ def main() -> int:
                     "api": ("opengda_b200.baselines.gemm_nccl.NcclDistGemm.__call__" if args.impl == "nccl"
                             else "opengda_b200.models.dist_gemm.DistGemm.__call__")},
             "gpu_launches": model.launches_per_step * args.steps,
+            "nccl_arm": arm,
         }
         print(json.dumps(out))
     if world > 1:

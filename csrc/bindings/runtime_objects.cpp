@@ -324,7 +324,8 @@ void bind_runtime_objects(py::module_& m) {
      py::arg("units_per_band"), py::arg("grid"), py::arg("timeout_ns"), py::arg("trace") = 0, py::arg("diag") = 0,
      py::arg("comm_ctas") = 0, py::arg("tile_counter") = 0, py::arg("a_mc") = 0, py::arg("arrivals_mc") = 0);
   m.def("ag_transfer_ce", [](int n, int r, int M, int K, std::vector<uint64_t> a_full, std::vector<uint64_t> arrivals,
-                             uint64_t done_local, uint64_t epoch, int grid, int units_per_band, int chunks) {
+                             uint64_t done_local, uint64_t epoch, int grid, int units_per_band, int chunks,
+                             uint64_t timeout_ns) {
     if ((int)a_full.size() != n || (int)arrivals.size() != n || n > 16)
       throw std::runtime_error("ag_transfer_ce: per-rank pointer lists must have n <= 16 entries");
     ops::AgCeArgs a;
@@ -335,9 +336,11 @@ void bind_runtime_objects(py::module_& m) {
     }
     a.done_local = P<const uint64_t>(done_local);
     a.epoch = epoch; a.grid = grid; a.units_per_band = units_per_band; a.chunks = chunks;
+    a.timeout_ns = timeout_ns;
     ops::ag_transfer_ce(a, cur_stream());
   }, py::arg("n"), py::arg("r"), py::arg("M"), py::arg("K"), py::arg("a_full"), py::arg("arrivals"),
-     py::arg("done_local"), py::arg("epoch"), py::arg("grid"), py::arg("units_per_band"), py::arg("chunks"));
+     py::arg("done_local"), py::arg("epoch"), py::arg("grid"), py::arg("units_per_band"), py::arg("chunks"),
+     py::arg("timeout_ns") = 0);
   m.def("k_gemm_rs", [](int n, int r, int M, int N, int K, uint64_t A, long long lda, uint64_t B, long long ldb,
                         std::vector<uint64_t> slots, std::vector<uint64_t> arrivals, std::vector<uint64_t> done,
                         uint64_t out, long long ldo, uint64_t epoch, int grid, uint64_t timeout_ns,

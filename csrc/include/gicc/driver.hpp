@@ -38,7 +38,6 @@ struct DriverApi {
   CUresult (*DeviceGetAttribute)(int*, CUdevice_attribute, CUdevice) = nullptr;
   CUresult (*DeviceGet)(CUdevice*, int) = nullptr;
   CUresult (*StreamWriteValue64)(CUstream, CUdeviceptr, cuuint64_t, unsigned int) = nullptr;
-  CUresult (*StreamWaitValue64)(CUstream, CUdeviceptr, cuuint64_t, unsigned int) = nullptr;
 };
 
 GICC_EXPORT const DriverApi& driver();  // resolves on first use; throws if no driver

@@ -25,7 +25,12 @@
  *
  * Set-up: the first call on a device looks up the array's device address with
  * cudaGetSymbolAddress (with that device current) and caches it.  Make that first call
- * before capturing a stream into a CUDA graph.
+ * before capturing a stream into a CUDA graph.  The cached address is not refreshed
+ * after cudaDeviceReset (or any other teardown of the device's primary context): do not
+ * call this entry point on a device after resetting it in the same process.
+ *
+ * Aliasing: a and b must be two separate fields (the sweep reads the neighbours of cells
+ * it writes); overlapping fields are rejected with cudaErrorInvalidValue.
  *
  * Concurrency: all calls share the one array.  Calls that overlap on the GPU (different
  * streams, or different host threads) race on it and may return wrong norms; serialise

@@ -250,9 +250,8 @@ GICC_EXPORT void put_tile_test(void* dst, int tiles, uint32_t tile_bytes, uint32
 // landing buffer with cudaMemcpyAsync, `chunks` pieces per peer, and after each piece write
 // d's arrival counters of its bands to epoch * units_per_band.  No SM issues NVLink
 // traffic; launch ag_gemm with diag bit 1 (external transfer) on another stream.
-// The peer-progress wait is a stream memory operation and has no time bound: if a peer
-// stops for good, stream `s` waits (the consumer kernels still end with ETIMEDOUT).  The
-// SM-push path keeps every wait bounded and is the default.
+// The peer-progress wait is a one-thread kernel on `s` bounded by timeout_ns (0 = the
+// configured default); on timeout it records GICC_ETIMEDOUT and the copies go ahead.
 struct AgCeArgs {
   int n = 0, r = 0, M = 0, K = 0;
   void* a_full[16] = {};        // each rank's landing buffer (current parity), mapped here
@@ -262,6 +261,7 @@ struct AgCeArgs {
   int grid = 0;                 // CTAs of the ag_gemm launch (done-counter unit)
   int units_per_band = 4;
   int chunks = 4;               // copies per peer (each followed by its bands' counters)
+  uint64_t timeout_ns = 0;      // bound of the peer-progress wait (0 = default)
 };
 GICC_EXPORT void ag_transfer_ce(const AgCeArgs& a, cudaStream_t s);
 GICC_EXPORT void ag_gemm(const AgGemmArgs& a, cudaStream_t s);

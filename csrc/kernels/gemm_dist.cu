@@ -768,17 +768,19 @@ void ag_transfer_ce(const AgCeArgs& a, cudaStream_t s) {
   using namespace gemm;
   if (a.n < 2 || a.n > kMaxR || a.M % (a.n * BM)) throw std::runtime_error("gicc::ag_transfer_ce: bad shape");
   const DriverApi& d = driver();
-  if (!d.StreamWaitValue64 || !d.StreamWriteValue64)
-    throw std::runtime_error("gicc::ag_transfer_ce: stream memory operations unavailable");
+  if (!d.StreamWriteValue64) throw std::runtime_error("gicc::ag_transfer_ce: stream memory operations unavailable");
+  const uint64_t timeout_ns = a.timeout_ns ? a.timeout_ns : default_timeout_ns();
   const int Ms = a.M / a.n, nb = Ms / BM;
   const int chunks = a.chunks > 0 && a.chunks <= nb ? a.chunks : 1;
   const size_t row_bytes = (size_t)a.K * 2;
   const uint64_t target = a.epoch * (uint64_t)(a.units_per_band > 0 ? a.units_per_band : 4);
   for (int k = 1; k < a.n; ++k) {
     const int dst = (a.r - k + a.n) % a.n;
-    if (a.epoch > 2)  // dst finished the call that last used this parity (its CTAs' exit counts)
-      GICC_DRV(d.StreamWaitValue64(s, reinterpret_cast<CUdeviceptr>(a.done_local + dst),
-                                   (a.epoch - 2) * (uint64_t)a.grid, CU_STREAM_WAIT_VALUE_GEQ));
+    // dst finished the call that last used this parity (its CTAs' exit counts).  The wait
+    // is a one-thread kernel bounded by timeout_ns: on timeout it records GICC_ETIMEDOUT in
+    // the device error record (read by the host after the call) and the stream goes on.
+    if (a.epoch > 2)
+      wait_signal(a.done_local + dst, proto::CMP_GE, (a.epoch - 2) * (uint64_t)a.grid, timeout_ns, nullptr, s);
     for (int c = 0; c < chunks; ++c) {
       const int b0 = nb * c / chunks, b1 = nb * (c + 1) / chunks;
       const size_t off = ((size_t)a.r * Ms + (size_t)b0 * BM) * row_bytes;

@@ -124,12 +124,20 @@ extern "C" __attribute__((visibility("default"))) cudaError_t gicc_jacobi_step_n
                          "16-byte aligned fields)\n");
     return cudaErrorInvalidValue;
   }
-  const long long blocks = (long long)((nx + kColsPerCta - 1) / kColsPerCta) * ((rows + kRun - 1) / kRun);
+  // 64-bit arithmetic: nx and rows near INT_MAX must fail the size check below, not wrap.
+  const long long blocks = (((long long)nx + kColsPerCta - 1) / kColsPerCta) * (((long long)rows + kRun - 1) / kRun);
   if (blocks > GICC_NOALLOC_MAX_BLOCKS) {
     std::fprintf(stderr,
                  "gicc_jacobi_step_norm_noalloc: %d x %d cells need %lld partial sums, more than the %d this "
                  "entry point holds (at most 32768 x 32768 cells)\n",
                  nx, rows, blocks, GICC_NOALLOC_MAX_BLOCKS);
+    return cudaErrorInvalidValue;
+  }
+  const size_t field_bytes = ((size_t)rows + 2) * (size_t)nx * sizeof(float);
+  const uintptr_t pa = reinterpret_cast<uintptr_t>(a), pb = reinterpret_cast<uintptr_t>(b);
+  if (pa < pb + field_bytes && pb < pa + field_bytes) {
+    std::fprintf(stderr, "gicc_jacobi_step_norm_noalloc: the input and output fields overlap (the sweep reads "
+                         "neighbours of cells it writes; pass two separate fields)\n");
     return cudaErrorInvalidValue;
   }
   double* partials = nullptr;

@@ -49,7 +49,6 @@ const DriverApi& driver() {
       resolve("cuDeviceGetAttribute", api.DeviceGetAttribute);
       resolve("cuDeviceGet", api.DeviceGet);
       resolve("cuStreamWriteValue64", api.StreamWriteValue64, false);
-      resolve("cuStreamWaitValue64", api.StreamWaitValue64, false);
     } catch (const std::exception& e) {
       err = e.what();
     }

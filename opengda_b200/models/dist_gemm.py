@@ -203,7 +203,7 @@ class DistGemm:
                     grid = self.grid or torch.cuda.get_device_properties(self.device).multi_processor_count
                     with torch.cuda.stream(self._side):
                         n.ag_transfer_ce(w, r, self.M, self.K, ptrs, self.arrivals, self.done[r], self.epoch, grid,
-                                         self.units_per_band, self.ce_chunks)
+                                         self.units_per_band, self.ce_chunks, self.rt.timeout_ns)
                     done_ev = torch.cuda.Event()
                     done_ev.record(self._side)
                 n.k_ag_gemm(w, r, self.M, self.N // w, self.K, ptrs, B.data_ptr(),

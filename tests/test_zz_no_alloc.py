@@ -28,12 +28,15 @@ def _entry():
     return fn
 
 
-def test_noalloc_jacobi_matches_regular_entry_point_twice():
+@pytest.mark.parametrize("nx, ny", [(2048, 1030), (2052, 37)])
+def test_noalloc_jacobi_matches_regular_entry_point_twice(nx, ny):
+    """nx = 2048 fills every lane of every block; nx = 2052 (not a multiple of the 128
+    columns a warp covers) leaves most lanes of the last block idle, and ny = 37 leaves the
+    last row block short."""
     from opengda_b200 import native
 
     fn = _entry()
     n = native()
-    nx, ny = 2048, 1030
     rows = ny - 2
     a = torch.empty(rows + 2, nx, dtype=torch.float32, device="cuda")
     n.k_jacobi_init(a.data_ptr(), 0, nx, ny, rows, 1, 3)
@@ -60,4 +63,8 @@ def test_noalloc_rejects_oversized_grid():
     # 65536 columns x 32768 rows needs 64 x 2048 = 131072 partial sums > 65536
     rc = fn(a.data_ptr(), a.data_ptr(), 65536, 32768, norm.data_ptr(), torch.cuda.current_stream().cuda_stream)
     assert rc == 1  # cudaErrorInvalidValue, nothing launched
+    # input and output must not overlap (the sweep would read cells it already rewrote)
+    f = torch.zeros(10 * 64, dtype=torch.float32, device="cuda")
+    rc = fn(f.data_ptr(), f.data_ptr(), 64, 8, norm.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 1
     torch.cuda.synchronize()
