@@ -205,6 +205,8 @@ def main() -> int:
     e2e_run(e2e_steps)
     ee.record()
     torch.cuda.synchronize()
+    from opengda_b200.utils.timing import max_over_ranks
+
     e2e_ms = max_over_ranks(es.elapsed_time(ee) / e2e_steps)
 
     # ---- the NCCL (+cuBLAS) arm, same process, same shapes, steps, warm-up and clock record

@@ -72,6 +72,8 @@ def main():
     rt = Runtime()
     right, left = (r + 1) % n, (r - 1) % n
     results = {"n_gpus": n, "nvls": rt.multicast_supported, "gpu": torch.cuda.get_device_name()}
+    from opengda_b200.utils.clocks import BenchClocks
+    clk = BenchClocks(local)
 
     # ---------------- put / get bandwidth ----------------
     maxb = 1 << args.max_put
@@ -229,6 +231,7 @@ def main():
         results["reduce_scatter_all_gather"] = rows
         rt.check_device_errors()
         ar = None
+    results["clocks"] = clk.finish()
     if r == 0:
         js = json.dumps(results)
         print(js)

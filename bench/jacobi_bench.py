@@ -44,6 +44,9 @@ def main():
     from opengda_b200.models.jacobi import Jacobi
     from opengda_b200.utils.timing import max_over_ranks
 
+    from opengda_b200.utils.clocks import BenchClocks
+
+    clk = BenchClocks(local)
     jac = Jacobi(args.nx, args.ny, rt=rt, persistent=args.persistent)
     jac.run(5)  # warm-up
     torch.cuda.synchronize()
@@ -95,6 +98,7 @@ def main():
         res["nccl"] = {"total_s_scaled_to_iters": ms_n / it_n * args.iters / 1e3, "ms_per_iter": ms_n / it_n}
         # numerics: fused and NCCL fields agree after the same number of iterations? (different
         # iteration counts here; equality is covered by the tests)
+    res["clocks"] = clk.finish()
     if rank == 0:
         js = json.dumps(res)
         print(js)

@@ -52,6 +52,9 @@ def main():
     from opengda_b200.models.moe import MoELayer, make_inputs
     from opengda_b200.utils.timing import max_over_ranks
 
+    from opengda_b200.utils.clocks import BenchClocks
+
+    clk = BenchClocks(local)
     layer = MoELayer(args.tokens, args.hidden, args.experts, args.topk, args.inter, rt=rt)
     layer.dispatch_ctas = args.dispatch_ctas
     layer.combine_ctas = args.combine_ctas
@@ -90,6 +93,7 @@ def main():
             base = NcclMoE(layer)
             ms_b = timeit(lambda: base.dispatch_combine(x, logits), max(2, args.steps // 2), 1)
             res["nccl_torch"] = {"us": ms_b * 1e3}
+        res["clocks"] = clk.finish()
         if rank == 0:
             print(json.dumps(res))
             if args.out:
@@ -120,6 +124,7 @@ def main():
         res["rel_err_vs_baseline"] = float(((ours - ref).norm() / ref.norm()).item())
         ms_b = timeit(lambda: base(x, logits), max(2, args.steps // 2), 1)
         res["nccl_torch"] = {"layer_us": ms_b * 1e3, "tflops_total": layer.flops() * world / (ms_b * 1e-3) / 1e12}
+    res["clocks"] = clk.finish()
     if rank == 0:
         js = json.dumps(res)
         print(js)

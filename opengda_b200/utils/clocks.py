@@ -91,3 +91,36 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(r[1] for r in loaded), "sm_max_mhz": mx,
                 "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def gather_clock_summary(summary: dict) -> dict:
+    """Combine every rank's ``ClockSampler.summary()`` (collective over the default
+    torch.distributed group when it is initialised): the lowest per-rank median SM clock,
+    the union of throttle reasons and the per-rank medians."""
+    try:
+        import torch.distributed as dist
+        multi = dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1
+    except Exception:  # pragma: no cover
+        multi = False
+    if not multi:
+        return summary
+    allc = [None] * dist.get_world_size()
+    dist.all_gather_object(allc, summary)
+    sm = [c.get("sm_mhz") for c in allc]
+    known = [v for v in sm if v]
+    return {"sm_mhz": min(known) if known else None, "sm_max_mhz": allc[0].get("sm_max_mhz"),
+            "reasons": sorted({r for c in allc for r in c.get("reasons", [])}), "per_rank_sm_mhz": sm}
+
+
+class BenchClocks:
+    """Clock record for a whole benchmark run: ``clk = BenchClocks(local_gpu)`` starts
+    sampling; ``clk.finish()`` (a collective when several ranks run) stops it and returns
+    the combined record, to be embedded in the benchmark's JSON."""
+
+    def __init__(self, gpu: int, period_ms: int = 100):
+        self._cs = ClockSampler([gpu], period_ms=period_ms)
+        self._cs.__enter__()
+
+    def finish(self) -> dict:
+        self._cs.__exit__(None, None, None)
+        return gather_clock_summary(self._cs.summary())

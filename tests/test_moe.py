@@ -1,7 +1,5 @@
 """MoE layer: routing kernel and the full fused forward (one GPU: every expert local)
 against an fp32 PyTorch reference."""
-import os
-
 import pytest
 import torch
 
@@ -41,8 +39,6 @@ def test_moe_forward_single_gpu(T, H, E, k, I):
         assert rel < 2e-2, (call, rel)
 
 
-@pytest.mark.skipif(not os.environ.get("GICC_TEST_NOT_YET_RUN"),
-                    reason="not yet run on a GPU: set GICC_TEST_NOT_YET_RUN=1")
 @pytest.mark.parametrize("dispatch_ctas,combine_ctas", [(8, 0), (0, 8), (8, 8)])
 def test_moe_forward_confined_options(dispatch_ctas, combine_ctas):
     """The A/B options that confine NVLink stores to a few CTAs (dynamic tiles in both grouped

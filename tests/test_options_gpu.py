@@ -1,19 +1,16 @@
-"""GPU checks of kernels and options that compile and whose host logic is tested on CPU,
-but that have not yet run on a GPU: the ring-stripe fp32 matmul (one GPU and a ring of
-ranks), the copy-engine all-gather GEMM, the reduce-scatter join, and the MoE layer with
-confined dispatch and staged combine, the persistent Jacobi kernel, and allreduce
-replayed from a CUDA graph.  They run only with GICC_TEST_NOT_YET_RUN=1; once a
-check has passed on a B200 it moves into the regular GPU suites."""
+"""GPU checks of options and secondary kernels: the ring-stripe fp32 matmul (one GPU and a
+ring of ranks), the copy-engine all-gather GEMM, the reduce-scatter join and raster-group
+options, the MoE layer with confined dispatch and staged combine, the persistent Jacobi
+kernel, allreduce replayed from a CUDA graph, the bulk tile put, the native example
+programs on several ranks, and rank loss between steps detected on the host."""
 import json
 import os
 import sys
 
 import pytest
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(not os.environ.get("GICC_TEST_NOT_YET_RUN"),
-                                 reason="not yet run on a GPU: set GICC_TEST_NOT_YET_RUN=1")]
-WORKER = os.path.join(os.path.dirname(__file__), "workers", "pending_worker.py")
+pytestmark = [pytest.mark.gpu]
+WORKER = os.path.join(os.path.dirname(__file__), "workers", "options_worker.py")
 
 
 def test_ring_mm_single_gpu_matches_fp64():

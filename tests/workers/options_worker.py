@@ -1,5 +1,5 @@
-"""Rank program for the multi-GPU checks of the options and kernels that have not yet run
-on a GPU (launched by opengda_b200.parallel.launch; one JSON result per rank):
+"""Rank program for the multi-GPU checks of the options and secondary kernels
+(launched by opengda_b200.parallel.launch; one JSON result per rank):
 
 * the ring-stripe fp32 matmul (RingMatmul) against an fp64 product of the full matrices;
 * the fused all-gather GEMM with the copy-engine transfer (transfer="ce");
