@@ -1,21 +1,33 @@
 // gemm_core2.cuh -- persistent tcgen05 GEMM core on CTA pairs (cta_group::2).
 //
-// A cluster of two CTAs on neighbouring SMs computes one 256 x BN2 output tile:
-//   * each CTA TMA-loads its own 128 rows of A and its own BN2/2 rows of B (no multicast:
-//     every load reads this GPU's memory); both CTAs' loads complete on the leader CTA's
-//     "full" mbarrier (cta_group::2 form of cp.async.bulk.tensor);
-//   * one thread of the leader issues tcgen05.mma.cta_group::2 (M=256, N=BN2, K=16), which
-//     reads both CTAs' shared memory and accumulates into both CTAs' TMEM (each CTA holds
-//     its 128 rows x BN2 columns, double-buffered: 2 x BN2 columns);
+// A cluster of two CTAs on neighbouring SMs computes one 256 x (NH*256) output tile:
+//   * each CTA TMA-loads its own 128 rows of A and, for each of the NH column halves, its
+//     own 128 rows of B (no multicast: every load reads this GPU's memory); both CTAs'
+//     loads complete on the leader CTA's "full" mbarrier (cta_group::2 form of
+//     cp.async.bulk.tensor);
+//   * one thread of the leader issues tcgen05.mma.cta_group::2 (M=256, N=256, K=16) NH
+//     times per k-step (the A tile is shared by the NH halves), which reads both CTAs'
+//     shared memory and accumulates into both CTAs' TMEM (each CTA holds its 128 rows x
+//     NH*256 columns);
+//   * NH = 1: the accumulator is double-buffered (2 x 256 of the 512 TMEM columns), so the
+//     epilogue of tile i overlaps the MMAs of tile i+1;
+//     NH = 2: one 512-column accumulator (all of TMEM), drained by 8 epilogue warps (two
+//     per TMEM lane quarter, one per column half) while the producer already loads the
+//     next tile's operands;
 //   * the leader's tcgen05.commit arrives on the barrier of each CTA (two commits, no
 //     multicast form), and the peer CTA's epilogue warps arrive on the leader's
 //     "accumulator free" barrier remotely.
-// Per SM and k-step this moves 16 KB of A and 16 KB of B instead of 16 KB + 32 KB for a
-// 128 x 256 single-CTA tile with the same tensor work, i.e. a third less L2 -> SMEM traffic.
+// Shared-memory traffic per SM and k-step (64 deep), per 128 x 256 block of output:
+//   single-CTA 128 x 256 tile: 16 KB of A + 32 KB of B = 48 KB;
+//   pair, NH = 1:             16 KB of A + 16 KB of B = 32 KB;
+//   pair, NH = 2:            (16 KB of A + 32 KB of B) / 2 = 24 KB,
+// and the shared-memory ring (192 KB) covers 2, 3 and 4 k-steps of MMA time respectively,
+// so the wider tile both halves the L2 -> SMEM bytes per FLOP of the single-CTA kernel and
+// doubles the load latency it tolerates.
 //
-// Warp roles per CTA as in gemm_core.cuh (192 threads): 0 producer, 1 TMEM + MMA (leader
-// only issues), 2..5 epilogue.  Every wait is bounded; both CTAs always reach the final
-// cluster barrier, after which TMEM is released.
+// Warp roles per CTA: 0 producer, 1 TMEM + MMA (leader only issues), 2.. epilogue.  Every
+// wait is bounded; both CTAs always reach the final cluster barrier, after which TMEM is
+// released.
 #pragma once
 #include <cstdint>
 
@@ -25,13 +37,28 @@ namespace gicc {
 namespace gemm {
 namespace pair {
 
-constexpr int BN2 = 256;  // pair tile width (each CTA loads BN2/2 rows of B)
-constexpr int kStages = 6;
+constexpr int BN2 = 256;  // columns per MMA (each CTA loads BN2/2 rows of B per column half)
 constexpr uint32_t kABytes = BM * BK * 2;          // 16 KB
-constexpr uint32_t kBBytes = (BN2 / 2) * BK * 2;   // 16 KB
-constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr uint32_t kTmemCols = 2 * BN2;            // 512
-constexpr uint32_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
+constexpr uint32_t kBBytes = (BN2 / 2) * BK * 2;   // 16 KB per column half
+
+template <int NH>
+struct PairCfg {
+  static_assert(NH == 1 || NH == 2, "a pair tile has 1 or 2 column halves of 256");
+  static constexpr int kCols = NH * BN2;                  // output columns of a pair tile
+  static constexpr int kAccs = NH == 1 ? 2 : 1;           // TMEM accumulators (2 x 256 or 1 x 512)
+  static constexpr uint32_t kStageBytes = kABytes + NH * kBBytes;
+  static constexpr int kStages = NH == 1 ? 6 : 4;
+  static constexpr int kEpiWarps = 4 * NH;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+};
+// The 256 x 256 configuration's constants, kept under their original names.
+constexpr int kStages = PairCfg<1>::kStages;
+constexpr uint32_t kStageBytes = PairCfg<1>::kStageBytes;
+constexpr uint32_t kTmemCols = PairCfg<1>::kTmemCols;
+constexpr uint32_t kSmemBytes = PairCfg<1>::kSmemBytes;
 
 __device__ __forceinline__ uint32_t cta_rank() {
   uint32_t r;
@@ -81,18 +108,21 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
-// Sched for pairs: tile(t) gives the pair tile (m0 = first of 256 rows, n0 = first of BN2
-// columns, kb range); the core derives each CTA's A row (m0 + 128*rank) and B row
-// (n0 + 64*... BN2/2*rank).  Epi::store gets the CTA-local row (0..127) and column chunk.
-template <class Sched, class Epi>
+// Sched for pairs: tile(t) gives the pair tile (m0 = first of 256 rows, n0 = first of
+// NH*256 columns, kb range); the core derives each CTA's A row (m0 + 128*rank) and B rows
+// (n0 + h*256 + 128*rank for column half h).  Epi::store gets the CTA-local row (0..127)
+// and the column offset within the pair tile.
+template <int NH = 1, class Sched, class Epi>
 __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUtensorMap* tmB, const Sched& sched,
                                                Epi& epi, ErrorRecord* err, uint64_t timeout_ns, int rank) {
-  constexpr int S = kStages;
+  using Cf = PairCfg<NH>;
+  constexpr int S = Cf::kStages;
+  constexpr int kAccs = Cf::kAccs;
   extern __shared__ uint8_t gemm2_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gemm2_smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + S * kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * kStageBytes);
+  uint8_t* sB = smem + S * kABytes;  // per stage: NH consecutive 16 KB boxes (one per column half)
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cf::kStageBytes);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
@@ -114,7 +144,7 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&tfull[a], 1);
-      ptx::mbar_init(&tempty[a], 8);  // 4 epilogue warps x 2 CTAs
+      ptx::mbar_init(&tempty[a], 2 * Cf::kEpiWarps);  // every epilogue warp of both CTAs
     }
     ptx::mbar_init(drain, 1);
     *abort_flag = 0;
@@ -123,7 +153,7 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
     ptx::prefetch_tmap(tmB);
   }
   if (warp == 1) {
-    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_alloc_pair(tmem_slot, Cf::kTmemCols);
     tmem_relinquish_pair();
   }
   ptx::tc_fence_before();
@@ -154,9 +184,12 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
             break;
           }
           const uint32_t bar = map_to(ptx::smem_u32(&full[stage]), 0);
-          if (leader) ptx::mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes);
+          if (leader) ptx::mbar_arrive_expect_tx(&full[stage], 2 * Cf::kStageBytes);
           tma_load_2d_pair(sA + stage * kABytes, tmA, bar, kb * BK, ti.a_row + (int)crank * BM);
-          tma_load_2d_pair(sB + stage * kBBytes, tmB, bar, kb * BK, ti.b_row + (int)crank * (BN2 / 2));
+#pragma unroll
+          for (int h = 0; h < NH; ++h)
+            tma_load_2d_pair(sB + (stage * NH + h) * kBBytes, tmB, bar, kb * BK,
+                             ti.b_row + h * BN2 + (int)crank * (BN2 / 2));
           armed[stage]++;
           if (++stage == S) {
             stage = 0;
@@ -192,7 +225,7 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t d = tmem + acc * BN2;
+        const uint32_t d = tmem + acc * NH * BN2;
         bool ok = true;
         for (int kb = ti.kb0; kb < ti.kb1; ++kb) {
           if (!ptx::mbar_wait(&full[stage], phase, timeout_ns, abort_flag)) {
@@ -201,12 +234,15 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
           }
           ptx::tc_fence_after();
           const uint32_t a0 = ptx::smem_u32(sA + stage * kABytes);
-          const uint32_t b0 = ptx::smem_u32(sB + stage * kBBytes);
+          const uint32_t b0 = ptx::smem_u32(sB + stage * NH * kBBytes);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = ptx::sdesc_kmajor_sw128(a0 + k * 32);
-            const uint64_t bd = ptx::sdesc_kmajor_sw128(b0 + k * 32);
-            mma_pair(d, ad, bd, idesc, (kb > ti.kb0 || k > 0) ? 1u : 0u);
+#pragma unroll
+            for (int h = 0; h < NH; ++h) {
+              const uint64_t bd = ptx::sdesc_kmajor_sw128(b0 + h * kBBytes + k * 32);
+              mma_pair(d + h * BN2, ad, bd, idesc, (kb > ti.kb0 || k > 0) ? 1u : 0u);
+            }
           }
           issued = true;
           const uint32_t e_own = ptx::smem_u32(&empty[stage]);
@@ -225,7 +261,7 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
         const uint32_t f_own = ptx::smem_u32(&tfull[acc]);
         commit_pair(f_own);
         commit_pair(map_to(f_own, peer));
-        if (++acc == 2) {
+        if (++acc == kAccs) {
           acc = 0;
           acc_phase ^= 1;
         }
@@ -236,8 +272,11 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+    // ---------------- epilogue (warps 2.., both CTAs) ----------------
+    // Warp w may read TMEM lanes 32*(w%4)..+31; with NH = 2 warps 2..5 take columns
+    // 0..255 and warps 6..9 columns 256..511 of the same rows.
     const int q = warp & 3;
+    const int half = NH == 1 ? 0 : ((int)warp - 2) / 4;
     const int row = q * 32 + lane;
     const uint32_t tempty_leader0 = map_to(ptx::smem_u32(&tempty[0]), 0);
     const uint32_t tempty_leader1 = map_to(ptx::smem_u32(&tempty[1]), 0);
@@ -252,7 +291,7 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
         break;
       }
       ptx::tc_fence_after();
-      const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + acc * BN2;
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + (acc * NH + half) * BN2;
       epi.begin_tile(ti, row);
 #pragma unroll 1
       for (int c = 0; c < BN2; c += 32) {
@@ -264,10 +303,10 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
           __syncwarp();
           if (lane == 0) arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
         }
-        epi.store(ti, row, c, r);
+        epi.store(ti, row, half * BN2 + c, r);
       }
       epi.end_tile(ti, row);
-      if (++acc == 2) {
+      if (++acc == kAccs) {
         acc = 0;
         acc_phase ^= 1;
       }
@@ -278,7 +317,7 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
   cluster_sync();  // the peer may still arrive on our barriers / the leader's MMAs write our TMEM
   if (warp == 1) {
     ptx::tc_fence_after();
-    tmem_dealloc_pair(tmem, kTmemCols);
+    tmem_dealloc_pair(tmem, Cf::kTmemCols);
   }
 }
 

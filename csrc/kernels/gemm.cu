@@ -108,10 +108,12 @@ static void launch_plain(const void* A, const void* B, void* C, int M, int N, in
   GICC_CUDA(cudaGetLastError());
 }
 
-// ---- CTA-pair (cta_group::2) variant: 256 x 256 tiles per cluster of two CTAs ----
+// ---- CTA-pair (cta_group::2) variants: 256 x 256 (NH = 1) or 256 x 512 (NH = 2) tiles per
+// cluster of two CTAs ----
 struct PairPlainSched {
   int M, N, K;
   int num_m, num_n, group_m;
+  int cols;  // output columns per pair tile (NH * 256)
   static constexpr int kCommWarps = 0;
   __device__ int num_tiles() const { return num_m * num_n; }
   __device__ TileInfo tile(int t) const {
@@ -119,7 +121,7 @@ struct PairPlainSched {
     raster(t, num_m, num_n, group_m, mb, nb);
     TileInfo ti;
     ti.m0 = mb * 2 * BM;
-    ti.n0 = nb * pair::BN2;
+    ti.n0 = nb * cols;
     ti.a_row = ti.m0;
     ti.b_row = ti.n0;
     ti.kb0 = 0;
@@ -131,14 +133,17 @@ struct PairPlainSched {
   __device__ bool producer_wait(const TileInfo&, uint64_t, volatile int*, ErrorRecord*) const { return true; }
 };
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+template <int NH>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::PairCfg<NH>::kThreads, 1)
     k_gemm_bf16_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      PairPlainSched sched, StoreEpi epi, ErrorRecord* err, uint64_t timeout_ns) {
-  pair::gemm_core_pair(&tmA, &tmB, sched, epi, err, timeout_ns, -1);
+  pair::gemm_core_pair<NH>(&tmA, &tmB, sched, epi, err, timeout_ns, -1);
 }
 
+template <int NH>
 static void launch_pair(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
                         long long ldc, bool out_f32, float alpha, cudaStream_t stream) {
+  using Cf = pair::PairCfg<NH>;
   const CUtensorMap tA = make_tmap_2d(A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, lda, BM, BK,
                                       CU_TENSOR_MAP_SWIZZLE_128B);
   const CUtensorMap tB = make_tmap_2d(B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldb, pair::BN2 / 2, BK,
@@ -147,8 +152,9 @@ static void launch_pair(const void* A, const void* B, void* C, int M, int N, int
   s.M = M;
   s.N = N;
   s.K = K;
+  s.cols = Cf::kCols;
   s.num_m = (M + 2 * BM - 1) / (2 * BM);
-  s.num_n = (N + pair::BN2 - 1) / pair::BN2;
+  s.num_n = (N + Cf::kCols - 1) / Cf::kCols;
   s.group_m = ops::gemm_tuning().pair_group_m;
   StoreEpi e;
   e.C = C;
@@ -161,14 +167,14 @@ static void launch_pair(const void* A, const void* B, void* C, int M, int N, int
   int dev = 0;
   GICC_CUDA(cudaGetDevice(&dev));
   if (!attr_set[dev]) {
-    GICC_CUDA(cudaFuncSetAttribute(k_gemm_bf16_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, pair::kSmemBytes));
+    GICC_CUDA(cudaFuncSetAttribute(k_gemm_bf16_pair<NH>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmemBytes));
     attr_set[dev] = true;
   }
   const int pairs_max = num_sms(dev) / 2;
   const int tiles = s.num_m * s.num_n;
   const int grid = 2 * (tiles < pairs_max ? tiles : pairs_max);
-  k_gemm_bf16_pair<<<grid, kThreads, pair::kSmemBytes, stream>>>(tA, tB, s, e, device_error_record(),
-                                                                  default_timeout_ns());
+  k_gemm_bf16_pair<NH><<<grid, Cf::kThreads, Cf::kSmemBytes, stream>>>(tA, tB, s, e, device_error_record(),
+                                                                        default_timeout_ns());
   GICC_CUDA(cudaGetLastError());
 }
 
@@ -281,8 +287,10 @@ void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long 
   switch (bn) {
     case 256: gemm::launch_plain<256>(A, B, C, M, N, K, lda, ldb, ldc, out_f32, alpha, stream); break;
     case 128: gemm::launch_plain<128>(A, B, C, M, N, K, lda, ldb, ldc, out_f32, alpha, stream); break;
-    case 512: gemm::launch_pair(A, B, C, M, N, K, lda, ldb, ldc, out_f32, alpha, stream); break;  // CTA pairs
-    default: throw std::runtime_error("gicc::gemm_bf16: bn must be 128, 256 or 512 (CTA pairs)");
+    case 512: gemm::launch_pair<1>(A, B, C, M, N, K, lda, ldb, ldc, out_f32, alpha, stream); break;   // pairs, 256 x 256
+    case 1024: gemm::launch_pair<2>(A, B, C, M, N, K, lda, ldb, ldc, out_f32, alpha, stream); break;  // pairs, 256 x 512
+    default: throw std::runtime_error("gicc::gemm_bf16: bn must be 128, 256, 512 (CTA pairs, 256 x 256) or 1024 "
+                                      "(CTA pairs, 256 x 512)");
   }
 }
 

@@ -11,7 +11,9 @@ def gemm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = None, alph
     """Run the persistent warp-specialised tcgen05 GEMM (csrc/kernels/gemm.cu).
 
     A is [M, K], B is [N, K] (the nn.Linear weight layout); both bf16, row-major.
-    Accumulation is f32 in TMEM; the output is bf16 or f32.
+    Accumulation is f32 in TMEM; the output is bf16 or f32.  ``bn`` picks the tile:
+    128 or 256 (one CTA, 128 x bn), 512 (CTA pairs, 256 x 256), 1024 (CTA pairs, 256 x 512)
+    or 0 (the default for the shape).
     """
     if out_dtype not in (torch.bfloat16, torch.float32):
         raise ValueError("out_dtype must be bfloat16 or float32")

@@ -52,14 +52,18 @@ def test_gemm_strided_views():
     assert (C.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item()
 
 
-@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (512, 768, 1024), (300, 520, 136), (2048, 2048, 4096)])
-def test_gemm_cta_pair_matches_fp32_reference(M, N, K):
-    """The cta_group::2 variant (256 x 256 tiles on CTA pairs)."""
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (512, 768, 1024), (300, 520, 136), (2048, 2048, 4096),
+                                   (4352, 1800, 200)])
+@pytest.mark.parametrize("bn", [512, 1024])
+def test_gemm_cta_pair_matches_fp32_reference(M, N, K, bn):
+    """The cta_group::2 variants: 256 x 256 tiles (bn=512) and 256 x 512 tiles with one
+    512-column TMEM accumulator drained by 8 epilogue warps (bn=1024); ragged M, N and K
+    edges included, and more tiles than CTA pairs (4352 x 1800: 17 x 4 wide tiles)."""
     from opengda_b200.ops.gemm import gemm, check_errors
     g = torch.Generator(device="cuda").manual_seed(M + 11 * N + K)
     A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
     B = torch.randn(N, K, device="cuda", generator=g).to(torch.bfloat16)
-    C = gemm(A, B, bn=512)
+    C = gemm(A, B, bn=bn)
     torch.cuda.synchronize()
     check_errors()
     ref = _ref(A, B)
