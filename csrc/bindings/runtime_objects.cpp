@@ -303,7 +303,8 @@ void bind_runtime_objects(py::module_& m) {
   m.def("k_ag_gemm", [](int n, int r, int M, int Ns, int K, std::vector<uint64_t> a_full, uint64_t B, long long ldb,
                         uint64_t C, long long ldc, std::vector<uint64_t> arrivals, std::vector<uint64_t> done,
                         uint64_t epoch, int units_per_band, int grid, uint64_t timeout_ns, uint64_t trace,
-                        int diag, int comm_ctas, uint64_t tile_counter, uint64_t a_mc, uint64_t arrivals_mc) {
+                        int diag, int comm_ctas, uint64_t tile_counter, uint64_t a_mc, uint64_t arrivals_mc,
+                        int pair) {
     if ((int)a_full.size() != n || (int)arrivals.size() != n || (int)done.size() != n || n > 16)
       throw std::runtime_error("k_ag_gemm: per-rank pointer lists must have n <= 16 entries");
     ops::AgGemmArgs a;
@@ -318,11 +319,13 @@ void bind_runtime_objects(py::module_& m) {
     a.trace = P<uint64_t>(trace); a.diag = diag; a.comm_ctas = comm_ctas;
     a.tile_counter = P<uint64_t>(tile_counter);
     a.a_mc = P<void>(a_mc); a.arrivals_mc = P<uint64_t>(arrivals_mc);
+    a.pair = pair;
     ops::ag_gemm(a, cur_stream());
   }, py::arg("n"), py::arg("r"), py::arg("M"), py::arg("Ns"), py::arg("K"), py::arg("a_full"), py::arg("B"),
      py::arg("ldb"), py::arg("C"), py::arg("ldc"), py::arg("arrivals"), py::arg("done"), py::arg("epoch"),
      py::arg("units_per_band"), py::arg("grid"), py::arg("timeout_ns"), py::arg("trace") = 0, py::arg("diag") = 0,
-     py::arg("comm_ctas") = 0, py::arg("tile_counter") = 0, py::arg("a_mc") = 0, py::arg("arrivals_mc") = 0);
+     py::arg("comm_ctas") = 0, py::arg("tile_counter") = 0, py::arg("a_mc") = 0, py::arg("arrivals_mc") = 0,
+     py::arg("pair") = 0);
   m.def("ag_transfer_ce", [](int n, int r, int M, int K, std::vector<uint64_t> a_full, std::vector<uint64_t> arrivals,
                              uint64_t done_local, uint64_t epoch, int grid, int units_per_band, int chunks,
                              uint64_t timeout_ns) {

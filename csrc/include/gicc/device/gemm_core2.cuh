@@ -49,7 +49,9 @@ struct PairCfg {
   static constexpr uint32_t kStageBytes = kABytes + NH * kBBytes;
   static constexpr int kStages = NH == 1 ? 6 : 4;
   static constexpr int kEpiWarps = 4 * NH;
-  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;  // without communication warps
+  // threads of a CTA for a schedule with `comm_warps` communication warps after the epilogue
+  __host__ __device__ static constexpr int threads(int comm_warps) { return kThreads + 32 * comm_warps; }
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
@@ -96,6 +98,36 @@ __device__ __forceinline__ void commit_pair(uint32_t bar_cluster_addr) {
 __device__ __forceinline__ void arrive_cluster(uint32_t bar_cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
 }
+// Bounded wait on an mbarrier phase with cluster-scope acquire semantics: for barriers
+// that another CTA of the cluster arrives on after writing this CTA's shared memory.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(ptx::smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint64_t timeout_ns,
+                                                  volatile int* abort_flag) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = ptx::globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 15) == 0) {
+      if (abort_flag != nullptr && *abort_flag) return false;
+      if (ptx::globaltimer() - t0 > timeout_ns) return false;
+    }
+  }
+}
+// 32-bit store into another CTA's shared memory (address from map_to).
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, int v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(ptx::smem_u32(dst_smem)),
                "r"(ncols)
@@ -112,12 +144,24 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 // NH*256 columns, kb range); the core derives each CTA's A row (m0 + 128*rank) and B rows
 // (n0 + h*256 + 128*rank for column half h).  Epi::store gets the CTA-local row (0..127)
 // and the column offset within the pair tile.
+//
+// Schedules with kDynamic take tiles from Sched::next_tile(), called by the leader's
+// producer only; the index goes to both CTAs through a 4-entry queue in shared memory (the
+// leader writes its own and the peer's entry, st.shared::cluster, then arrives on both
+// CTAs' "queue full" barriers with cluster-scope release).  Readers -- the leader's MMA
+// thread, the peer's producer and every epilogue warp of both CTAs -- arrive on the
+// leader's "queue empty" barrier.  Sched::producer_wait(ti, crank, ...) runs in each CTA's
+// producer before that CTA loads its half of a tile.  Schedules with kCommWarps > 0 get
+// that many warps after the epilogue warps, running Sched::comm.
 template <int NH = 1, class Sched, class Epi>
 __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUtensorMap* tmB, const Sched& sched,
                                                Epi& epi, ErrorRecord* err, uint64_t timeout_ns, int rank) {
   using Cf = PairCfg<NH>;
+  static_assert(!Epi::kNeedsTileDone, "pair core: epilogues that publish finished tiles are not supported");
   constexpr int S = Cf::kStages;
   constexpr int kAccs = Cf::kAccs;
+  constexpr bool kDyn = sched_dynamic<Sched>::value;
+  constexpr int kFirstComm = 2 + Cf::kEpiWarps;  // first communication warp
   extern __shared__ uint8_t gemm2_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gemm2_smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -127,8 +171,11 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* tq_full = drain + 1;
+  uint64_t* tq_empty = tq_full + kTileQ;  // only the leader's is used
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tq_empty + kTileQ);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* tq = reinterpret_cast<volatile int*>(tmem_slot + 2);  // [kTileQ] tile indices
 
   const uint32_t warp = ptx::warp_id();
   const uint32_t lane = ptx::lane_id();
@@ -147,6 +194,10 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
       ptx::mbar_init(&tempty[a], 2 * Cf::kEpiWarps);  // every epilogue warp of both CTAs
     }
     ptx::mbar_init(drain, 1);
+    for (int q = 0; q < kTileQ; ++q) {
+      ptx::mbar_init(&tq_full[q], 1);
+      ptx::mbar_init(&tq_empty[q], 2 + 2 * Cf::kEpiWarps);  // MMA + peer producer + all epilogue warps
+    }
     *abort_flag = 0;
     ptx::fence_mbar_init();
     ptx::prefetch_tmap(tmA);
@@ -162,6 +213,24 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int ntiles = sched.num_tiles();
+  // the leader's queue-empty barriers and the peer's queue (leader writes it)
+  const uint32_t tq_empty_leader = map_to(ptx::smem_u32(&tq_empty[0]), 0);
+  const uint32_t tq_peer = map_to(ptx::smem_u32(const_cast<int*>(&tq[0])), 1);
+  const uint32_t tq_full_peer = map_to(ptx::smem_u32(&tq_full[0]), 1);
+
+  // Next tile index of the dynamic order for a reader (not the leader's producer); -1 ends.
+  // Returns false on timeout (abort).
+  auto take = [&](int& slot, uint32_t& qphase, int& t, bool epi_warp) -> bool {
+    if (!mbar_wait_cluster(&tq_full[slot], qphase, timeout_ns, abort_flag)) return false;
+    t = tq[slot];
+    if (epi_warp) __syncwarp();
+    if (!epi_warp || lane == 0) arrive_cluster(tq_empty_leader + slot * 8);
+    if (++slot == kTileQ) {
+      slot = 0;
+      qphase ^= 1;
+    }
+    return true;
+  };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -171,9 +240,36 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
       uint32_t armed[S];
 #pragma unroll
       for (int s = 0; s < S; ++s) armed[s] = 0;
-      for (int t = pair_id; t < ntiles && !*abort_flag; t += npairs) {
+      int qslot = 0;
+      uint32_t qphase = 0;
+      for (int t = pair_id; !*abort_flag; t += npairs) {
+        if constexpr (kDyn) {
+          if (leader) {
+            if (!mbar_wait_cluster(&tq_empty[qslot], qphase ^ 1, timeout_ns, abort_flag)) {
+              if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_GEMM_PIPE, rank, 0, 4, 0);
+              *abort_flag = 1;
+              break;
+            }
+            t = sched.next_tile();
+            const int v = t < ntiles ? t : -1;
+            tq[qslot] = v;
+            st_cluster_u32(tq_peer + qslot * 4, v);
+            ptx::mbar_arrive(&tq_full[qslot]);
+            arrive_cluster(tq_full_peer + qslot * 8);
+            if (++qslot == kTileQ) {
+              qslot = 0;
+              qphase ^= 1;
+            }
+          } else if (!take(qslot, qphase, t, false)) {
+            if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_GEMM_PIPE, rank, 1, 5, 0);
+            *abort_flag = 1;
+            break;
+          }
+          if (t < 0) break;
+        }
+        if (t >= ntiles) break;
         TileInfo ti = sched.tile(t);
-        if (!sched.producer_wait(ti, timeout_ns, abort_flag, err)) {
+        if (!sched.producer_wait(ti, (int)crank, timeout_ns, abort_flag, err)) {
           *abort_flag = 1;
           break;
         }
@@ -217,7 +313,18 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
       int acc = 0;
       uint32_t acc_phase = 0;
       bool issued = false;
-      for (int t = pair_id; t < ntiles && !*abort_flag; t += npairs) {
+      int qslot = 0;
+      uint32_t qphase = 0;
+      for (int t = pair_id; !*abort_flag; t += npairs) {
+        if constexpr (kDyn) {
+          if (!take(qslot, qphase, t, false)) {
+            if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_GEMM_PIPE, rank, 0, 6, 0);
+            *abort_flag = 1;
+            break;
+          }
+          if (t < 0) break;
+        }
+        if (t >= ntiles) break;
         TileInfo ti = sched.tile(t);
         if (!ptx::mbar_wait(&tempty[acc], acc_phase ^ 1, timeout_ns, abort_flag)) {
           if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_GEMM_PIPE, rank, 0, 1, 0);
@@ -271,6 +378,9 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
         ptx::mbar_wait(drain, 0, 20000000ull, nullptr);
       }
     }
+  } else if ((int)warp >= kFirstComm) {
+    // ---------------- communication warps (schedules that move data) ----------------
+    if constexpr (Sched::kCommWarps > 0) sched.comm((int)warp - kFirstComm, (int)lane, abort_flag, err, timeout_ns);
   } else {
     // ---------------- epilogue (warps 2.., both CTAs) ----------------
     // Warp w may read TMEM lanes 32*(w%4)..+31; with NH = 2 warps 2..5 take columns
@@ -282,7 +392,18 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
     const uint32_t tempty_leader1 = map_to(ptx::smem_u32(&tempty[1]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = pair_id; t < ntiles; t += npairs) {
+    int qslot = 0;
+    uint32_t qphase = 0;
+    for (int t = pair_id;; t += npairs) {
+      if constexpr (kDyn) {
+        if (!take(qslot, qphase, t, true)) {
+          if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_GEMM_PIPE, rank, (int)crank, 7, 0);
+          *abort_flag = 1;
+          break;
+        }
+        if (t < 0) break;
+      }
+      if (t >= ntiles) break;
       TileInfo ti = sched.tile(t);
       ti.m0 += (int)crank * BM;  // this CTA's 128 rows of the pair tile
       if (!ptx::mbar_wait(&tfull[acc], acc_phase, timeout_ns, abort_flag)) {

@@ -177,6 +177,8 @@ struct AgGemmArgs {
   uint64_t* trace = nullptr;   // diagnostics: %globaltimer stamps per tile / unit / CTA
   int diag = 0;                // bit 0 = no transfer (diagnostics: times the math alone);
                                // bit 1 = external transfer (ag_transfer_ce): no pushes, waits kept
+  int pair = 0;                // tensor-core tiles: 0 = one CTA, 128 x 256; 1 = CTA pairs, 256 x 256;
+                               // 2 = CTA pairs, 256 x 512 (pairs need M/n % 256 == 0, no trace)
 };
 struct GemmRsArgs {
   int n = 0, r = 0, M = 0, N = 0, K = 0;  // K = local K

@@ -130,7 +130,7 @@ struct PairPlainSched {
     ti.aux2 = 0;
     return ti;
   }
-  __device__ bool producer_wait(const TileInfo&, uint64_t, volatile int*, ErrorRecord*) const { return true; }
+  __device__ bool producer_wait(const TileInfo&, int, uint64_t, volatile int*, ErrorRecord*) const { return true; }
 };
 
 template <int NH>

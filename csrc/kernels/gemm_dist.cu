@@ -40,6 +40,7 @@
 
 #include "gicc/device/comm.cuh"
 #include "gicc/device/gemm_core.cuh"
+#include "gicc/device/gemm_core2.cuh"
 #include "gicc/config.hpp"
 #include "gicc/driver.hpp"
 #include "gicc/host_util.hpp"
@@ -282,6 +283,57 @@ struct AgSched {
     }
   }
 };
+// The same all-gather GEMM on CTA pairs (cta_group::2): tiles of 256 rows x NH*256 columns,
+// numbered like AgSched's (local shard first, then band-major over the other shards) over
+// pair bands of 256 rows.  Each CTA of a pair loads its own 128-row band of A, so each
+// producer waits for its own band's arrival counter.  The transfer (comm warps) is AgSched's.
+template <int NH>
+struct AgPairSched : AgSched {
+  int nb2;  // 256-row pair bands per shard
+  __device__ int num_tiles() const { return n * nb2 * num_n; }
+  __device__ int next_tile() const {
+    const unsigned long long v = atomicAdd(tile_counter, 1ull) - tile_base;
+    return v < (unsigned long long)num_tiles() ? (int)v : num_tiles();
+  }
+  __device__ TileInfo tile(int t) const {
+    const int per = nb2 * num_n;
+    int k, b, nbk;
+    if (a_mc && t >= per) {
+      int vm;
+      raster(t - per, nb2 * (n - 1), num_n, 8, vm, nbk);
+      b = vm / (n - 1);
+      k = 1 + vm - b * (n - 1);
+    } else {
+      k = t / per;
+      raster(t - k * per, nb2, num_n, 8, b, nbk);
+    }
+    const int s = (r + k) % n;
+    TileInfo ti;
+    ti.m0 = s * Ms + b * 2 * BM;
+    ti.a_row = ti.m0;
+    ti.n0 = nbk * NH * 256;
+    ti.b_row = ti.n0;
+    ti.kb0 = 0;
+    ti.kb1 = (K + BK - 1) / BK;
+    ti.aux = s;
+    ti.aux2 = 2 * b;  // the pair's first 128-row band
+    return ti;
+  }
+  __device__ bool producer_wait(const TileInfo& ti, int crank, uint64_t timeout_ns, volatile int* abort_flag,
+                                ErrorRecord* err) const {
+    if (ti.aux != r && !(diag & 1)) {
+      const uint64_t* c = arrivals + (size_t)ti.aux * nb + ti.aux2 + crank;
+      const uint64_t target = epoch * (uint64_t)Q;
+      if (!wait_counter(c, target, timeout_ns, abort_flag)) {
+        if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_AG_FLAG, r, ti.aux, ptx::ld_relaxed_sys(c), target);
+        return false;
+      }
+      ptx::fence_proxy_async_global();  // peer's generic-proxy stores -> our TMA reads
+    }
+    return true;
+  }
+};
+
 // Trace layout (uint64 %globaltimer ns), T = tiles (m-block major), U = (n-1)*nb*Q units:
 //   [2t, 2t+1]        producer: before / after the wait for tile t's A band
 //   [2T + t]          epilogue: tile t stored (first epilogue warp)
@@ -337,6 +389,15 @@ __global__ void __launch_bounds__(cta_threads(kCommWarpsAG), 1)
   gemm_core<BN>(&tmA, &tmB, sched, epi, err, timeout_ns, sched.r);
   signal_cta_done(done_peer.p, sched.n, sched.r);
   if (tr && threadIdx.x == 0) tr[2 * blockIdx.x + 1] = ptx::globaltimer();
+}
+
+template <int NH>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::PairCfg<NH>::threads(kCommWarpsAG), 1)
+    k_ag_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   AgPairSched<NH> sched, PlainStoreEpi epi, DoneTable done_peer, ErrorRecord* err,
+                   uint64_t timeout_ns) {
+  pair::gemm_core_pair<NH>(&tmA, &tmB, sched, epi, err, timeout_ns, sched.r);
+  signal_cta_done(done_peer.p, sched.n, sched.r);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -698,6 +759,45 @@ __global__ void __launch_bounds__(cta_threads(kCommWarpsAG), 1)
 
 namespace ops {
 
+namespace {
+// The CTA-pair variant of ag_gemm: same schedule fields, pair tiles, grid of whole pairs.
+template <int NH>
+void launch_ag_pair(const AgGemmArgs& a, const gemm::AgSched& base, const gemm::PlainStoreEpi& e0,
+                    const gemm::DoneTable& dt, int G, cudaStream_t s) {
+  using namespace gemm;
+  using Cf = pair::PairCfg<NH>;
+  const int Ms = a.M / a.n;
+  if (Ms % (2 * BM) || a.Ns % (NH * 256) || a.trace)
+    throw std::runtime_error("gicc::ag_gemm (pairs): need M/ranks % 256 == 0, N/ranks % (pair*256) == 0, no trace");
+  const int Gp = G & ~1;  // whole CTA pairs
+  const CUtensorMap tA = make_tmap_2d(a.a_full[a.r], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, a.K, BM, BK,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tB = make_tmap_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.Ns, a.K, a.ldb, pair::BN2 / 2, BK,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  AgPairSched<NH> sc;
+  static_cast<AgSched&>(sc) = base;
+  sc.G = Gp;
+  sc.C = a.comm_ctas > 0 && a.comm_ctas < Gp ? a.comm_ctas : Gp;
+  sc.nb2 = Ms / (2 * BM);
+  sc.num_n = a.Ns / (NH * 256);
+  sc.bn = NH * 256;
+  // every leader takes one index past the end of each call
+  sc.tile_base = (unsigned long long)(a.epoch - 1) * (unsigned long long)(a.n * sc.nb2 * sc.num_n + Gp / 2);
+  PlainStoreEpi e = e0;
+  e.trace_epi = nullptr;
+  static bool attr[2][64] = {};
+  int dev = 0;
+  GICC_CUDA(cudaGetDevice(&dev));
+  if (!attr[NH - 1][dev]) {
+    GICC_CUDA(cudaFuncSetAttribute(k_ag_gemm_pair<NH>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmemBytes));
+    attr[NH - 1][dev] = true;
+  }
+  k_ag_gemm_pair<NH><<<Gp, Cf::threads(kCommWarpsAG), Cf::kSmemBytes, s>>>(
+      tA, tB, sc, e, dt, device_error_record(), a.timeout_ns ? a.timeout_ns : default_timeout_ns());
+  GICC_CUDA(cudaGetLastError());
+}
+}  // namespace
+
 void ag_gemm(const AgGemmArgs& a, cudaStream_t s) {
   NvtxRange nvtx("gicc::ops::ag_gemm");
   using namespace gemm;
@@ -750,6 +850,11 @@ void ag_gemm(const AgGemmArgs& a, cudaStream_t s) {
                   a.Ns / BN_, BN_};
   DoneTable dt{};
   for (int i = 0; i < a.n; ++i) dt.p[i] = a.done[i];
+  if (a.pair) {
+    if (a.pair == 1) launch_ag_pair<1>(a, sc, e, dt, G, s);
+    else launch_ag_pair<2>(a, sc, e, dt, G, s);
+    return;
+  }
   constexpr uint32_t smem = Cfg<BN_>::kSmemBytes;
   static bool attr[64] = {false};
   int dev = 0;

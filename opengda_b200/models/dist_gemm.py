@@ -68,6 +68,9 @@ class DistGemm:
         self.rs_raster_group = 0
         self.trace: Optional[torch.Tensor] = None
         self.diag = 0
+        # AG tensor-core tiles: 0 = one CTA per 128 x 256 tile; 1 / 2 = CTA pairs (cta_group::2)
+        # with 256 x 256 / 256 x 512 tiles.  Fixed by the first call (the counters depend on it).
+        self.pair = 0
         if w > 1 and fused:
             # fused kernels: double-buffered landing areas + epoch counters in the signal heap
             if mode == "ag":
@@ -132,7 +135,7 @@ class DistGemm:
         with rs_join).  They are fixed by the first call; changing them later would
         desynchronise the counters, so it is refused.
         comm_ctas, rs_reduce_ctas and trace may change freely."""
-        now = (self.grid, self.units_per_band, self.diag, self.rs_join)
+        now = (self.grid, self.units_per_band, self.diag, self.rs_join, self.pair)
         first = getattr(self, "_frozen", None)
         if first is None:
             self._frozen = now
@@ -180,6 +183,8 @@ class DistGemm:
             from .. import native
 
             self._check_frozen_settings()
+            if self.pair and self.trace is not None:
+                raise ValueError("DistGemm: the trace buffer is supported by the single-CTA kernel only (pair=0)")
             self.epoch += 1
             p = self.epoch % 2
             C = out if out is not None else self.C
@@ -210,7 +215,8 @@ class DistGemm:
                             B.stride(0), C.data_ptr(), C.stride(0), self.arrivals, self.done, self.epoch,
                             self.units_per_band, self.grid, self.rt.timeout_ns,
                             self.trace.data_ptr() if self.trace is not None else 0, diag, self.comm_ctas,
-                            self.tile_counter, buf.mc_ptr if self.nvls else 0, self.arrivals_mc)
+                            self.tile_counter, buf.mc_ptr if self.nvls else 0, self.arrivals_mc,
+                            self.pair)
                 if done_ev is not None:
                     # later work on this stream (e.g. rewriting the shard slot) waits for the outgoing copies
                     torch.cuda.current_stream().wait_event(done_ev)

@@ -48,10 +48,14 @@ def main():
     # 2. distributed GEMM options vs fp32
     try:
         from opengda_b200.models.dist_gemm import DistGemm, make_operands
-        M = Nn = K = 2048
         for name, mode, kw, attr in (("ag_ce", "ag", {"transfer": "ce"}, {}), ("rs_join", "rs", {}, {"rs_join": True}),
                                      ("rs_group2", "rs", {}, {"rs_raster_group": 2}),
-                                     ("ag_unicast", "ag", {"nvls": False}, {}), ("rs_unicast", "rs", {"nvls": False}, {})):
+                                     ("ag_unicast", "ag", {"nvls": False}, {}), ("rs_unicast", "rs", {"nvls": False}, {}),
+                                     ("ag_pair1", "ag", {}, {"pair": 1}), ("ag_pair2", "ag", {}, {"pair": 2}),
+                                     ("ag_pair2_unicast", "ag", {"nvls": False}, {"pair": 2})):
+            # CTA-pair tiles need 256-row bands per shard and 512-column blocks per rank
+            M = Nn = 4096 if "pair" in attr else 2048
+            K = 2048
             model = DistGemm(M, Nn, K, mode, rt=rt, fused=True, **kw)
             for k, v in attr.items():
                 setattr(model, k, v)
