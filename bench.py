@@ -66,7 +66,8 @@ def check_numerics(model, A, B, Afull, Bfull, mode, world, rank) -> float:
 def timed_run(step, steps, warmup, world, local_rank):
     """W untimed steps, then K steps between a barrier + synchronize on both sides, timed
     with CUDA events on the launching stream (one event per step boundary, which adds no
-    synchronisation).  Returns (ms per step, max over ranks; per-step ms summary of the
+    synchronisation); with several ranks a one-element all-reduce on the stream right
+    before the first event lines the ranks' starts up on the device.  Returns (ms per step, max over ranks; per-step ms summary of the
     slowest rank; clock record during the timed steps, all ranks)."""
     import torch
     import torch.distributed as dist
@@ -81,7 +82,13 @@ def timed_run(step, steps, warmup, world, local_rank):
         dist.barrier()
     torch.cuda.synchronize()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    tiny = torch.zeros(1, device=torch.device("cuda", local_rank))
     with ClockSampler([local_rank]) as cs:
+        if world > 1:
+            # a device-side barrier (one-element all-reduce on this stream) right before the
+            # first timed step: every rank's clock starts when all ranks are ready, so a rank
+            # whose host left the barrier late does not stretch the others' first step
+            dist.all_reduce(tiny)
         ev[0].record()
         for i in range(steps):
             step()
