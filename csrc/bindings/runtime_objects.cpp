@@ -349,7 +349,7 @@ void bind_runtime_objects(py::module_& m) {
                         uint64_t out, long long ldo, uint64_t epoch, int grid, uint64_t timeout_ns,
                         uint64_t staging_mc, uint64_t band_tiles, uint64_t tile_counter, int comm_ctas,
                         int units_per_band, uint64_t trace, int join_reduce, uint64_t unit_counter,
-                        int raster_group) {
+                        int raster_group, int pair) {
     if ((int)slots.size() != n || (int)arrivals.size() != n || (int)done.size() != n || n > 16)
       throw std::runtime_error("k_gemm_rs: per-rank pointer lists must have n <= 16 entries");
     ops::GemmRsArgs a;
@@ -366,12 +366,13 @@ void bind_runtime_objects(py::module_& m) {
     a.trace = P<uint64_t>(trace);
     a.join_reduce = join_reduce; a.unit_counter = P<uint64_t>(unit_counter);
     a.raster_group = raster_group;
+    a.pair = pair;
     ops::gemm_rs(a, cur_stream());
   }, py::arg("n"), py::arg("r"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("A"), py::arg("lda"), py::arg("B"),
      py::arg("ldb"), py::arg("slots"), py::arg("arrivals"), py::arg("done"), py::arg("out"), py::arg("ldo"),
      py::arg("epoch"), py::arg("grid"), py::arg("timeout_ns"), py::arg("staging_mc") = 0, py::arg("band_tiles") = 0,
      py::arg("tile_counter") = 0, py::arg("comm_ctas") = 0, py::arg("units_per_band") = 4, py::arg("trace") = 0,
-     py::arg("join_reduce") = 0, py::arg("unit_counter") = 0, py::arg("raster_group") = 0);
+     py::arg("join_reduce") = 0, py::arg("unit_counter") = 0, py::arg("raster_group") = 0, py::arg("pair") = 0);
   m.def("k_litmus", [](int test, int iters, int k, int use_fence, uint32_t seed, uint32_t max_delay, uint64_t timeout_ns,
                        int role_base, int nroles_here, std::vector<std::vector<uint64_t>> roles) {
     if (roles.size() != 2) throw std::runtime_error("k_litmus: two role pointer lists");

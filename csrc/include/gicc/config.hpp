@@ -27,7 +27,7 @@ struct GICC_EXPORT Config {
   size_t signal_heap_bytes = 0;          // GICC_SIGNAL_HEAP_BYTES: 0 = the RuntimeOptions value [64 KiB, 1 GiB]
   int gemm_group_m = 16;                 // GICC_GEMM_GROUP_M: m-blocks per raster group of gemm_bf16 [1, 1024]
   int gemm_l2_hint = 0;                  // GICC_GEMM_L2_HINT: 0 none, 1 keep A / stream B, 2 the reverse
-  int gemm_pair_group_m = 8;             // GICC_GEMM_PAIR_GROUP_M: the CTA-pair kernel's raster group [1, 1024]
+  int gemm_pair_group_m = 16;            // GICC_GEMM_PAIR_GROUP_M: the CTA-pair kernel's raster group [1, 1024]
 
   // Parses the environment now; throws std::invalid_argument naming the bad variable.
   static Config from_env();

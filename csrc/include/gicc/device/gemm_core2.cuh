@@ -152,12 +152,13 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 // thread, the peer's producer and every epilogue warp of both CTAs -- arrive on the
 // leader's "queue empty" barrier.  Sched::producer_wait(ti, crank, ...) runs in each CTA's
 // producer before that CTA loads its half of a tile.  Schedules with kCommWarps > 0 get
-// that many warps after the epilogue warps, running Sched::comm.
+// that many warps after the epilogue warps, running Sched::comm.  Epilogues with
+// kNeedsTileDone get tile_done(ti) once per CTA and tile (ti.m0 = that CTA's first row),
+// after all of that CTA's epilogue warps stored their part.
 template <int NH = 1, class Sched, class Epi>
 __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUtensorMap* tmB, const Sched& sched,
                                                Epi& epi, ErrorRecord* err, uint64_t timeout_ns, int rank) {
   using Cf = PairCfg<NH>;
-  static_assert(!Epi::kNeedsTileDone, "pair core: epilogues that publish finished tiles are not supported");
   constexpr int S = Cf::kStages;
   constexpr int kAccs = Cf::kAccs;
   constexpr bool kDyn = sched_dynamic<Sched>::value;
@@ -176,6 +177,9 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tq_empty + kTileQ);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* tq = reinterpret_cast<volatile int*>(tmem_slot + 2);  // [kTileQ] tile indices
+  // Per accumulator: epilogue warps of this CTA that finished a tile held in it (monotonic;
+  // epilogues that publish finished tiles).
+  uint32_t* epi_cnt = tmem_slot + 2 + kTileQ;
 
   const uint32_t warp = ptx::warp_id();
   const uint32_t lane = ptx::lane_id();
@@ -199,6 +203,8 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
       ptx::mbar_init(&tq_empty[q], 2 + 2 * Cf::kEpiWarps);  // MMA + peer producer + all epilogue warps
     }
     *abort_flag = 0;
+    epi_cnt[0] = 0;
+    epi_cnt[1] = 0;
     ptx::fence_mbar_init();
     ptx::prefetch_tmap(tmA);
     ptx::prefetch_tmap(tmB);
@@ -419,14 +425,33 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
         uint32_t r[32];
         ptx::tmem_ld32(tbase + c, r);
         ptx::tmem_ld_wait();
-        if (c + 32 >= BN2) {
-          ptx::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+        if constexpr (!Epi::kNeedsTileDone) {
+          if (c + 32 >= BN2) {
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+          }
         }
         epi.store(ti, row, half * BN2 + c, r);
       }
       epi.end_tile(ti, row);
+      if constexpr (Epi::kNeedsTileDone) {
+        // The last of this CTA's epilogue warps to finish publishes this CTA's 128 rows of
+        // the tile (ti.m0 is this CTA's first row); the accumulator goes back to the MMA
+        // warp only afterwards, so the next tile in it cannot start counting first.
+        Epi::fence_before_done();
+        __syncwarp();
+        if (lane == 0) {
+          const uint32_t old = atomicAdd(&epi_cnt[acc], 1u);
+          if (old % Cf::kEpiWarps == Cf::kEpiWarps - 1) {
+            Epi::fence_before_done();
+            epi.tile_done(ti);
+          }
+        }
+        __syncwarp();
+        ptx::tc_fence_before();
+        if (lane == 0) arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+      }
       if (++acc == kAccs) {
         acc = 0;
         acc_phase ^= 1;

@@ -12,7 +12,9 @@ namespace gicc {
 namespace ops {
 
 // C[M,N] = alpha * A[M,K] * B[N,K]^T  (bf16 in, f32 accumulate; bf16 or f32 out).
-// bn selects the tile width (0 = default 256).
+// bn selects the tile: 128 or 256 (one CTA, 128 x bn), 512 (CTA pairs, 256 x 256), 1024 (CTA
+// pairs, 256 x 512), 0 = by shape: 1024 when the pair tiles fill the GPU's CTA pairs about as
+// evenly as 128 x 256 tiles fill its SMs, else 256.
 GICC_EXPORT void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
                            long long ldc, bool out_f32, float alpha, int bn, cudaStream_t stream);
 // Process-wide tuning of gemm_bf16's 1-CTA kernel (A/B experiments; the defaults are the
@@ -21,7 +23,7 @@ GICC_EXPORT void gemm_bf16(const void* A, const void* B, void* C, int M, int N, 
 struct GemmTuning {
   int group_m = 16;       // 1-CTA kernel: 128-row m-blocks per raster group
   int l2_hint = 0;
-  int pair_group_m = 8;   // CTA-pair kernel (bn = 512): 256-row m-blocks per raster group
+  int pair_group_m = 16;  // CTA-pair kernels (bn = 512, 1024): 256-row m-blocks per raster group
 };
 GICC_EXPORT void set_gemm_tuning(const GemmTuning& t);
 GICC_EXPORT GemmTuning gemm_tuning();
@@ -208,6 +210,8 @@ struct GemmRsArgs {
   int raster_group = 0;        // NVLS: m-blocks per raster group (0 = 16).  Smaller groups finish
                                // bands sooner (the owners can reduce them earlier); larger
                                // ones reuse B better in L2 when B does not fit there
+  int pair = 0;                // NVLS: 0 = one CTA per 128 x 256 tile; 1 / 2 = CTA pairs with
+                               // 256 x 256 / 256 x 512 tiles (M/n % 256 == 0; no join, no trace)
 };
 // Memory-model litmus tests (gicc/proto/litmus.hpp).  test 0 = MP (role 0 writes data and
 // flag into role 1's memory; role 1 checks), test 1 = SB (each role stores into the other's

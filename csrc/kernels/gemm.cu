@@ -275,6 +275,21 @@ GemmTuning gemm_tuning() {
   return g_tuning;
 }
 
+// Default tile for an M x N output: the 256 x 512 pair tile moves half the operand bytes
+// per FLOP of the 128 x 256 single-CTA tile (and runs faster under the power cap), unless
+// its coarser tiles leave a markedly larger share of the last wave of CTA pairs idle.
+static int default_tile(int M, int N) {
+  const int sms = num_sms();
+  auto fill = [](long long tiles, int slots) {
+    const long long waves = (tiles + slots - 1) / slots;
+    return (double)tiles / (double)(waves * slots);
+  };
+  const long long t1024 = (long long)((M + 255) / 256) * ((N + 511) / 512);
+  const long long t256 = (long long)((M + 127) / 128) * ((N + 255) / 256);
+  if (t1024 < sms / 2) return 256;
+  return fill(t1024, sms / 2) >= fill(t256, sms) - 0.05 ? 1024 : 256;
+}
+
 void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
                long long ldc, bool out_f32, float alpha, int bn, cudaStream_t stream) {
   NvtxRange nvtx("gicc::ops::gemm_bf16");
@@ -283,7 +298,7 @@ void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long 
     throw std::runtime_error("gicc::gemm_bf16: K and leading dimensions of A/B must be multiples of 8 (16-byte TMA rows)");
   if (out_f32 ? (N % 4 != 0 || ldc % 4 != 0) : (N % 8 != 0 || ldc % 8 != 0))
     throw std::runtime_error("gicc::gemm_bf16: N/ldc must allow 16-byte vector stores");
-  if (bn == 0) bn = 256;
+  if (bn == 0) bn = default_tile(M, N);
   switch (bn) {
     case 256: gemm::launch_plain<256>(A, B, C, M, N, K, lda, ldb, ldc, out_f32, alpha, stream); break;
     case 128: gemm::launch_plain<128>(A, B, C, M, N, K, lda, ldb, ldc, out_f32, alpha, stream); break;

@@ -739,6 +739,62 @@ struct RsNvEpi {
   }
 };
 
+// The NVLS reduce-scatter GEMM on CTA pairs: pair tiles of 256 rows (two 128-row bands of
+// one owner) x NH*256 columns in the same band-major order; each CTA publishes its own band.
+// The join option is not available here (only the leader's producer sees the tile counter).
+template <int NH>
+struct RsNvPairSched : RsNvSched {
+  int nbo2;  // 256-row pair bands per owner
+  __device__ int num_tiles() const { return n * nbo2 * num_n; }
+  __device__ int next_tile() const {
+    const unsigned long long v = atomicAdd(tile_counter, 1ull) - tile_base;
+    return v < (unsigned long long)num_tiles() ? (int)v : num_tiles();
+  }
+  __device__ TileInfo tile(int t) const {
+    int vm, nbk;
+    raster(t, nbo2 * n, num_n, group, vm, nbk);
+    const int b = vm / n, o = vm - b * n;
+    TileInfo ti;
+    ti.m0 = o * Mr + b * 2 * BM;
+    ti.a_row = ti.m0;
+    ti.n0 = nbk * NH * 256;
+    ti.b_row = ti.n0;
+    ti.kb0 = 0;
+    ti.kb1 = (K + BK - 1) / BK;
+    ti.aux = o;
+    ti.aux2 = 2 * b;
+    return ti;
+  }
+  __device__ bool producer_wait(const TileInfo& ti, int, uint64_t timeout_ns, volatile int* abort_flag,
+                                ErrorRecord* err) const {
+    return RsNvSched::producer_wait(ti, timeout_ns, abort_flag, err);
+  }
+};
+
+// RsNvEpi for pair tiles: the band that a CTA publishes follows from its first row.
+struct RsNvPairEpi : RsNvEpi {
+  int Mr;
+  __device__ void end_tile(const TileInfo&, int) {}
+  __device__ void tile_done(const TileInfo& ti) {
+    TileInfo t = ti;
+    t.aux2 = (ti.m0 - ti.aux * Mr) / BM;
+    RsNvEpi::tile_done(t);
+  }
+};
+
+template <int NH>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::PairCfg<NH>::threads(kCommWarpsAG), 1)
+    k_gemm_rs_nvls_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        RsNvPairSched<NH> sched, RsNvPairEpi epi, DoneTable done_peer, ErrorRecord* err,
+                        uint64_t timeout_ns) {
+  if (threadIdx.x == 0) {  // ordered by the core's set-up barrier
+    *sched.checked_flag() = 0;
+    *sched.gemm_done_flag() = 0;
+  }
+  pair::gemm_core_pair<NH>(&tmA, &tmB, sched, epi, err, timeout_ns, sched.r);
+  signal_cta_done(done_peer.p, sched.n, sched.r);
+}
+
 template <int BN>
 __global__ void __launch_bounds__(cta_threads(kCommWarpsAG), 1)
     k_gemm_rs_nvls(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, RsNvSched sched,
@@ -793,6 +849,49 @@ void launch_ag_pair(const AgGemmArgs& a, const gemm::AgSched& base, const gemm::
     attr[NH - 1][dev] = true;
   }
   k_ag_gemm_pair<NH><<<Gp, Cf::threads(kCommWarpsAG), Cf::kSmemBytes, s>>>(
+      tA, tB, sc, e, dt, device_error_record(), a.timeout_ns ? a.timeout_ns : default_timeout_ns());
+  GICC_CUDA(cudaGetLastError());
+}
+}  // namespace
+
+namespace {
+// The CTA-pair variant of the NVLS reduce-scatter GEMM.
+template <int NH>
+void launch_rs_pair(const GemmRsArgs& a, const gemm::RsNvSched& base, const gemm::RsNvEpi& e0,
+                    const gemm::DoneTable& dt, int G, cudaStream_t s) {
+  using namespace gemm;
+  using Cf = pair::PairCfg<NH>;
+  const int Mr = a.M / a.n;
+  if (Mr % (2 * BM) || a.N % (NH * 256) || a.trace || a.join_reduce)
+    throw std::runtime_error("gicc::gemm_rs (pairs): need M/ranks % 256 == 0, N % (pair*256) == 0, no join, no trace");
+  const int Gp = G & ~1;
+  const CUtensorMap tA = make_tmap_2d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, a.lda, BM, BK,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tB = make_tmap_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.ldb, pair::BN2 / 2, BK,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  RsNvPairSched<NH> sc;
+  static_cast<RsNvSched&>(sc) = base;
+  sc.G = Gp;
+  sc.C = a.comm_ctas > 0 && a.comm_ctas < Gp ? a.comm_ctas : 16;
+  sc.nbo2 = Mr / (2 * BM);
+  sc.num_n = a.N / (NH * 256);
+  sc.bn = NH * 256;
+  sc.tile_base = (unsigned long long)(a.epoch - 1) * (unsigned long long)(a.n * sc.nbo2 * sc.num_n + Gp / 2);
+  sc.group = a.raster_group > 0 ? a.raster_group : 8;
+  RsNvPairEpi e;
+  static_cast<RsNvEpi&>(e) = e0;
+  e.trace_epi = nullptr;
+  e.num_n = sc.num_n;
+  e.Mr = Mr;
+  static bool attr[2][64] = {};
+  int dev = 0;
+  GICC_CUDA(cudaGetDevice(&dev));
+  if (!attr[NH - 1][dev]) {
+    GICC_CUDA(cudaFuncSetAttribute(k_gemm_rs_nvls_pair<NH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   Cf::kSmemBytes));
+    attr[NH - 1][dev] = true;
+  }
+  k_gemm_rs_nvls_pair<NH><<<Gp, Cf::threads(kCommWarpsAG), Cf::kSmemBytes, s>>>(
       tA, tB, sc, e, dt, device_error_record(), a.timeout_ns ? a.timeout_ns : default_timeout_ns());
   GICC_CUDA(cudaGetLastError());
 }
@@ -945,6 +1044,11 @@ void gemm_rs(const GemmRsArgs& a, cudaStream_t s) {
     e.epoch = a.epoch;
     DoneTable dt{};
     for (int i = 0; i < a.n; ++i) dt.p[i] = a.done[i];
+    if (a.pair) {
+      if (a.pair == 1) launch_rs_pair<1>(a, sc, e, dt, G, s);
+      else launch_rs_pair<2>(a, sc, e, dt, G, s);
+      return;
+    }
     constexpr uint32_t smem = Cfg<BN_>::kSmemBytes;
     static bool attr_nv[64] = {false};
     int dev = 0;

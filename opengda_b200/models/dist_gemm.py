@@ -68,9 +68,11 @@ class DistGemm:
         self.rs_raster_group = 0
         self.trace: Optional[torch.Tensor] = None
         self.diag = 0
-        # AG tensor-core tiles: 0 = one CTA per 128 x 256 tile; 1 / 2 = CTA pairs (cta_group::2)
-        # with 256 x 256 / 256 x 512 tiles.  Fixed by the first call (the counters depend on it).
-        self.pair = 0
+        # Tensor-core tiles of the fused kernels (AG, and RS over NVLS): 0 = one CTA per
+        # 128 x 256 tile; 1 / 2 = CTA pairs (cta_group::2) with 256 x 256 / 256 x 512 tiles.
+        # Fixed by the first call (the counters depend on it).  Default: the 256 x 512 pair
+        # tile where it fills the CTA pairs about as evenly as 128 x 256 tiles fill the SMs.
+        self.pair = self._default_pair() if (w > 1 and fused and (mode == "ag" or self.nvls)) else 0
         if w > 1 and fused:
             # fused kernels: double-buffered landing areas + epoch counters in the signal heap
             if mode == "ag":
@@ -114,6 +116,21 @@ class DistGemm:
                 self.P = rt.alloc_tensor((M, N), torch.bfloat16)  # bf16 partials, f32 reduction
                 self.C = torch.empty(M // w, N, dtype=torch.bfloat16, device=self.device)
                 self.launches_per_step = 1 + 2 + 1
+
+    def _default_pair(self) -> int:
+        w = self.world
+        rows, cols = (self.M, self.N // w) if self.mode == "ag" else (self.M, self.N)
+        if (self.M // w) % 256 or cols % 512 or self.transfer != "sm":
+            return 0
+        # B200: 148 SMs (used where no GPU is visible, e.g. host-side tests)
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count if torch.cuda.is_available() else 148
+
+        def fill(tiles: int, slots: int) -> float:
+            return tiles / (-(-tiles // slots) * slots)
+
+        t2 = (rows // 256) * (cols // 512)
+        t0 = (rows // 128) * (cols // 256)
+        return 2 if t2 >= sms // 2 and fill(t2, sms // 2) >= fill(t0, sms) - 0.05 else 0
 
     # shapes of this rank's operands
     def a_shape(self):
@@ -228,7 +245,7 @@ class DistGemm:
                                 C.stride(0), self.epoch, self.grid, self.rt.timeout_ns, buf.mc_ptr, self.band_tiles,
                                 self.tile_counter, self.rs_reduce_ctas, self.units_per_band,
                                 self.trace.data_ptr() if self.trace is not None else 0, int(self.rs_join),
-                                self.unit_counter, self.rs_raster_group)
+                                self.unit_counter, self.rs_raster_group, self.pair)
                 else:
                     n.k_gemm_rs(w, r, self.M, self.N, self.K // w, A.data_ptr(), A.stride(0), B.data_ptr(),
                                 B.stride(0), self._peer_ptrs(buf, p), self.arrivals, self.done, C.data_ptr(),

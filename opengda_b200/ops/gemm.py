@@ -20,7 +20,7 @@ def gemm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = None, alph
     return native().gemm(A, B, out, float(alpha), out_dtype == torch.float32, int(bn))
 
 
-def set_tuning(group_m: int = 16, l2_hint: int = 0, pair_group_m: int = 8) -> None:
+def set_tuning(group_m: int = 16, l2_hint: int = 0, pair_group_m: int = 16) -> None:
     """Process-wide tuning of ``gemm`` (A/B experiments; the defaults are the measured
     configuration): m-blocks per raster group, L2 eviction hints on the operand loads
     (0 none, 1 keep A / stream B, 2 keep B / stream A), and the CTA-pair kernel's raster

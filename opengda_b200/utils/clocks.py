@@ -89,8 +89,17 @@ class ClockSampler:
             for name, v in zip(REASONS, r[4]):
                 if v.lower() == "active":
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(r[1] for r in loaded), "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(rows)}
+        watts = []
+        for r in loaded:
+            try:
+                watts.append(float(r[3]))
+            except ValueError:
+                pass
+        out = {"sm_mhz": statistics.median(r[1] for r in loaded), "sm_max_mhz": mx,
+               "reasons": sorted(reasons), "samples": len(rows)}
+        if watts:
+            out["power_w"] = round(statistics.median(watts), 1)
+        return out
 
 
 def gather_clock_summary(summary: dict) -> dict:

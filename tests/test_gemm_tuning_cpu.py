@@ -5,7 +5,7 @@ from opengda_b200.ops.gemm import set_tuning, tuning
 
 
 def test_tuning_roundtrip_and_validation():
-    assert tuning() == {"group_m": 16, "l2_hint": 0, "pair_group_m": 8}
+    assert tuning() == {"group_m": 16, "l2_hint": 0, "pair_group_m": 16}
     try:
         set_tuning(group_m=8, l2_hint=2, pair_group_m=4)
         assert tuning() == {"group_m": 8, "l2_hint": 2, "pair_group_m": 4}
@@ -15,7 +15,7 @@ def test_tuning_roundtrip_and_validation():
         assert tuning() == {"group_m": 8, "l2_hint": 2, "pair_group_m": 4}  # a rejected call changes nothing
     finally:
         set_tuning()
-    assert tuning() == {"group_m": 16, "l2_hint": 0, "pair_group_m": 8}
+    assert tuning() == {"group_m": 16, "l2_hint": 0, "pair_group_m": 16}
 
 
 def test_tuning_from_environment():

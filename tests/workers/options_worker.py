@@ -52,7 +52,8 @@ def main():
                                      ("rs_group2", "rs", {}, {"rs_raster_group": 2}),
                                      ("ag_unicast", "ag", {"nvls": False}, {}), ("rs_unicast", "rs", {"nvls": False}, {}),
                                      ("ag_pair1", "ag", {}, {"pair": 1}), ("ag_pair2", "ag", {}, {"pair": 2}),
-                                     ("ag_pair2_unicast", "ag", {"nvls": False}, {"pair": 2})):
+                                     ("ag_pair2_unicast", "ag", {"nvls": False}, {"pair": 2}),
+                                     ("rs_pair1", "rs", {}, {"pair": 1}), ("rs_pair2", "rs", {}, {"pair": 2})):
             # CTA-pair tiles need 256-row bands per shard and 512-column blocks per rank
             M = Nn = 4096 if "pair" in attr else 2048
             K = 2048
