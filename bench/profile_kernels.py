@@ -1,8 +1,10 @@
 """Small single-GPU workloads for kernel profiling (ncu) -- one kernel family per case,
 a few launches, a few GB on the device at most.
 
-    python bench/profile_kernels.py gemm 8192          # k_gemm_bf16, 4 launches
-    python bench/profile_kernels.py gemm_pair 8192     # k_gemm_bf16_pair (CTA pairs), 4 launches
+    python bench/profile_kernels.py gemm 8192          # k_gemm_bf16 (128 x 256 tiles), 4 launches
+    python bench/profile_kernels.py gemm_pair 8192     # k_gemm_bf16_pair<1> (CTA pairs, 256 x 256), 4 launches
+    python bench/profile_kernels.py gemm_pair_wide 8192  # k_gemm_bf16_pair<2> (CTA pairs, 256 x 512), 4 launches
+    python bench/profile_kernels.py cublas 8192        # torch.matmul (cuBLAS) on the same operands, 4 launches
     python bench/profile_kernels.py jacobi 8192 8192   # k_jacobi, 4 launches
     python bench/profile_kernels.py moe 1024           # MoE layer (n=1), 2 forwards
     python bench/profile_kernels.py copy 268435456     # k_copy (local HBM copy)
@@ -28,16 +30,17 @@ def main():
     from opengda_b200 import native
     from opengda_b200.ops.gemm import check_errors, gemm
     torch.manual_seed(0)
-    if case in ("gemm", "gemm_pair"):
+    if case in ("gemm", "gemm_pair", "gemm_pair_wide", "cublas"):
         M = N = K = args[0] if args else 8192
         A = torch.randn(M, K, device="cuda").to(torch.bfloat16)
         B = torch.randn(N, K, device="cuda").to(torch.bfloat16)
         C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        bn = {"gemm": 256, "gemm_pair": 512, "gemm_pair_wide": 1024}.get(case)
         for _ in range(4):
-            if case == "gemm":
-                gemm(A, B, out=C)
+            if bn is None:
+                torch.matmul(A, B.t(), out=C)
             else:
-                native().gemm(A, B, out=C, bn=512)
+                gemm(A, B, out=C, bn=bn)
     elif case == "jacobi":
         from opengda_b200.models.jacobi import Jacobi
         nx = args[0] if args else 8192
