@@ -353,7 +353,7 @@ struct G1SchedT {
     const int tid = cw * 32 + lane;
     constexpr int kT = kCommWarps * 32;
     const int nvec = H / 8;  // 16-byte vectors per row
-    constexpr int kBatch = 4;  // rows per fence / barrier
+    constexpr int kBatch = 16;  // rows per fence / barrier (a fence waits for every store in flight)
     constexpr int kVec = 8;    // vectors in flight per thread
     if ((int)blockIdx.x >= C) return;
     // CTA c owns pairs c, c+C, c+2C, ... (send order, so every owner's first expert
