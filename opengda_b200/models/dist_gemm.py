@@ -15,6 +15,7 @@ rotated around the ring while a SIMT kernel accumulates with atomicAdd).
 """
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -72,7 +73,13 @@ class DistGemm:
         # 128 x 256 tile; 1 / 2 = CTA pairs (cta_group::2) with 256 x 256 / 256 x 512 tiles.
         # Fixed by the first call (the counters depend on it).  Default: the 256 x 512 pair
         # tile where it fills the CTA pairs about as evenly as 128 x 256 tiles fill the SMs.
+        # GICC_DIST_GEMM_PAIR=0|1|2 overrides the default (A/B experiments).
         self.pair = self._default_pair() if (w > 1 and fused and (mode == "ag" or self.nvls)) else 0
+        env_pair = os.environ.get("GICC_DIST_GEMM_PAIR")
+        if env_pair not in (None, "") and w > 1 and fused and (mode == "ag" or self.nvls):
+            if env_pair not in ("0", "1", "2"):
+                raise ValueError("GICC_DIST_GEMM_PAIR must be 0, 1 or 2")
+            self.pair = int(env_pair)
         if w > 1 and fused:
             # fused kernels: double-buffered landing areas + epoch counters in the signal heap
             if mode == "ag":
