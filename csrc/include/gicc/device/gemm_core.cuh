@@ -348,7 +348,7 @@ __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensor
       }
       if (t >= ntiles) break;
       TileInfo ti = sched.tile(t);
-      if (!ptx::mbar_wait(&tfull[acc], acc_phase, timeout_ns, abort_flag)) {
+      if (!ptx::mbar_wait_long(&tfull[acc], acc_phase, timeout_ns, abort_flag)) {
         if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_GEMM_PIPE, rank, -1, 3, 0);
         *abort_flag = 1;
         break;

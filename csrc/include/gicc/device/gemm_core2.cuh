@@ -412,7 +412,7 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
       if (t >= ntiles) break;
       TileInfo ti = sched.tile(t);
       ti.m0 += (int)crank * BM;  // this CTA's 128 rows of the pair tile
-      if (!ptx::mbar_wait(&tfull[acc], acc_phase, timeout_ns, abort_flag)) {
+      if (!ptx::mbar_wait_long(&tfull[acc], acc_phase, timeout_ns, abort_flag)) {
         if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_GEMM_PIPE, rank, (int)crank, 3, 0);
         *abort_flag = 1;
         break;

@@ -177,6 +177,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread may sleep until the phase completes or
+// `hint_ns` elapses, instead of returning after the hardware's default interval.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for a phase that is expected to take long (a whole tile): the thread sleeps
+// in the barrier (up to 20 us per try) rather than spinning, which saves issue slots and
+// power; the abort flag and the timeout are checked after every try.
+__device__ __forceinline__ bool mbar_wait_long(uint64_t* bar, uint32_t parity, uint64_t timeout_ns,
+                                               volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (abort_flag != nullptr && *abort_flag) return false;
+    if (globaltimer() - t0 > timeout_ns) return false;
+  }
+}
+
 // Bounded wait on an mbarrier phase.  Returns false (without waiting further) when the
 // timeout elapses or when another role of the CTA raised `abort_flag`.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns,
