@@ -134,6 +134,7 @@ def main() -> int:
                  transfer=args.transfer if args.mode == "ag" else "sm")
     if args.mode == "rs" and not m.nvls:
         raise SystemExit("the trace covers the NVLS reduce-scatter kernel only")
+    m.pair = 0  # the trace buffer belongs to the single-CTA kernels
     m.units_per_band = args.units
     m.rs_join = bool(args.join)
     m.rs_raster_group = args.raster_group
