@@ -127,6 +127,7 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--unfused", action="store_true", help="decomposed path: copy kernels + GEMM (A/B only)")
     ap.add_argument("--no-nccl-arm", action="store_true", help="skip the same-run NCCL(+cuBLAS) comparison arm")
+    ap.add_argument("--no-tune", action="store_true", help="AG, several GPUs: keep the default number of pushing CTAs")
     ap.add_argument("--transfer", default="sm", choices=["sm", "ce"],
                     help="fused AG: SM pushes (NVLS multicast or unicast) or copy engines (A/B option)")
     args = ap.parse_args()
@@ -170,6 +171,10 @@ def main() -> int:
     del Afull, Bfull
     torch.cuda.empty_cache()
     zero_copy = world > 1 and args.mode == "ag" and args.impl == "ours"
+    tuned = {}
+    if zero_copy and not args.unfused and args.transfer == "sm" and not args.no_tune:
+        # pick the number of pushing CTAs on this node (before warm-up, outside the timed steps)
+        tuned = model.tune(A, B)
     if zero_copy:  # the shard lives in the symmetric landing buffers (both parities)
         model.a_slot(0).copy_(A)
         model.a_slot(1).copy_(A)
@@ -263,6 +268,10 @@ def main() -> int:
                 "numerics_rows": ("256 rows of the next rank's shard (gathered data), max over ranks"
                                   if args.mode == "ag" and world > 1 else "256 rows of each rank's output, max over ranks"),
                 "step_ms": step_ms,
+                "tiles": ("pair256x512" if getattr(model, "pair", 0) == 2 else "pair256x256"
+                          if getattr(model, "pair", 0) == 1 else "cta128x256") if world > 1 else "by shape",
+                "comm_ctas": getattr(model, "comm_ctas", None) if world > 1 else None,
+                "comm_ctas_tuning_ms": {str(k): round(v, 4) for k, v in tuned.items()} or None,
             },
             "impl": args.impl,
             "clocks": clocks,

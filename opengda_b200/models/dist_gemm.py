@@ -139,6 +139,39 @@ class DistGemm:
         t0 = (rows // 128) * (cols // 256)
         return 2 if t2 >= sms // 2 and fill(t2, sms // 2) >= fill(t0, sms) - 0.05 else 0
 
+    def tune(self, A: torch.Tensor, B: torch.Tensor, comm_ctas=None, calls: int = 3) -> dict:
+        """Fused all-gather GEMM on several ranks: time candidate numbers of pushing CTAs on
+        this node and keep the fastest.  How fast a few SMs fill the NVLink ingress differs
+        from node to node (NVLS multicast or unicast, switch load), so the count is measured
+        rather than fixed.  Each candidate gets one untimed call and `calls` timed calls
+        (device time of the calls, max over ranks); A (this rank's shard) goes into both
+        landing buffers first, so the calls read it in place.  Collective: every rank calls
+        it with the same arguments.  Returns {comm_ctas: ms per call}; other modes return {}."""
+        if not (self.fused and self.mode == "ag" and self.world > 1 and self.transfer == "sm"):
+            return {}
+        from ..parallel.bootstrap import allreduce_max
+
+        cands = list(comm_ctas) if comm_ctas else ([8, 16, 24, 32] if self.nvls else [16, 32, 48])
+        self.a_slot(0).copy_(A)
+        self.a_slot(1).copy_(A)
+        boot = self.rt.boot
+        res = {}
+        for c in cands:
+            self.comm_ctas = c
+            self(self.a_slot(), B)
+            torch.cuda.synchronize(self.device)
+            boot.barrier()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(calls):
+                self(self.a_slot(), B)
+            e.record()
+            torch.cuda.synchronize(self.device)
+            res[c] = allreduce_max(boot, s.elapsed_time(e) / calls)
+        self.comm_ctas = min(res, key=res.get)
+        self.rt.check_device_errors()
+        return res
+
     # shapes of this rank's operands
     def a_shape(self):
         w = self.world
