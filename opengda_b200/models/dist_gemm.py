@@ -24,6 +24,12 @@ from ..ops.gemm import gemm
 from ..utils.graphs import refuse_capture
 
 
+# The fused kernels on CTA pairs become the default once their multi-GPU checks have passed
+# on B200s (tests/test_options_gpu.py::test_pending_options_multigpu); until then they run
+# when asked for (DistGemm.pair, GICC_DIST_GEMM_PAIR).
+PAIR_BY_DEFAULT = False
+
+
 class DistGemm:
     def __init__(self, M: int, N: int, K: int, mode: str = "ag", rt=None, device: Optional[torch.device] = None,
                  fused: bool = True, nvls: Optional[bool] = None, transfer: str = "sm"):
@@ -74,7 +80,7 @@ class DistGemm:
         # Fixed by the first call (the counters depend on it).  Default: the 256 x 512 pair
         # tile where it fills the CTA pairs about as evenly as 128 x 256 tiles fill the SMs.
         # GICC_DIST_GEMM_PAIR=0|1|2 overrides the default (A/B experiments).
-        self.pair = self._default_pair() if (w > 1 and fused and (mode == "ag" or self.nvls)) else 0
+        self.pair = self._default_pair() if (w > 1 and fused and (mode == "ag" or self.nvls) and PAIR_BY_DEFAULT) else 0
         env_pair = os.environ.get("GICC_DIST_GEMM_PAIR")
         if env_pair not in (None, "") and w > 1 and fused and (mode == "ag" or self.nvls):
             if env_pair not in ("0", "1", "2"):
