@@ -75,6 +75,10 @@ int main(int argc, char** argv) {
     const size_t flags = rt.signal_alloc(2);  // [0] top-halo arrivals, [1] bottom-halo arrivals
     float* a[2] = {static_cast<float*>(buf[0].ptr), static_cast<float*>(buf[1].ptr)};
     gicc::ops::jacobi_init(a[0], a[1], nx, ny, rows, g0, seed, nullptr);
+    // The init writes both buffers' halo rows; no rank may push a row into a neighbour before
+    // that neighbour's init has completed, or the init would overwrite it.
+    GICC_CUDA(cudaDeviceSynchronize());
+    rt.barrier();
     const int ctas = gicc::ops::jacobi_ctas_per_row(nx);
     double* norm = nullptr;
     GICC_CUDA(cudaMalloc(&norm, sizeof(double)));

@@ -59,6 +59,12 @@ class Jacobi:
         self.cur = 0
         self.done = 0  # iterations completed (same count on every rank)
         native().k_jacobi_init(self.bufs[0].data_ptr(), self.bufs[1].data_ptr(), nx, ny, self.rows, self.g0, seed)
+        if self.world > 1:
+            # The init writes both buffers' halo rows, which the neighbours overwrite with their
+            # pushed rows from the first iteration on: no rank may push before every rank's init
+            # has completed, or the init would clobber the pushed row.
+            torch.cuda.synchronize(self.device)
+            rt.barrier()
         self.norm_buf = torch.zeros(1, dtype=torch.float64, device=self.device)
         self.persistent = persistent
         if persistent:
