@@ -62,7 +62,9 @@ class DistGemm:
         if transfer == "ce":
             nvls = False
         self.nvls = bool(nvls if nvls is not None else (rt is not None and w > 1 and rt.multicast_supported))
-        self.units_per_band = 4
+        # Pieces each 128-row band of the shard is pushed in.  With NVLS, 16 pieces let the
+        # pushing CTAs finish the lowest bands first (8 GPUs: 1.015 ms against 1.114 ms with 4)
+        self.units_per_band = 16 if (self.nvls and mode == "ag") else 4
         self.grid = 0
         # NVLS at 8 GPUs is bound by each GPU's NVLink ingress (7 shards arrive at once), so
         # more CTAs push there; at 2-4 GPUs 8 keep well ahead of the tensor cores.
