@@ -654,12 +654,29 @@ struct G2StageSched {
       const int e = packed >> 22, mb = (packed >> 8) & 0x3fff, nb = packed & 0xff;
       const int a_row = expert_base[e] + mb * BM;
       const int valid = min(BM, expert_rows[e] - mb * BM);
-      for (int row = cw; row < valid; row += kCommWarps) {
-        const int4 m = meta[a_row + row];
-        const uint4 v = reinterpret_cast<const uint4*>(y + (size_t)(a_row + row) * H + nb * 256)[lane];
-        uint16_t* dst = reinterpret_cast<uint16_t*>(comb.p[m.x]) + (size_t)m.y * H + nb * 256;
-        ptx::st_v4_na(reinterpret_cast<uint4*>(dst) + lane, v);
-        if (lane == 0) atomicAdd(&cnt[m.x], 1u);
+      // Each warp loads kRows rows before it stores any, so kRows loads per lane are in
+      // flight (one row at a time leaves a single load in flight and bounds the push rate
+      // by the load latency).
+      constexpr int kRows = 8;
+      for (int row0 = cw * kRows; row0 < valid; row0 += kCommWarps * kRows) {
+        int4 m[kRows];
+        uint4 v[kRows];
+#pragma unroll
+        for (int k = 0; k < kRows; ++k) {
+          const int row = row0 + k;
+          if (row < valid) {
+            m[k] = meta[a_row + row];
+            v[k] = reinterpret_cast<const uint4*>(y + (size_t)(a_row + row) * H + nb * 256)[lane];
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < kRows; ++k) {
+          if (row0 + k < valid) {
+            uint16_t* dst = reinterpret_cast<uint16_t*>(comb.p[m[k].x]) + (size_t)m[k].y * H + nb * 256;
+            ptx::st_v4_na(reinterpret_cast<uint4*>(dst) + lane, v[k]);
+            if (lane == 0) atomicAdd(&cnt[m[k].x], 1u);
+          }
+        }
       }
       ptx::fence_acq_rel_sys();
       asm volatile("bar.sync 2, %0;" ::"n"(kT) : "memory");
@@ -779,14 +796,25 @@ __global__ void __launch_bounds__(256) k_moe_return(ReturnArgs a, ErrorRecord* e
       const float gate = __int_as_float(m.z);
       const uint4* src = reinterpret_cast<const uint4*>(a.recv + (size_t)(row0 + i) * a.H);
       uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.comb.p[m.x]) + (size_t)m.y * a.H);
-      for (int c = lane; c < a.H / 8; c += 32) {
-        const uint4 v = src[c];
-        uint4 o;
-        o.x = ptx::pack_bf16x2(gate * ptx::bf16_lo(v.x), gate * ptx::bf16_hi(v.x));
-        o.y = ptx::pack_bf16x2(gate * ptx::bf16_lo(v.y), gate * ptx::bf16_hi(v.y));
-        o.z = ptx::pack_bf16x2(gate * ptx::bf16_lo(v.z), gate * ptx::bf16_hi(v.z));
-        o.w = ptx::pack_bf16x2(gate * ptx::bf16_lo(v.w), gate * ptx::bf16_hi(v.w));
-        ptx::st_v4_na(dst + c, o);
+      // kU loads per lane in flight before the stores (one at a time is latency-bound)
+      constexpr int kU = 7;
+      const int nv = a.H / 8;
+      for (int c0 = lane; c0 < nv; c0 += 32 * kU) {
+        uint4 v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+          if (c0 + 32 * u < nv) v[u] = src[c0 + 32 * u];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          if (c0 + 32 * u < nv) {
+            uint4 o;
+            o.x = ptx::pack_bf16x2(gate * ptx::bf16_lo(v[u].x), gate * ptx::bf16_hi(v[u].x));
+            o.y = ptx::pack_bf16x2(gate * ptx::bf16_lo(v[u].y), gate * ptx::bf16_hi(v[u].y));
+            o.z = ptx::pack_bf16x2(gate * ptx::bf16_lo(v[u].z), gate * ptx::bf16_hi(v[u].z));
+            o.w = ptx::pack_bf16x2(gate * ptx::bf16_lo(v[u].w), gate * ptx::bf16_hi(v[u].w));
+            ptx::st_v4_na(dst + c0 + 32 * u, o);
+          }
+        }
       }
       if (lane == 0) atomicAdd(&cnt[m.x], (uint32_t)(a.H / 256));
     }
