@@ -4,7 +4,7 @@ ring; default N = 4096 as there): this framework's one-kernel-per-step ring (NVL
 inside the SGEMM kernel) against NCCL send/recv + cuBLAS fp32, both timed on the device as
 the max over ranks, with an fp64 CPU check of sampled elements of C.
 
-    python bench/ring_mm_bench.py [--n 4096]
+    python bench/ring_mm_bench.py [--size 4096]
     torchrun --nproc-per-node N bench/ring_mm_bench.py
 """
 from __future__ import annotations
@@ -23,7 +23,7 @@ import torch.distributed as dist  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--n", type=int, default=4096, help="matrix edge N")
+    ap.add_argument("--size", dest="n", type=int, default=4096, help="matrix edge N")
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--push-ctas", type=int, default=8)
