@@ -67,8 +67,12 @@ class Allreduce:
         nbytes = count * 2
         if nbytes <= 256 * 1024 or self.n == 1:
             return ONESHOT
-        # NVLS moves 1/n of the data per GPU; with two ranks it saves nothing over two-shot
-        return NVLS if (self.rt.multicast_supported and self.n > 2) else TWOSHOT
+        # NVLS moves 1/n of the data per GPU; with two ranks it saves nothing over two-shot.
+        # Measured at 8 GPUs: NVLS leads up to 256 MiB (724 GB/s bus bandwidth there) and falls
+        # behind two-shot at 1 GiB (588 against 646 GB/s).
+        if self.rt.multicast_supported and self.n > 2 and nbytes < (512 << 20):
+            return NVLS
+        return TWOSHOT
 
     def __call__(self, count: int, algo: str = "auto", scale: float = 1.0, blocks: int = 0) -> torch.Tensor:
         if count % 8 or count > self.max_count:
