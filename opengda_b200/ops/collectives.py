@@ -30,7 +30,8 @@ class Allreduce:
 
     ``inp`` is a symmetric bf16 buffer (write the data into ``allreduce.input(count)``),
     the result goes to a symmetric output buffer (bf16 or f32).  ``algo``: "oneshot",
-    "twoshot", "nvls" or "auto" (one-shot <= 256 KiB, NVLS when available, else two-shot).
+    "twoshot", "nvls" or "auto" (one-shot <= 256 KiB, NVLS when available on more than two
+    ranks below 512 MiB, else two-shot).
 
     ``graph_safe=True`` keeps the call counter on the device (each kernel reads it and its
     last CTA advances it), so calls can be captured in a CUDA graph (``torch.cuda.graph``)
