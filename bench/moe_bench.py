@@ -33,11 +33,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--no-baseline", action="store_true")
     ap.add_argument("--out", default=None)
-    ap.add_argument("--dispatch-ctas", type=int, default=0, help="CTAs that dispatch (0 = all; A/B option)")
+    ap.add_argument("--dispatch-ctas", type=int, default=None, help="CTAs that dispatch (0 = all; default: the layer's)")
     ap.add_argument("--comm-only", action="store_true",
                     help="time the dispatch + combine round trip alone (identity experts), vs NCCL all_to_all")
-    ap.add_argument("--combine-ctas", type=int, default=0,
-                    help="CTAs that push the combine (0 = all, from the epilogue; A/B option)")
+    ap.add_argument("--combine-ctas", type=int, default=None,
+                    help="CTAs that push the combine (0 = all, from the epilogue; default: the layer's)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -56,8 +56,10 @@ def main():
 
     clk = BenchClocks(local)
     layer = MoELayer(args.tokens, args.hidden, args.experts, args.topk, args.inter, rt=rt)
-    layer.dispatch_ctas = args.dispatch_ctas
-    layer.combine_ctas = args.combine_ctas
+    if args.dispatch_ctas is not None:
+        layer.dispatch_ctas = args.dispatch_ctas
+    if args.combine_ctas is not None:
+        layer.combine_ctas = args.combine_ctas
     x, logits = make_inputs(args.tokens, args.hidden, args.experts, rank, seed=4)
 
     def timeit(fn, steps, warmup):

@@ -98,7 +98,9 @@ class MoELayer:
         # CTAs that push the second GEMM's rows back to the sources (0 = every CTA pushes its
         # own tiles from the epilogue).  With fewer, the rows are staged in local HBM
         # (self.y_stage, [cap, H] bf16, allocated on first use) and queued for those CTAs.
-        self.combine_ctas = 0
+        # Default: staged with 64 pushing CTAs at 8 or more ranks, where 7/8 of the rows leave
+        # the GPU (8 GPUs: 5.00 ms per layer against 5.49 ms with epilogue pushes).
+        self.combine_ctas = 64 if n >= 8 else 0
         self.y_stage = None
         self.topk_idx = i32(pairs)
         self.topk_w = torch.zeros(pairs, dtype=torch.float32, device=dev)

@@ -134,13 +134,13 @@ def test_counter_settings_are_frozen_after_the_first_call(monkeypatch):
         m(A, B)
 
 
-@pytest.mark.parametrize("mode,n,nvls,want", [("ag", 2, True, 2), ("ag", 4, True, 2), ("ag", 8, True, 0),
+@pytest.mark.parametrize("mode,n,nvls,want", [("ag", 2, True, 2), ("ag", 4, True, 2), ("ag", 8, True, 1),
                                               ("rs", 8, True, 2), ("rs", 2, False, 0), ("ag", 2, False, 2)])
 def test_tile_choice_by_shape(monkeypatch, mode, n, nvls, want):
     """256 x 512 CTA-pair tiles where they fill the 74 CTA pairs about as evenly as 128 x 256
-    tiles fill the 148 SMs (16384^3: yes at 2 and 4 GPUs, no for the all-gather at 8, whose
-    2048-column shard gives 256 pair tiles = 3.5 waves); the unicast reduce-scatter has no
-    pair variant.  GICC_DIST_GEMM_PAIR overrides the choice."""
+    tiles fill the 148 SMs (16384^3: yes at 2 and 4 GPUs; not for the all-gather at 8, whose
+    2048-column shard gives 256 such tiles = 3.5 waves, so 256 x 256 pair tiles there); the
+    unicast reduce-scatter has no pair variant.  GICC_DIST_GEMM_PAIR overrides the choice."""
     monkeypatch.delenv("GICC_DIST_GEMM_PAIR", raising=False)
     m = dist_gemm.DistGemm(16384, 16384, 16384, mode, rt=_FakeRt(n, 0, mc=True), device=torch.device("cpu"),
                            nvls=nvls)
