@@ -36,6 +36,9 @@ def main():
     ap.add_argument("--ag", default="1,4,0:16;1,4,2:16", help="all-gather variants (see the module docstring)")
     ap.add_argument("--rs-pair", default="2,0", help="reduce-scatter tile choices (NVLS)")
     ap.add_argument("--rs-ctas", default="16,32", help="reduce-scatter: reducing CTAs (NVLS)")
+    ap.add_argument("--rs-join", action="store_true",
+                    help="also time the NVLS reduce-scatter on single-CTA tiles with the join option "
+                         "(CTAs out of GEMM tiles join the reduction)")
     ap.add_argument("--no-rs", action="store_true")
     ap.add_argument("--out", default=None)
     args = ap.parse_args()
@@ -132,17 +135,20 @@ def main():
         rref = Af[rank * Mr + rrows].float() @ Bf.float().t()
         del Af, Bf
         torch.cuda.empty_cache()
-        variants = [(1, int(p)) for p in args.rs_pair.split(",")] + [(0, 0)]
-        for nv, pr in variants:
+        variants = [(1, int(p), False) for p in args.rs_pair.split(",")] + [(0, 0, False)]
+        if args.rs_join:
+            variants.append((1, 0, True))
+        for nv, pr, join in variants:
             m = DistGemm(M, N, K, "rs", rt=rt, device=dev, nvls=bool(nv))
             m.pair = pr
+            m.rs_join = join
             for c in ([int(x) for x in args.rs_ctas.split(",")] if nv else [0]):
                 m.rs_reduce_ctas = c
                 ms, clk = timeit(lambda: m(A, B))
                 C = m(A, B)
                 torch.cuda.synchronize()
                 rel = mx(((C[rrows].float() - rref).norm() / rref.norm()).item())
-                record(f"rs nvls={nv} pair={pr} reduce_ctas={c}", ms, clk, rel)
+                record(f"rs nvls={nv} pair={pr} join={int(join)} reduce_ctas={c}", ms, clk, rel)
             del m
             torch.cuda.synchronize()
             dist.barrier()
