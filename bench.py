@@ -10,7 +10,8 @@ Rank 0 prints one JSON line.  ``value`` is whole-job TFLOP/s = 2*M*N*K / step ti
 where the step time is the max over ranks of device time measured with CUDA events.
 ``e2e`` is the same metric through the public API (``DistGemm.__call__``) including
 the host->device copy of each step's A shard from pinned memory and a device->host read
-of the step's result checksum.
+of the step's result checksum.  ``nccl_arm`` is the NCCL + cuBLAS arm in the same process:
+the same device-timed steps and the same end-to-end loop (``nccl_arm.e2e``).
 """
 from __future__ import annotations
 
@@ -196,37 +197,39 @@ def main() -> int:
     h2d = A_host.numel() * A_host.element_size()
     feeder = HostFeeder(A.shape, A.dtype, dev)
 
-    def e2e_run(steps):
-        # step i's pinned H2D copy is issued during step i-1 (double-buffered side stream);
-        # every step ends with a 4-byte device->host read of its result checksum
-        feeder.submit(A_host)
-        for i in range(steps):
-            if i + 1 < steps:
-                feeder.submit(A_host)
-            a_dev = feeder.next()
-            out = model(a_dev, B)
-            feeder.release()
-            out.sum(dtype=torch.float32).item()  # 4-byte device->host read of a checksum
-
-    e2e_run(2)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    es.record()
-    e2e_run(e2e_steps)
-    ee.record()
-    torch.cuda.synchronize()
     from opengda_b200.utils.timing import max_over_ranks
 
-    e2e_ms = max_over_ranks(es.elapsed_time(ee) / e2e_steps)
+    def e2e_ms_of(fn):
+        def e2e_run(steps):
+            # step i's pinned H2D copy is issued during step i-1 (double-buffered side
+            # stream); every step ends with a 4-byte device->host read of its result checksum
+            feeder.submit(A_host)
+            for i in range(steps):
+                if i + 1 < steps:
+                    feeder.submit(A_host)
+                a_dev = feeder.next()
+                out = fn(a_dev, B)
+                feeder.release()
+                out.sum(dtype=torch.float32).item()  # 4-byte device->host read of a checksum
+
+        e2e_run(2)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        es.record()
+        e2e_run(e2e_steps)
+        ee.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(es.elapsed_time(ee) / e2e_steps)
+
+    e2e_ms = e2e_ms_of(model)
 
     # ---- the NCCL (+cuBLAS) arm, same process, same shapes, steps, warm-up and clock record
     arm = None
     if args.impl == "ours" and not args.no_nccl_arm:
         from opengda_b200.baselines.gemm_nccl import NcclDistGemm
 
-        del feeder, A_host
         try:
             base = NcclDistGemm(M, N, K, args.mode, device=dev)
             base_rel = check_numerics(base, A, B,
@@ -239,10 +242,16 @@ def main() -> int:
                    else "torch.matmul (cuBLAS)",
                    "value": round(flops / (b_ms * 1e-3) / 1e12, 2), "ms_per_step": round(b_ms, 4),
                    "step_ms": b_step_ms, "clocks": b_clocks, "numerics_rel_err_vs_fp32": round(base_rel, 6)}
+            # the same end-to-end loop (pinned H2D of A, D2H of a checksum) through the arm
+            b_e2e_ms = e2e_ms_of(base)
+            arm["e2e"] = {"value": round(flops / (b_e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                          "ms_per_step": round(b_e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+                          "api": "opengda_b200.baselines.gemm_nccl.NcclDistGemm.__call__"}
             del base
         except (RuntimeError, torch.cuda.OutOfMemoryError) as exc:  # the comparison arm must not cost our line
             arm = {"impl": "nccl+cublas", "error": f"{type(exc).__name__}: {exc}"[:300]}
         torch.cuda.empty_cache()
+    del feeder, A_host
     if rank == 0:
         out = {
             "metric": METRIC,

@@ -2,6 +2,7 @@
 (torch.matmul) on a square bf16 problem, C = A . B^T, f32 accumulation.
 
     python bench/gemm_bench.py [--size 16384] [--rounds 3] [--iters 30] [--tiles 256,512,1024]
+                               [--pair-opts h1p0,h0p4]
 
 Under the 1 kW power cap the SM clock depends on what ran just before, so the variants
 are timed round-robin (cuBLAS, then each tile, then again) and each keeps the median
@@ -10,13 +11,16 @@ warm-up launches (inputs 512 MiB each at 16384, larger than L2), with the SM clo
 power sampled by nvidia-smi during it.  `tflops_per_ghz` divides by the median SM clock,
 which separates how well a kernel keeps the tensor cores busy from how fast the power
 cap lets it clock.  Tiles: 128 / 256 = one CTA per 128 x bn tile; 512 = CTA pairs,
-256 x 256; 1024 = CTA pairs, 256 x 512.  Prints one JSON object.
+256 x 256; 1024 = CTA pairs, 256 x 512.  `--pair-opts` adds 256 x 512 variants with the
+pair kernel's options: `h<l2 hint>p<prefetch distance>[s<tma store>]` (`ops.gemm.set_tuning`'s
+pair_l2_hint, pair_prefetch and pair_tma_store).  Prints one JSON object.
 """
 from __future__ import annotations
 
 import argparse
 import json
 import os
+import re
 import statistics
 import sys
 
@@ -33,6 +37,7 @@ def main():
     ap.add_argument("--iters", type=int, default=30)
     ap.add_argument("--tiles", default="256,512,1024")
     ap.add_argument("--pair-group", type=int, default=0, help="raster group of the pair kernels (0 = default)")
+    ap.add_argument("--pair-opts", default="", help="extra 256x512 variants: comma list of h<l2 hint>p<prefetch>")
     ap.add_argument("--out", default=None)
     args = ap.parse_args()
     from opengda_b200 import native
@@ -41,7 +46,7 @@ def main():
 
     if args.pair_group:
         t = tuning()
-        set_tuning(group_m=t["group_m"], l2_hint=t["l2_hint"], pair_group_m=args.pair_group)
+        set_tuning(**dict(t, pair_group_m=args.pair_group))
     S = args.size
     g = torch.Generator(device="cuda").manual_seed(0)
     A = torch.randn(S, S, device="cuda", generator=g).to(torch.bfloat16)
@@ -49,12 +54,26 @@ def main():
     C = torch.empty(S, S, device="cuda", dtype=torch.bfloat16)
     ref = torch.matmul(A, B.t()).float()
     flop = 2.0 * S ** 3
+    base = tuning()
     variants = {"cublas": lambda: torch.matmul(A, B.t(), out=C)}
+    setups = {}
     for bn in (int(x) for x in args.tiles.split(",")):
         variants[f"tile{bn}"] = (lambda bn=bn: native().gemm(A, B, out=C, bn=bn))
+    for spec in (x for x in args.pair_opts.split(",") if x):
+        m = re.fullmatch(r"h(\d)p(\d+)(?:s(\d))?", spec)
+        if not m:
+            raise SystemExit(f"--pair-opts: {spec!r} is not h<hint>p<prefetch>[s<tma store>]")
+        variants[f"tile1024_{spec}"] = lambda: native().gemm(A, B, out=C, bn=1024)
+        setups[f"tile1024_{spec}"] = dict(base, pair_l2_hint=int(m[1]), pair_prefetch=int(m[2]),
+                                          pair_tma_store=int(m[3] or base["pair_tma_store"]))
+
+    def setup(name):
+        set_tuning(**setups.get(name, base))
+
     out = {"size": S, "rounds": args.rounds, "iters": args.iters, "pair_group_m": tuning()["pair_group_m"],
            "variants": {}}
     for name, fn in variants.items():
+        setup(name)
         fn()
         torch.cuda.synchronize()
         out["variants"][name] = {"rel_err_vs_cublas": float(((C.float() - ref).norm() / ref.norm()).item())}
@@ -62,6 +81,7 @@ def main():
     samples = {k: [] for k in variants}
     for _ in range(args.rounds):
         for name, fn in variants.items():
+            setup(name)
             for _ in range(3):
                 fn()
             torch.cuda.synchronize()
@@ -76,6 +96,7 @@ def main():
             c = cs.summary()
             samples[name].append((flop / ms / 1e9, c.get("sm_mhz"), c.get("power_w"), c.get("reasons", [])))
     check_errors()
+    set_tuning(**base)
     for name, v in samples.items():
         tf = statistics.median(x[0] for x in v)
         mhz = [x[1] for x in v if x[1]]

@@ -88,19 +88,27 @@ void bind_runtime(py::module_& m);  // runtime.cpp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "opengda_b200 native ops (sm_100a)";
-  m.def("set_gemm_tuning", [](int group_m, int l2_hint, int pair_group_m) {
+  m.def("set_gemm_tuning", [](int group_m, int l2_hint, int pair_group_m, int pair_l2_hint, int pair_prefetch,
+                              int pair_tma_store) {
     gicc::ops::GemmTuning t;
     t.group_m = group_m;
     t.l2_hint = l2_hint;
     t.pair_group_m = pair_group_m;
+    t.pair_l2_hint = pair_l2_hint;
+    t.pair_prefetch = pair_prefetch;
+    t.pair_tma_store = pair_tma_store;
     gicc::ops::set_gemm_tuning(t);
-  }, py::arg("group_m") = 16, py::arg("l2_hint") = 0, py::arg("pair_group_m") = 8);
+  }, py::arg("group_m") = 16, py::arg("l2_hint") = 0, py::arg("pair_group_m") = 16, py::arg("pair_l2_hint") = 0,
+     py::arg("pair_prefetch") = 0, py::arg("pair_tma_store") = 0);
   m.def("gemm_tuning", []() {
     const auto t = gicc::ops::gemm_tuning();
     py::dict d;
     d["group_m"] = t.group_m;
     d["l2_hint"] = t.l2_hint;
     d["pair_group_m"] = t.pair_group_m;
+    d["pair_l2_hint"] = t.pair_l2_hint;
+    d["pair_prefetch"] = t.pair_prefetch;
+    d["pair_tma_store"] = t.pair_tma_store;
     return d;
   });
   m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("out") = py::none(), py::arg("alpha") = 1.0,

@@ -12,8 +12,11 @@
 //   * NH = 1: the accumulator is double-buffered (2 x 256 of the 512 TMEM columns), so the
 //     epilogue of tile i overlaps the MMAs of tile i+1;
 //     NH = 2: one 512-column accumulator (all of TMEM), drained by 8 epilogue warps (two
-//     per TMEM lane quarter, one per column half) while the producer already loads the
-//     next tile's operands;
+//     per TMEM lane quarter, each 128 columns of each half) column half 0 first; the MMA
+//     thread starts the next tile on half 0 as soon as that half is free, for up to
+//     kStages - 1 k-steps, and issues the lagging half-1 MMAs of those k-steps once the
+//     epilogue has drained half 1 (the stages are released only then), so most of the
+//     drain overlaps tensor work;
 //   * the leader's tcgen05.commit arrives on the barrier of each CTA (two commits, no
 //     multicast form), and the peer CTA's epilogue warps arrive on the leader's
 //     "accumulator free" barrier remotely.
@@ -30,6 +33,7 @@
 // released.
 #pragma once
 #include <cstdint>
+#include <type_traits>
 
 #include "gicc/device/gemm_core.cuh"
 
@@ -54,7 +58,11 @@ struct PairCfg {
   __host__ __device__ static constexpr int threads(int comm_warps) { return kThreads + 32 * comm_warps; }
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
-  static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+  // Epilogues that stage C through shared memory (Epi::kStagedStore): two 32 x 32 bf16
+  // boxes per epilogue warp after the barrier area.
+  static constexpr uint32_t kBoxBytes = 32 * 32 * 2;
+  static constexpr uint32_t kSmemBytesStaged = kSmemBytes + kEpiWarps * 2 * kBoxBytes;
+  static_assert(kSmemBytesStaged <= 227 * 1024, "shared memory");
 };
 // The 256 x 256 configuration's constants, kept under their original names.
 constexpr int kStages = PairCfg<1>::kStages;
@@ -81,6 +89,18 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
           ptx::smem_u32(dst)),
       "l"(m), "r"(bar_cluster_addr), "r"(x), "r"(y)
       : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair_hint(void* dst, const CUtensorMap* m, uint32_t bar_cluster_addr, int x,
+                                                      int y, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(
+          ptx::smem_u32(dst)),
+      "l"(m), "r"(bar_cluster_addr), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+// Prefetch of one tile of a tensor map into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* m, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(m), "r"(x), "r"(y) : "memory");
 }
 __device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t accumulate) {
@@ -140,6 +160,27 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
+// Epilogues with `static constexpr bool kStagedStore = true` may store C through shared
+// memory and TMA (Epi::staged(), Epi::pack(), Epi::tmap(), Epi::chunk_in_bounds()).
+template <class E, class = void>
+struct epi_staged : std::false_type {};
+template <class E>
+struct epi_staged<E, std::void_t<decltype(E::kStagedStore)>> : std::integral_constant<bool, E::kStagedStore> {};
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+
+// Options of the operand loads (the plain GEMM's tuning; the fused kernels use none):
+// l2hint 1 = A kept in L2 / B streamed, 2 = the reverse; prefetch = k-steps ahead at which
+// each CTA's producer prefetches its A and B boxes into L2 while loading the current one.
+struct PairLoadOpts {
+  int l2hint = 0;
+  int prefetch = 0;
+};
+
 // Sched for pairs: tile(t) gives the pair tile (m0 = first of 256 rows, n0 = first of
 // NH*256 columns, kb range); the core derives each CTA's A row (m0 + 128*rank) and B rows
 // (n0 + h*256 + 128*rank for column half h).  Epi::store gets the CTA-local row (0..127)
@@ -157,7 +198,8 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 // after all of that CTA's epilogue warps stored their part.
 template <int NH = 1, class Sched, class Epi>
 __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUtensorMap* tmB, const Sched& sched,
-                                               Epi& epi, ErrorRecord* err, uint64_t timeout_ns, int rank) {
+                                               Epi& epi, ErrorRecord* err, uint64_t timeout_ns, int rank,
+                                               PairLoadOpts lopt = PairLoadOpts()) {
   using Cf = PairCfg<NH>;
   constexpr int S = Cf::kStages;
   constexpr int kAccs = Cf::kAccs;
@@ -248,6 +290,12 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
       for (int s = 0; s < S; ++s) armed[s] = 0;
       int qslot = 0;
       uint32_t qphase = 0;
+      uint64_t pol_a = 0, pol_b = 0;
+      if (lopt.l2hint != 0) {
+        const uint64_t keep = ptx::l2_policy_evict_last(), stream = ptx::l2_policy_evict_first();
+        pol_a = lopt.l2hint == 1 ? keep : stream;
+        pol_b = lopt.l2hint == 1 ? stream : keep;
+      }
       for (int t = pair_id; !*abort_flag; t += npairs) {
         if constexpr (kDyn) {
           if (leader) {
@@ -287,11 +335,26 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
           }
           const uint32_t bar = map_to(ptx::smem_u32(&full[stage]), 0);
           if (leader) ptx::mbar_arrive_expect_tx(&full[stage], 2 * Cf::kStageBytes);
-          tma_load_2d_pair(sA + stage * kABytes, tmA, bar, kb * BK, ti.a_row + (int)crank * BM);
+          const int a_y = ti.a_row + (int)crank * BM;
+          if (lopt.l2hint == 0) {
+            tma_load_2d_pair(sA + stage * kABytes, tmA, bar, kb * BK, a_y);
 #pragma unroll
-          for (int h = 0; h < NH; ++h)
-            tma_load_2d_pair(sB + (stage * NH + h) * kBBytes, tmB, bar, kb * BK,
-                             ti.b_row + h * BN2 + (int)crank * (BN2 / 2));
+            for (int h = 0; h < NH; ++h)
+              tma_load_2d_pair(sB + (stage * NH + h) * kBBytes, tmB, bar, kb * BK,
+                               ti.b_row + h * BN2 + (int)crank * (BN2 / 2));
+          } else {
+            tma_load_2d_pair_hint(sA + stage * kABytes, tmA, bar, kb * BK, a_y, pol_a);
+#pragma unroll
+            for (int h = 0; h < NH; ++h)
+              tma_load_2d_pair_hint(sB + (stage * NH + h) * kBBytes, tmB, bar, kb * BK,
+                                    ti.b_row + h * BN2 + (int)crank * (BN2 / 2), pol_b);
+          }
+          if (lopt.prefetch > 0 && kb + lopt.prefetch < ti.kb1) {
+            const int px = (kb + lopt.prefetch) * BK;
+            tma_prefetch_2d(tmA, px, a_y);
+#pragma unroll
+            for (int h = 0; h < NH; ++h) tma_prefetch_2d(tmB, px, ti.b_row + h * BN2 + (int)crank * (BN2 / 2));
+          }
           armed[stage]++;
           if (++stage == S) {
             stage = 0;
@@ -332,6 +395,7 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
         }
         if (t >= ntiles) break;
         TileInfo ti = sched.tile(t);
+        // NH = 1: tempty[acc] frees the whole accumulator; NH = 2: tempty[h] frees column half h.
         if (!ptx::mbar_wait(&tempty[acc], acc_phase ^ 1, timeout_ns, abort_flag)) {
           if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_GEMM_PIPE, rank, 0, 1, 0);
           *abort_flag = 1;
@@ -339,28 +403,77 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
         }
         ptx::tc_fence_after();
         const uint32_t d = tmem + acc * NH * BN2;
-        bool ok = true;
-        for (int kb = ti.kb0; kb < ti.kb1; ++kb) {
-          if (!ptx::mbar_wait(&full[stage], phase, timeout_ns, abort_flag)) {
-            ok = false;
-            break;
-          }
-          ptx::tc_fence_after();
-          const uint32_t a0 = ptx::smem_u32(sA + stage * kABytes);
-          const uint32_t b0 = ptx::smem_u32(sB + stage * NH * kBBytes);
+        // k-step kb's MMAs for column halves [h0, h1) from the stage that holds it
+        auto issue = [&](int st, int kb, int h0, int h1) {
+          const uint32_t a0 = ptx::smem_u32(sA + st * kABytes);
+          const uint32_t b0 = ptx::smem_u32(sB + st * NH * kBBytes);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = ptx::sdesc_kmajor_sw128(a0 + k * 32);
 #pragma unroll
             for (int h = 0; h < NH; ++h) {
+              if (h < h0 || h >= h1) continue;
               const uint64_t bd = ptx::sdesc_kmajor_sw128(b0 + h * kBBytes + k * 32);
               mma_pair(d + h * BN2, ad, bd, idesc, (kb > ti.kb0 || k > 0) ? 1u : 0u);
             }
           }
-          issued = true;
-          const uint32_t e_own = ptx::smem_u32(&empty[stage]);
+        };
+        auto release = [&](int st) {
+          const uint32_t e_own = ptx::smem_u32(&empty[st]);
           commit_pair(e_own);
           commit_pair(map_to(e_own, peer));
+        };
+        bool ok = true;
+        // NH = 2: the first `lag` k-steps run on half 0 only (their stages stay held), then
+        // half 1 catches up once the epilogue has drained it.  One stage is left to the
+        // producer so the k-step after the catch-up is already loaded.
+        const int nk = ti.kb1 - ti.kb0;
+        const int lag = NH == 2 ? (nk < S - 1 ? nk : S - 1) : 0;
+        if (lag > 0) {
+          int st = stage;
+          for (int i = 0; i < lag; ++i) {
+            if (!ptx::mbar_wait(&full[st], phase ^ (stage + i >= S ? 1u : 0u), timeout_ns, abort_flag)) {
+              ok = false;
+              break;
+            }
+            ptx::tc_fence_after();
+            issue(st, ti.kb0 + i, 0, 1);
+            issued = true;
+            if (++st == S) st = 0;
+          }
+          if (ok && !ptx::mbar_wait(&tempty[1], acc_phase ^ 1, timeout_ns, abort_flag)) {
+            if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_GEMM_PIPE, rank, 0, 8, 0);
+            *abort_flag = 1;
+            break;
+          }
+          if (ok) {
+            ptx::tc_fence_after();
+            for (int i = 0; i < lag; ++i) {
+              issue(stage, ti.kb0 + i, 1, NH);
+              release(stage);
+              if (++stage == S) {
+                stage = 0;
+                phase ^= 1;
+              }
+            }
+          }
+        } else if (NH == 2) {
+          if (!ptx::mbar_wait(&tempty[1], acc_phase ^ 1, timeout_ns, abort_flag)) {
+            if (!*abort_flag) report_error(err, GICC_ETIMEDOUT, W_GEMM_PIPE, rank, 0, 8, 0);
+            *abort_flag = 1;
+            break;
+          }
+          ptx::tc_fence_after();
+        }
+        for (int kb = ti.kb0 + lag; ok && kb < ti.kb1; ++kb) {
+          if (!ptx::mbar_wait(&full[stage], phase, timeout_ns, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          issue(stage, kb, 0, NH);
+          issued = true;
+          release(stage);
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
@@ -390,10 +503,22 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
   } else {
     // ---------------- epilogue (warps 2.., both CTAs) ----------------
     // Warp w may read TMEM lanes 32*(w%4)..+31; with NH = 2 warps 2..5 take columns
-    // 0..255 and warps 6..9 columns 256..511 of the same rows.
+    // 0..127 and warps 6..9 columns 128..255 of each column half of the same rows, half 0
+    // first, and free each half (tempty[h]) as soon as they have read it.
+    constexpr int kSeg = NH == 1 ? BN2 : BN2 / 2;  // columns of one half that a warp drains
+    // TMEM columns read per wait: as many as the registers of this launch allow (65536 per
+    // SM over Cf::threads(kCommWarps) threads, 1 CTA per SM)
+    constexpr int kRegs = 65536 / Cf::threads(Sched::kCommWarps);
+    constexpr int kW0 = kRegs >= 200 ? 128 : (kRegs >= 136 ? 64 : 32);
+    constexpr int kW = kW0 < kSeg ? kW0 : kSeg;
     const int q = warp & 3;
-    const int half = NH == 1 ? 0 : ((int)warp - 2) / 4;
+    const int part = NH == 1 ? 0 : ((int)warp - 2) / 4;
     const int row = q * 32 + lane;
+    // Staged stores: this warp's two 32 x 32 bf16 boxes, used in turn; the TMA store that
+    // read a box must have finished reading it before the box is written again.
+    constexpr bool kStaged = epi_staged<Epi>::value;
+    uint8_t* my_boxes = smem + S * Cf::kStageBytes + 256 + ((int)warp - 2) * 2 * Cf::kBoxBytes;
+    uint32_t box_turn = 0;
     const uint32_t tempty_leader0 = map_to(ptx::smem_u32(&tempty[0]), 0);
     const uint32_t tempty_leader1 = map_to(ptx::smem_u32(&tempty[1]), 0);
     int acc = 0;
@@ -418,27 +543,72 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
         break;
       }
       ptx::tc_fence_after();
-      const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + (acc * NH + half) * BN2;
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + acc * NH * BN2;
       epi.begin_tile(ti, row);
 #pragma unroll 1
-      for (int c = 0; c < BN2; c += 32) {
-        uint32_t r[32];
-        ptx::tmem_ld32(tbase + c, r);
-        ptx::tmem_ld_wait();
-        if constexpr (!Epi::kNeedsTileDone) {
-          if (c + 32 >= BN2) {
-            ptx::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+      for (int h = 0; h < NH; ++h) {
+        // the barrier that frees what this warp has read: the accumulator (NH = 1) or half h
+        const uint32_t free_bar = (NH == 1 ? acc : h) ? tempty_leader1 : tempty_leader0;
+#pragma unroll 1
+        for (int c = 0; c < kSeg; c += kW) {
+          // kW columns: every TMEM load issued before one wait (each wait is a round trip)
+          const int col0 = h * BN2 + part * kSeg + c;
+          uint32_t r[kW];
+#pragma unroll
+          for (int i = 0; i < kW / 32; ++i) ptx::tmem_ld32(tbase + col0 + 32 * i, r + 32 * i);
+          ptx::tmem_ld_wait();
+          // Epilogues that publish finished tiles free the last half only after tile_done
+          // (below); half 0 of a 512-column accumulator can go back at once, because the
+          // next tile's epilogue cannot start before half 1 is free.
+          if (!Epi::kNeedsTileDone || h + 1 < NH) {
+            if (c + kW >= kSeg) {
+              ptx::tc_fence_before();
+              __syncwarp();
+              if (lane == 0) arrive_cluster(free_bar);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < kW / 32; ++i) {
+            const int col = col0 + 32 * i;
+            const uint32_t* ri = r + 32 * i;
+            bool done = false;
+            if constexpr (kStaged) {
+              if (epi.staged()) {
+                uint8_t* box = my_boxes + (box_turn & 1) * Cf::kBoxBytes;
+                ++box_turn;
+                if (lane == 0) bulk_wait_read_1();  // the store issued from this box two chunks ago
+                __syncwarp();
+                uint4 v[4];
+                epi.pack(ri, v);
+                // row `lane` of the box (64 bytes); the 16-byte pieces are written in an
+                // order rotated by lane/2, so each group of 8 lanes covers all 32 banks
+                const uint32_t rowaddr = ptx::smem_u32(box) + lane * 64;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const int cj = (j + (int)(lane >> 1)) & 3;
+                  const uint4 w = cj == 0 ? v[0] : cj == 1 ? v[1] : cj == 2 ? v[2] : v[3];
+                  st_shared_v4(rowaddr + cj * 16, w);
+                }
+                ptx::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                  if (epi.chunk_in_bounds(ti, q * 32, col))
+                    ptx::tma_store_2d(epi.tmap(), box, ti.n0 + col, ti.m0 + q * 32);
+                  ptx::bulk_commit();  // a group per box, empty when out of bounds, so the wait counts boxes
+                }
+                done = true;
+              }
+            }
+            if (!done) epi.store(ti, row, col, ri);
           }
         }
-        epi.store(ti, row, half * BN2 + c, r);
       }
       epi.end_tile(ti, row);
       if constexpr (Epi::kNeedsTileDone) {
         // The last of this CTA's epilogue warps to finish publishes this CTA's 128 rows of
-        // the tile (ti.m0 is this CTA's first row); the accumulator goes back to the MMA
-        // warp only afterwards, so the next tile in it cannot start counting first.
+        // the tile (ti.m0 is this CTA's first row); the accumulator (its last half, with
+        // NH = 2) goes back to the MMA warp only afterwards, so the next tile in it cannot
+        // start counting first.
         Epi::fence_before_done();
         __syncwarp();
         if (lane == 0) {
@@ -450,12 +620,15 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
         }
         __syncwarp();
         ptx::tc_fence_before();
-        if (lane == 0) arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+        if (lane == 0) arrive_cluster(NH == 1 ? (acc ? tempty_leader1 : tempty_leader0) : tempty_leader1);
       }
       if (++acc == kAccs) {
         acc = 0;
         acc_phase ^= 1;
       }
+    }
+    if constexpr (kStaged) {
+      if (lane == 0) ptx::bulk_wait_all();  // staged stores complete before the CTA's memory goes
     }
   }
   ptx::tc_fence_before();

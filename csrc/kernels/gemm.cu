@@ -19,11 +19,30 @@ namespace gemm {
 struct StoreEpi {
   static constexpr bool kNeedsTileDone = false;
   static constexpr bool kPairHalves = false;
+  static constexpr bool kStagedStore = true;  // the CTA-pair core may store bf16 C through TMA
   void* C;
   long long ldc;
   int M, N;
   float alpha;
   int out_f32;
+  int vec = 1;                       // C's base and row pitch are multiples of 16 bytes
+  int use_tma = 0;                   // bf16 C stored as 32 x 32 boxes by TMA (tmC valid)
+  const CUtensorMap* tmC = nullptr;  // set by the kernel (a __grid_constant__ parameter)
+  __device__ bool staged() const { return use_tma != 0; }
+  __device__ const CUtensorMap* tmap() const { return tmC; }
+  // A box whose first row or column lies past C's edge is not stored (TMA clips the rest).
+  __device__ bool chunk_in_bounds(const TileInfo& ti, int row0, int c) const {
+    return ti.m0 + row0 < M && ti.n0 + c < N;
+  }
+  __device__ __forceinline__ void pack(const uint32_t* r, uint4* v) const {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[j].x = ptx::pack_bf16x2(alpha * __uint_as_float(r[8 * j + 0]), alpha * __uint_as_float(r[8 * j + 1]));
+      v[j].y = ptx::pack_bf16x2(alpha * __uint_as_float(r[8 * j + 2]), alpha * __uint_as_float(r[8 * j + 3]));
+      v[j].z = ptx::pack_bf16x2(alpha * __uint_as_float(r[8 * j + 4]), alpha * __uint_as_float(r[8 * j + 5]));
+      v[j].w = ptx::pack_bf16x2(alpha * __uint_as_float(r[8 * j + 6]), alpha * __uint_as_float(r[8 * j + 7]));
+    }
+  }
   __device__ static void fence_before_done() {}
   __device__ void tile_done(const TileInfo&) {}
   __device__ void begin_tile(const TileInfo&, int) {}
@@ -32,35 +51,51 @@ struct StoreEpi {
     const int gm = ti.m0 + row;
     if (gm >= M) return;
     const int gn = ti.n0 + c;
+    // 16-byte vector stores where C's base and row pitch allow them (vec) and the group lies
+    // inside C; element stores otherwise (unaligned views, the last N % 8 (bf16) or N % 4
+    // (f32) columns).
     if (out_f32) {
       float* p = static_cast<float*>(C) + (size_t)gm * ldc + gn;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        if (gn + 4 * j + 4 <= N) {
+        if (vec && gn + 4 * j + 4 <= N) {
           uint4 v;
           v.x = __float_as_uint(alpha * __uint_as_float(r[4 * j + 0]));
           v.y = __float_as_uint(alpha * __uint_as_float(r[4 * j + 1]));
           v.z = __float_as_uint(alpha * __uint_as_float(r[4 * j + 2]));
           v.w = __float_as_uint(alpha * __uint_as_float(r[4 * j + 3]));
           ptx::st_v4(p + 4 * j, v);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (gn + 4 * j + e < N) p[4 * j + e] = alpha * __uint_as_float(r[4 * j + e]);
         }
       }
     } else {
       uint16_t* p = static_cast<uint16_t*>(C) + (size_t)gm * ldc + gn;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        if (gn + 8 * j + 8 <= N) {
+        if (vec && gn + 8 * j + 8 <= N) {
           uint4 v;
           v.x = ptx::pack_bf16x2(alpha * __uint_as_float(r[8 * j + 0]), alpha * __uint_as_float(r[8 * j + 1]));
           v.y = ptx::pack_bf16x2(alpha * __uint_as_float(r[8 * j + 2]), alpha * __uint_as_float(r[8 * j + 3]));
           v.z = ptx::pack_bf16x2(alpha * __uint_as_float(r[8 * j + 4]), alpha * __uint_as_float(r[8 * j + 5]));
           v.w = ptx::pack_bf16x2(alpha * __uint_as_float(r[8 * j + 6]), alpha * __uint_as_float(r[8 * j + 7]));
           ptx::st_v4(p + 8 * j, v);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (gn + 8 * j + e < N) p[8 * j + e] = static_cast<uint16_t>(ptx::pack_bf16x2(alpha * __uint_as_float(r[8 * j + e]), 0.f) & 0xffffu);
         }
       }
     }
   }
 };
+
+// 16-byte vector (and TMA) stores of C need a 16-byte aligned base and row pitch.
+static bool c_vector_ok(const void* C, long long ldc, bool out_f32) {
+  return (reinterpret_cast<uintptr_t>(C) & 15) == 0 && ((ldc * (out_f32 ? 4 : 2)) & 15) == 0;
+}
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -94,6 +129,7 @@ static void launch_plain(const void* A, const void* B, void* C, int M, int N, in
   e.N = N;
   e.alpha = alpha;
   e.out_f32 = out_f32 ? 1 : 0;
+  e.vec = c_vector_ok(C, ldc, out_f32) ? 1 : 0;
   static bool attr_set[64] = {false};
   int dev = 0;
   GICC_CUDA(cudaGetDevice(&dev));
@@ -114,6 +150,7 @@ struct PairPlainSched {
   int M, N, K;
   int num_m, num_n, group_m;
   int cols;  // output columns per pair tile (NH * 256)
+  pair::PairLoadOpts lopt;
   static constexpr int kCommWarps = 0;
   __device__ int num_tiles() const { return num_m * num_n; }
   __device__ TileInfo tile(int t) const {
@@ -136,8 +173,10 @@ struct PairPlainSched {
 template <int NH>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::PairCfg<NH>::kThreads, 1)
     k_gemm_bf16_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     PairPlainSched sched, StoreEpi epi, ErrorRecord* err, uint64_t timeout_ns) {
-  pair::gemm_core_pair<NH>(&tmA, &tmB, sched, epi, err, timeout_ns, -1);
+                     const __grid_constant__ CUtensorMap tmC, PairPlainSched sched, StoreEpi epi, ErrorRecord* err,
+                     uint64_t timeout_ns) {
+  epi.tmC = &tmC;
+  pair::gemm_core_pair<NH>(&tmA, &tmB, sched, epi, err, timeout_ns, -1, sched.lopt);
 }
 
 template <int NH>
@@ -155,7 +194,10 @@ static void launch_pair(const void* A, const void* B, void* C, int M, int N, int
   s.cols = Cf::kCols;
   s.num_m = (M + 2 * BM - 1) / (2 * BM);
   s.num_n = (N + Cf::kCols - 1) / Cf::kCols;
-  s.group_m = ops::gemm_tuning().pair_group_m;
+  const ops::GemmTuning tune = ops::gemm_tuning();
+  s.group_m = tune.pair_group_m;
+  s.lopt.l2hint = tune.pair_l2_hint;
+  s.lopt.prefetch = tune.pair_prefetch;
   StoreEpi e;
   e.C = C;
   e.ldc = ldc;
@@ -163,18 +205,27 @@ static void launch_pair(const void* A, const void* B, void* C, int M, int N, int
   e.N = N;
   e.alpha = alpha;
   e.out_f32 = out_f32 ? 1 : 0;
+  e.vec = c_vector_ok(C, ldc, out_f32) ? 1 : 0;
+  // bf16 C whose base and row pitch suit TMA is stored in 32 x 32 boxes through shared
+  // memory (whole 128-byte lines to L2); otherwise each thread stores its row directly.
+  const bool tma_c = !out_f32 && tune.pair_tma_store != 0 && e.vec;
+  e.use_tma = tma_c ? 1 : 0;
+  const CUtensorMap tC = tma_c ? make_tmap_2d(C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, N, ldc, 32, 32,
+                                              CU_TENSOR_MAP_SWIZZLE_NONE)
+                               : tA;  // unused
   static bool attr_set[64] = {false};
   int dev = 0;
   GICC_CUDA(cudaGetDevice(&dev));
   if (!attr_set[dev]) {
-    GICC_CUDA(cudaFuncSetAttribute(k_gemm_bf16_pair<NH>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmemBytes));
+    GICC_CUDA(cudaFuncSetAttribute(k_gemm_bf16_pair<NH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   Cf::kSmemBytesStaged));
     attr_set[dev] = true;
   }
   const int pairs_max = num_sms(dev) / 2;
   const int tiles = s.num_m * s.num_n;
   const int grid = 2 * (tiles < pairs_max ? tiles : pairs_max);
-  k_gemm_bf16_pair<NH><<<grid, Cf::kThreads, Cf::kSmemBytes, stream>>>(tA, tB, s, e, device_error_record(),
-                                                                        default_timeout_ns());
+  k_gemm_bf16_pair<NH><<<grid, Cf::kThreads, Cf::kSmemBytesStaged, stream>>>(tA, tB, tC, s, e, device_error_record(),
+                                                                              default_timeout_ns());
   GICC_CUDA(cudaGetLastError());
 }
 
@@ -259,8 +310,12 @@ GemmTuning g_tuning;
 bool g_tuning_set = false;  // set_gemm_tuning() wins over the environment
 }
 void set_gemm_tuning(const GemmTuning& t) {
-  if (t.group_m < 1 || t.l2_hint < 0 || t.l2_hint > 2 || t.pair_group_m < 1)
-    throw std::runtime_error("gicc::set_gemm_tuning: group_m >= 1, l2_hint in 0..2, pair_group_m >= 1");
+  if (t.group_m < 1 || t.l2_hint < 0 || t.l2_hint > 2 || t.pair_group_m < 1 || t.pair_l2_hint < 0 ||
+      t.pair_l2_hint > 2 || t.pair_prefetch < 0 || t.pair_prefetch > 64 || t.pair_tma_store < 0 ||
+      t.pair_tma_store > 1)
+    throw std::runtime_error(
+        "gicc::set_gemm_tuning: group_m >= 1, l2_hint in 0..2, pair_group_m >= 1, pair_l2_hint in 0..2, "
+        "pair_prefetch in 0..64, pair_tma_store 0 or 1");
   g_tuning = t;
   g_tuning_set = true;
 }
@@ -270,6 +325,9 @@ GemmTuning gemm_tuning() {
     g_tuning.group_m = c.gemm_group_m;
     g_tuning.l2_hint = c.gemm_l2_hint;
     g_tuning.pair_group_m = c.gemm_pair_group_m;
+    g_tuning.pair_l2_hint = c.gemm_pair_l2_hint;
+    g_tuning.pair_prefetch = c.gemm_pair_prefetch;
+    g_tuning.pair_tma_store = c.gemm_pair_tma_store;
     g_tuning_set = true;
   }
   return g_tuning;
@@ -296,8 +354,7 @@ void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long 
   if (M <= 0 || N <= 0 || K <= 0) throw std::runtime_error("gicc::gemm_bf16: empty shape");
   if (K % 8 != 0 || lda % 8 != 0 || ldb % 8 != 0)
     throw std::runtime_error("gicc::gemm_bf16: K and leading dimensions of A/B must be multiples of 8 (16-byte TMA rows)");
-  if (out_f32 ? (N % 4 != 0 || ldc % 4 != 0) : (N % 8 != 0 || ldc % 8 != 0))
-    throw std::runtime_error("gicc::gemm_bf16: N/ldc must allow 16-byte vector stores");
+  if (ldc < N) throw std::runtime_error("gicc::gemm_bf16: ldc < N");
   if (bn == 0) bn = default_tile(M, N);
   switch (bn) {
     case 256: gemm::launch_plain<256>(A, B, C, M, N, K, lda, ldb, ldc, out_f32, alpha, stream); break;

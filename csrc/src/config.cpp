@@ -75,6 +75,9 @@ Config Config::from_env() {
   if (parse_u64("GICC_GEMM_GROUP_M", 1, 1024, &v)) c.gemm_group_m = (int)v;
   if (parse_u64("GICC_GEMM_L2_HINT", 0, 2, &v)) c.gemm_l2_hint = (int)v;
   if (parse_u64("GICC_GEMM_PAIR_GROUP_M", 1, 1024, &v)) c.gemm_pair_group_m = (int)v;
+  if (parse_u64("GICC_GEMM_PAIR_L2_HINT", 0, 2, &v)) c.gemm_pair_l2_hint = (int)v;
+  if (parse_u64("GICC_GEMM_PAIR_PREFETCH", 0, 64, &v)) c.gemm_pair_prefetch = (int)v;
+  if (parse_u64("GICC_GEMM_PAIR_TMA_STORE", 0, 1, &v)) c.gemm_pair_tma_store = (int)v;
   return c;
 }
 

@@ -20,12 +20,16 @@ def gemm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = None, alph
     return native().gemm(A, B, out, float(alpha), out_dtype == torch.float32, int(bn))
 
 
-def set_tuning(group_m: int = 16, l2_hint: int = 0, pair_group_m: int = 16) -> None:
+def set_tuning(group_m: int = 16, l2_hint: int = 0, pair_group_m: int = 16, pair_l2_hint: int = 0,
+               pair_prefetch: int = 0, pair_tma_store: int = 0) -> None:
     """Process-wide tuning of ``gemm`` (A/B experiments; the defaults are the measured
     configuration): m-blocks per raster group, L2 eviction hints on the operand loads
-    (0 none, 1 keep A / stream B, 2 keep B / stream A), and the CTA-pair kernel's raster
-    group (256-row m-blocks)."""
-    native().set_gemm_tuning(int(group_m), int(l2_hint), int(pair_group_m))
+    (0 none, 1 keep A / stream B, 2 keep B / stream A), the CTA-pair kernel's raster
+    group (256-row m-blocks), its L2 hints (same codes) and how many k-steps ahead its
+    producer prefetches the operands into L2 (0 = no prefetch), and whether it stores bf16 C
+    through shared memory and TMA (1) or from each thread's registers (0)."""
+    native().set_gemm_tuning(int(group_m), int(l2_hint), int(pair_group_m), int(pair_l2_hint), int(pair_prefetch),
+                             int(pair_tma_store))
 
 
 def tuning() -> dict:

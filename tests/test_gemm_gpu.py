@@ -71,6 +71,81 @@ def test_gemm_cta_pair_matches_fp32_reference(M, N, K, bn):
     assert err <= 1e-2 * ref.abs().max().item() + 1e-2, err
 
 
+@pytest.mark.parametrize("l2_hint,prefetch", [(1, 0), (2, 0), (0, 2), (0, 8), (1, 4)])
+def test_gemm_cta_pair_load_options(l2_hint, prefetch):
+    """The CTA-pair kernel's L2 eviction hints and L2 prefetch distance change only how the
+    operands are loaded: results equal the fp32 reference (prefetch past the last k-step of a
+    tile is skipped; 4352 x 1800 x 1000 has ragged edges and 16 k-steps per tile)."""
+    from opengda_b200.ops.gemm import gemm, check_errors, set_tuning, tuning
+    g = torch.Generator(device="cuda").manual_seed(l2_hint * 10 + prefetch)
+    A = torch.randn(4352, 1000, device="cuda", generator=g).to(torch.bfloat16)
+    B = torch.randn(1800, 1000, device="cuda", generator=g).to(torch.bfloat16)
+    base = tuning()
+    try:
+        set_tuning(**dict(base, pair_l2_hint=l2_hint, pair_prefetch=prefetch))
+        for bn in (512, 1024):
+            C = gemm(A, B, bn=bn)
+            torch.cuda.synchronize()
+            check_errors()
+            ref = _ref(A, B)
+            err = (C.float() - ref).abs().max().item()
+            assert err <= 1e-2 * ref.abs().max().item() + 1e-2, (bn, err)
+    finally:
+        set_tuning(**base)
+
+
+@pytest.mark.parametrize("N", [100, 264])
+@pytest.mark.parametrize("bn", [128, 256, 512, 1024])
+@pytest.mark.parametrize("out_f32", [False, True])
+def test_gemm_unaligned_out_and_ragged_n(N, bn, out_f32):
+    """C views whose base is not 16-byte aligned, and N not a multiple of the 16-byte vector
+    (8 bf16 / 4 f32 columns): every element of C is stored (element stores where vector
+    stores do not fit) and nothing outside it."""
+    from opengda_b200.ops.gemm import gemm, check_errors
+    M, K = 300, 136
+    g = torch.Generator(device="cuda").manual_seed(N + bn)
+    A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    B = torch.randn(N, K, device="cuda", generator=g).to(torch.bfloat16)
+    dt = torch.float32 if out_f32 else torch.bfloat16
+    ref = _ref(A, B, 0.5)
+    big = torch.full((M + 1, N + 8), 7.0, device="cuda", dtype=dt)
+    for off in (0, 3):
+        C = big[:M, off:off + N]
+        out = gemm(A, B, out=C, alpha=0.5, out_dtype=dt, bn=bn)
+        torch.cuda.synchronize()
+        check_errors()
+        err = (out.float() - ref).abs().max().item()
+        assert err <= 1e-2 * ref.abs().max().item() + 1e-2, (off, err)
+    assert (big[M] == 7.0).all() and (big[:M, N + 3:] == 7.0).all()
+
+
+@pytest.mark.parametrize("M,N,K", [(4352, 1800, 1000), (300, 520, 136), (256, 256, 64), (2048, 2048, 4096),
+                                   (300, 100, 136)])
+def test_gemm_cta_pair_tma_store(M, N, K):
+    """bf16 C stored by the pair kernels in 32 x 32 boxes through shared memory and TMA:
+    ragged M and N (partial boxes clipped, boxes past the edge skipped), alpha, and a C view
+    whose row pitch is not a multiple of 16 bytes (falls back to per-thread stores)."""
+    from opengda_b200.ops.gemm import gemm, check_errors, set_tuning, tuning
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    B = torch.randn(N, K, device="cuda", generator=g).to(torch.bfloat16)
+    ref = _ref(A, B, 0.5)
+    base = tuning()
+    try:
+        set_tuning(**dict(base, pair_tma_store=1))
+        for bn in (512, 1024):
+            big = torch.full((M + 1, N + 40), 7.0, device="cuda", dtype=torch.bfloat16)
+            for C in (big[:M, :N], big[:M, 3:N + 3]):  # 16-byte pitch; unaligned base -> fallback
+                out = gemm(A, B, out=C, alpha=0.5, bn=bn)
+                torch.cuda.synchronize()
+                check_errors()
+                err = (out.float() - ref).abs().max().item()
+                assert err <= 1e-2 * ref.abs().max().item() + 1e-2, (bn, err)
+            assert (big[M] == 7.0).all() and (big[:M, N + 3:] == 7.0).all()  # nothing stored past C
+    finally:
+        set_tuning(**base)
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("skew_ns", [0, 20000])
 def test_gemm_core_publishes_each_tile_once_after_all_epilogue_warps(skew_ns):
