@@ -99,7 +99,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     t.pair_tma_store = pair_tma_store;
     gicc::ops::set_gemm_tuning(t);
   }, py::arg("group_m") = 16, py::arg("l2_hint") = 0, py::arg("pair_group_m") = 16, py::arg("pair_l2_hint") = 0,
-     py::arg("pair_prefetch") = 0, py::arg("pair_tma_store") = 0);
+     py::arg("pair_prefetch") = 0, py::arg("pair_tma_store") = 1);
   m.def("gemm_tuning", []() {
     const auto t = gicc::ops::gemm_tuning();
     py::dict d;

@@ -30,7 +30,7 @@ struct GICC_EXPORT Config {
   int gemm_pair_group_m = 16;            // GICC_GEMM_PAIR_GROUP_M: the CTA-pair kernel's raster group [1, 1024]
   int gemm_pair_l2_hint = 0;             // GICC_GEMM_PAIR_L2_HINT: as GICC_GEMM_L2_HINT, for the CTA-pair kernel
   int gemm_pair_prefetch = 0;            // GICC_GEMM_PAIR_PREFETCH: L2 prefetch distance in k-steps [0, 64], 0 off
-  int gemm_pair_tma_store = 0;           // GICC_GEMM_PAIR_TMA_STORE: 1 = bf16 C through shared memory and TMA
+  int gemm_pair_tma_store = 1;           // GICC_GEMM_PAIR_TMA_STORE: 1 = bf16 C through shared memory and TMA, 0 = per thread
 
   // Parses the environment now; throws std::invalid_argument naming the bad variable.
   static Config from_env();

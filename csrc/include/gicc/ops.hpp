@@ -26,7 +26,7 @@ struct GemmTuning {
   int pair_group_m = 16;  // CTA-pair kernels (bn = 512, 1024): 256-row m-blocks per raster group
   int pair_l2_hint = 0;   // CTA-pair kernels: L2 eviction hints as l2_hint
   int pair_prefetch = 0;  // CTA-pair kernels: L2 prefetch of the operands this many k-steps ahead (0 off)
-  int pair_tma_store = 0; // CTA-pair kernels: bf16 C stored through shared memory and TMA (1) or per thread (0)
+  int pair_tma_store = 1; // CTA-pair kernels: bf16 C stored through shared memory and TMA (1) or per thread (0)
 };
 GICC_EXPORT void set_gemm_tuning(const GemmTuning& t);
 GICC_EXPORT GemmTuning gemm_tuning();

@@ -343,11 +343,28 @@ struct AgPairSched : AgSched {
 struct PlainStoreEpi {
   static constexpr bool kNeedsTileDone = false;
   static constexpr bool kPairHalves = false;
+  static constexpr bool kStagedStore = true;  // the CTA-pair core may store C through TMA
   uint16_t* C;
   long long ldc;
   int M, N;
   uint64_t* trace_epi;  // diagnostics: [tile] stamp when stored, or null
   int num_n, bn;
+  int use_tma = 0;                   // C stored as 32 x 32 boxes by TMA (tmC valid; pair kernels)
+  const CUtensorMap* tmC = nullptr;  // set by the kernel (a __grid_constant__ parameter)
+  __device__ bool staged() const { return use_tma != 0; }
+  __device__ const CUtensorMap* tmap() const { return tmC; }
+  __device__ bool chunk_in_bounds(const TileInfo& ti, int row0, int c) const {
+    return ti.m0 + row0 < M && ti.n0 + c < N;
+  }
+  __device__ __forceinline__ void pack(const uint32_t* r, uint4* v) const {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[j].x = ptx::pack_bf16x2(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
+      v[j].y = ptx::pack_bf16x2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
+      v[j].z = ptx::pack_bf16x2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
+      v[j].w = ptx::pack_bf16x2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
+    }
+  }
   __device__ static void fence_before_done() {}
   __device__ void tile_done(const TileInfo&) {}
   __device__ void begin_tile(const TileInfo&, int) {}
@@ -394,8 +411,9 @@ __global__ void __launch_bounds__(cta_threads(kCommWarpsAG), 1)
 template <int NH>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::PairCfg<NH>::threads(kCommWarpsAG), 1)
     k_ag_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   AgPairSched<NH> sched, PlainStoreEpi epi, DoneTable done_peer, ErrorRecord* err,
-                   uint64_t timeout_ns) {
+                   const __grid_constant__ CUtensorMap tmC, AgPairSched<NH> sched, PlainStoreEpi epi,
+                   DoneTable done_peer, ErrorRecord* err, uint64_t timeout_ns) {
+  epi.tmC = &tmC;
   pair::gemm_core_pair<NH>(&tmA, &tmB, sched, epi, err, timeout_ns, sched.r);
   signal_cta_done(done_peer.p, sched.n, sched.r);
 }
@@ -841,15 +859,21 @@ void launch_ag_pair(const AgGemmArgs& a, const gemm::AgSched& base, const gemm::
   sc.tile_base = (unsigned long long)(a.epoch - 1) * (unsigned long long)(a.n * sc.nb2 * sc.num_n + Gp / 2);
   PlainStoreEpi e = e0;
   e.trace_epi = nullptr;
+  // C in 32 x 32 boxes through shared memory and TMA (whole lines to L2), as the plain GEMM
+  e.use_tma = ops::gemm_tuning().pair_tma_store != 0 ? 1 : 0;
+  const CUtensorMap tC = e.use_tma ? make_tmap_2d(a.C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.Ns, a.ldc, 32, 32,
+                                                  CU_TENSOR_MAP_SWIZZLE_NONE)
+                                   : tA;  // unused
   static bool attr[2][64] = {};
   int dev = 0;
   GICC_CUDA(cudaGetDevice(&dev));
   if (!attr[NH - 1][dev]) {
-    GICC_CUDA(cudaFuncSetAttribute(k_ag_gemm_pair<NH>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmemBytes));
+    GICC_CUDA(cudaFuncSetAttribute(k_ag_gemm_pair<NH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   Cf::kSmemBytesStaged));
     attr[NH - 1][dev] = true;
   }
-  k_ag_gemm_pair<NH><<<Gp, Cf::threads(kCommWarpsAG), Cf::kSmemBytes, s>>>(
-      tA, tB, sc, e, dt, device_error_record(), a.timeout_ns ? a.timeout_ns : default_timeout_ns());
+  k_ag_gemm_pair<NH><<<Gp, Cf::threads(kCommWarpsAG), Cf::kSmemBytesStaged, s>>>(
+      tA, tB, tC, sc, e, dt, device_error_record(), a.timeout_ns ? a.timeout_ns : default_timeout_ns());
   GICC_CUDA(cudaGetLastError());
 }
 }  // namespace
@@ -904,6 +928,8 @@ void ag_gemm(const AgGemmArgs& a, cudaStream_t s) {
   if (a.n < 2 || a.n > kMaxR) throw std::runtime_error("gicc::ag_gemm: 2..16 ranks");
   if (a.M % (a.n * BM) || a.Ns % BN_ || a.K % BK)
     throw std::runtime_error("gicc::ag_gemm: need M % (ranks*128) == 0, N/ranks % 256 == 0, K % 64 == 0");
+  if ((reinterpret_cast<uintptr_t>(a.C) & 15) || (a.ldc % 8) || a.ldc < a.Ns)
+    throw std::runtime_error("gicc::ag_gemm: C needs a 16-byte aligned base and ldc % 8 == 0, ldc >= N/ranks");
   const int Ms = a.M / a.n, nb = Ms / BM;
   const int Q = a.units_per_band > 0 ? a.units_per_band : 4;
   if (((long long)BM * a.K * 2 / 16) % Q) throw std::runtime_error("gicc::ag_gemm: units_per_band must divide a band's 16-byte vectors");

@@ -21,7 +21,7 @@ def gemm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = None, alph
 
 
 def set_tuning(group_m: int = 16, l2_hint: int = 0, pair_group_m: int = 16, pair_l2_hint: int = 0,
-               pair_prefetch: int = 0, pair_tma_store: int = 0) -> None:
+               pair_prefetch: int = 0, pair_tma_store: int = 1) -> None:
     """Process-wide tuning of ``gemm`` (A/B experiments; the defaults are the measured
     configuration): m-blocks per raster group, L2 eviction hints on the operand loads
     (0 none, 1 keep A / stream B, 2 keep B / stream A), the CTA-pair kernel's raster

@@ -121,10 +121,11 @@ def test_gemm_unaligned_out_and_ragged_n(N, bn, out_f32):
 
 @pytest.mark.parametrize("M,N,K", [(4352, 1800, 1000), (300, 520, 136), (256, 256, 64), (2048, 2048, 4096),
                                    (300, 100, 136)])
-def test_gemm_cta_pair_tma_store(M, N, K):
-    """bf16 C stored by the pair kernels in 32 x 32 boxes through shared memory and TMA:
-    ragged M and N (partial boxes clipped, boxes past the edge skipped), alpha, and a C view
-    whose row pitch is not a multiple of 16 bytes (falls back to per-thread stores)."""
+@pytest.mark.parametrize("tma", [1, 0])
+def test_gemm_cta_pair_store_paths(M, N, K, tma):
+    """bf16 C stored by the pair kernels in 32 x 32 boxes through shared memory and TMA (the
+    default) or per thread: ragged M and N (partial boxes clipped, boxes past the edge
+    skipped), alpha, and a C view whose base is not 16-byte aligned (per-thread stores)."""
     from opengda_b200.ops.gemm import gemm, check_errors, set_tuning, tuning
     g = torch.Generator(device="cuda").manual_seed(M + N + K)
     A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
@@ -132,7 +133,7 @@ def test_gemm_cta_pair_tma_store(M, N, K):
     ref = _ref(A, B, 0.5)
     base = tuning()
     try:
-        set_tuning(**dict(base, pair_tma_store=1))
+        set_tuning(**dict(base, pair_tma_store=tma))
         for bn in (512, 1024):
             big = torch.full((M + 1, N + 40), 7.0, device="cuda", dtype=torch.bfloat16)
             for C in (big[:M, :N], big[:M, 3:N + 3]):  # 16-byte pitch; unaligned base -> fallback

@@ -6,10 +6,10 @@ from opengda_b200.ops.gemm import set_tuning, tuning
 
 def test_tuning_roundtrip_and_validation():
     default = {"group_m": 16, "l2_hint": 0, "pair_group_m": 16, "pair_l2_hint": 0, "pair_prefetch": 0,
-               "pair_tma_store": 0}
+               "pair_tma_store": 1}
     assert tuning() == default
     custom = {"group_m": 8, "l2_hint": 2, "pair_group_m": 4, "pair_l2_hint": 1, "pair_prefetch": 6,
-              "pair_tma_store": 1}
+              "pair_tma_store": 0}
     try:
         set_tuning(**custom)
         assert tuning() == custom
