@@ -195,11 +195,14 @@ def main() -> int:
 
     A_host = A.cpu().pin_memory()
     h2d = A_host.numel() * A_host.element_size()
-    feeder = HostFeeder(A.shape, A.dtype, dev)
 
     from opengda_b200.utils.timing import max_over_ranks
 
     def e2e_ms_of(fn):
+        # the fused AG model takes its input zero-copy: the host copy lands in its A slots
+        slots = fn.input_slots() if hasattr(fn, "input_slots") else None
+        feeder = HostFeeder(A.shape, A.dtype, dev, bufs=slots)
+
         def e2e_run(steps):
             # step i's pinned H2D copy is issued during step i-1 (double-buffered side
             # stream); every step ends with a 4-byte device->host read of its result checksum
@@ -251,7 +254,7 @@ def main() -> int:
         except (RuntimeError, torch.cuda.OutOfMemoryError) as exc:  # the comparison arm must not cost our line
             arm = {"impl": "nccl+cublas", "error": f"{type(exc).__name__}: {exc}"[:300]}
         torch.cuda.empty_cache()
-    del feeder, A_host
+    del A_host
     if rank == 0:
         out = {
             "metric": METRIC,

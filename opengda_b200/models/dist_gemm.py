@@ -238,6 +238,14 @@ class DistGemm:
             return self.A_bufs[p].local[self.rank * Ms:(self.rank + 1) * Ms]
         return self.A_full.local[self.rank * Ms:(self.rank + 1) * Ms]
 
+    def input_slots(self) -> Optional[list]:
+        """The A slots of this rank's next two calls, in call order, when the fused AG mode
+        double-buffers them (so a producer can fill call i+1's slot while call i runs);
+        None otherwise.  Valid while every call takes its A from these slots in turn."""
+        if not (self.fused and self.mode == "ag" and self.world > 1):
+            return None
+        return [self.a_slot((self.epoch + 1) % 2), self.a_slot((self.epoch + 2) % 2)]
+
     def _peer_ptrs(self, buf, parity: int):
         """Every rank's address of a symmetric buffer (fixed for the object's life; cached so
         a call does not rebuild the list)."""

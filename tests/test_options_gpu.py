@@ -141,7 +141,7 @@ def test_pending_options_multigpu(tmp_path):
     for r in res:
         assert r["ring_mm_err"] < 2e-5, r
         for k in ("ag_ce", "rs_join", "rs_group2", "ag_unicast", "rs_unicast", "ag_pair1", "ag_pair2",
-                  "ag_pair2_unicast", "rs_pair1", "rs_pair2"):
+                  "ag_pair2_unicast", "rs_pair1", "rs_pair2", "ag_feeder"):
             assert r[f"gemm_{k}_relerr"] < 1e-2, (k, r)
         assert r["moe_confined_relerr"] < 2e-2, r
         assert r["jacobi_persistent_mismatch"] == 0, r

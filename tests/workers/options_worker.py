@@ -2,7 +2,8 @@
 (launched by opengda_b200.parallel.launch; one JSON result per rank):
 
 * the ring-stripe fp32 matmul (RingMatmul) against an fp64 product of the full matrices;
-* the fused all-gather GEMM with the copy-engine transfer (transfer="ce");
+* the fused all-gather GEMM with the copy-engine transfer (transfer="ce"), and fed
+  zero-copy from pinned host memory through its input slots;
 * the reduce-scatter GEMM with the join option (rs_join);
 * the MoE layer with confined dispatch and the staged combine (dispatch_ctas, combine_ctas);
 * the persistent Jacobi kernel (one cooperative launch for many iterations);
@@ -72,6 +73,35 @@ def main():
             res[f"gemm_{name}_relerr"] = worst
     except Exception as e:  # record it and go on: the other steps still report
         res["step2_error"] = f"{type(e).__name__}: {e}"
+
+    # 2b. the fused AG GEMM fed zero-copy: pinned host copies land in the model's input slots
+    #     (HostFeeder over DistGemm.input_slots()), a different A every call
+    try:
+        from opengda_b200.models.dist_gemm import DistGemm, make_operands
+        from opengda_b200.utils.feeder import HostFeeder
+        M = Nn = 2048
+        K = 1024
+        model = DistGemm(M, Nn, K, "ag", rt=rt, fused=True)
+        model(*make_operands(M, Nn, K, "ag", n, r, seed=1)[:2])  # one plain call first: the slots rotate
+        ops = [make_operands(M, Nn, K, "ag", n, r, seed=30 + i) for i in range(5)]
+        hosts = [o[0].cpu().pin_memory() for o in ops]
+        feeder = HostFeeder(ops[0][0].shape, ops[0][0].dtype, torch.device("cuda"), bufs=model.input_slots())
+        worst = 0.0
+        feeder.submit(hosts[0])
+        for i in range(5):
+            if i + 1 < 5:
+                feeder.submit(hosts[i + 1])
+            a = feeder.next()
+            C = model(a, ops[i][1])
+            feeder.release()
+            Af, Bf = ops[i][2]
+            ref = (Af.float() @ Bf.float().t())[:, r * Nn // n:(r + 1) * Nn // n]
+            worst = max(worst, float(((C.float() - ref).norm() / ref.norm()).item()))
+        torch.cuda.synchronize()
+        rt.check_device_errors()
+        res["gemm_ag_feeder_relerr"] = worst
+    except Exception as e:  # record it and go on: the other steps still report
+        res["step2b_error"] = f"{type(e).__name__}: {e}"
 
     # 3. MoE with few dispatching CTAs and the staged combine
     try:
