@@ -326,6 +326,14 @@ __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensor
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
+    // TMEM columns read per tcgen05.wait::ld (each wait is a round trip): as many as the
+    // launch's registers allow (65536 per SM over cta_threads(kCommWarps), 1 CTA per SM)
+    constexpr int kRegs = 65536 / cta_threads(Sched::kCommWarps);
+    constexpr int kW0 = kRegs >= 240 ? 128 : (kRegs >= 160 ? 64 : 32);
+    constexpr int kW = kW0 < BN ? kW0 : BN;  // plain epilogues
+    constexpr int kWh0 = kW0 >= 64 ? kW0 / 2 : 32;
+    constexpr int kWh = kWh0 < BN / 2 ? kWh0 : BN / 2;  // per half, epilogues of column pairs
+    static_assert(BN % kW == 0 && (BN / 2) % kWh == 0 && kWh % 32 == 0, "TMEM read batches must tile the accumulator");
     int acc = 0;
     uint32_t acc_phase = 0;
     int tq_slot = 0;
@@ -359,33 +367,39 @@ __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensor
       if constexpr (Epi::kPairHalves) {
         // columns c and c + BN/2 together (e.g. gate | up halves of a SwiGLU tile)
 #pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 32) {
-          uint32_t lo[32], hi[32];
-          ptx::tmem_ld32(tbase + c, lo);
-          ptx::tmem_ld32(tbase + c + BN / 2, hi);
+        for (int c = 0; c < BN / 2; c += kWh) {
+          uint32_t lo[kWh], hi[kWh];
+#pragma unroll
+          for (int i = 0; i < kWh / 32; ++i) {
+            ptx::tmem_ld32(tbase + c + 32 * i, lo + 32 * i);
+            ptx::tmem_ld32(tbase + c + BN / 2 + 32 * i, hi + 32 * i);
+          }
           ptx::tmem_ld_wait();
           if constexpr (!Epi::kNeedsTileDone) {
-            if (c + 32 >= BN / 2) {
+            if (c + kWh >= BN / 2) {
               ptx::tc_fence_before();
               ptx::mbar_arrive(&tempty[acc]);
             }
           }
-          epi.store_pair(ti, row, c, lo, hi);
+#pragma unroll
+          for (int i = 0; i < kWh / 32; ++i) epi.store_pair(ti, row, c + 32 * i, lo + 32 * i, hi + 32 * i);
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t r[32];
-          ptx::tmem_ld32(tbase + c, r);
+        for (int c = 0; c < BN; c += kW) {
+          uint32_t r[kW];
+#pragma unroll
+          for (int i = 0; i < kW / 32; ++i) ptx::tmem_ld32(tbase + c + 32 * i, r + 32 * i);
           ptx::tmem_ld_wait();
           if constexpr (!Epi::kNeedsTileDone) {
-            if (c + 32 >= BN) {
+            if (c + kW >= BN) {
               // all TMEM reads of this accumulator are done: hand it back to the MMA warp
               ptx::tc_fence_before();
               ptx::mbar_arrive(&tempty[acc]);
             }
           }
-          epi.store(ti, row, c, r);
+#pragma unroll
+          for (int i = 0; i < kW / 32; ++i) epi.store(ti, row, c + 32 * i, r + 32 * i);
         }
       }
       epi.end_tile(ti, row);
