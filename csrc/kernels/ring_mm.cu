@@ -8,7 +8,9 @@
 //   arrival word, once that neighbour has reported finishing the step that last read the
 //   buffer;
 // * the other CTAs compute the column block C[:, b*Ns : (b+1)*Ns] = A_s . B_b with a
-//   register-tiled SIMT SGEMM (64 x 64 per CTA, fp32 in and out);
+//   register-tiled SIMT SGEMM, fp32 in and out: 128 x 128 per CTA (8 x 8 per thread,
+//   double-buffered shared memory, two CTAs per SM) when a step has at least 120 such
+//   tiles, else 64 x 64 (4 x 4 per thread) so that small stripes still fill the GPU;
 // * the last CTA to finish reports the step as consumed to the left neighbour.
 //
 // Every wait is bounded; a timeout records an error (where = W_RING_MM) and the CTA skips
@@ -79,6 +81,77 @@ __device__ void sgemm_tile(const ops::RingMmStep& a, int tile) {
         make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
 }
 
+// 128 x 128 tile: C[i0:i0+128, col0 + j0 : ... + 128] = A[i0:i0+128, :] . B[:, j0:j0+128].
+// Thread (ty, tx) of a 16 x 16 grid owns rows ty*4 + {0..3, 64..67} and columns tx*4 +
+// {0..3, 64..67}; a k-step is 8 deep.  A is stored k-major (transposed) with rows padded to
+// 132 floats, so the transposing stores of a warp fall in distinct banks; the next k-step's
+// operands are loaded into registers while the current one is multiplied.
+constexpr int kT2 = 128;
+constexpr int kK2 = 8;
+constexpr int kPadA = kT2 + 4;
+
+__device__ void sgemm_tile_128(const ops::RingMmStep& a, int tile) {
+  __shared__ __align__(16) float As[2][kK2][kPadA];
+  __shared__ __align__(16) float Bs[2][kK2][kT2];
+  const int tiles_n = a.Ns / kT2;
+  const int i0 = (tile / tiles_n) * kT2, j0 = (tile % tiles_n) * kT2;
+  const int t = threadIdx.x, ty = t / 16, tx = t % 16;
+  const int ar = t >> 1, ak = (t & 1) * 4;    // A: row, first k of this thread's float4
+  const int bk = t >> 5, bc = (t & 31) * 4;   // B: k row, first column
+  const float* pa = a.A + (size_t)(i0 + ar) * a.N + ak;
+  const float* pb = a.Bcur + (size_t)bk * a.Ns + j0 + bc;
+  float acc[8][8] = {};
+  float4 va = *reinterpret_cast<const float4*>(pa);
+  float4 vb = *reinterpret_cast<const float4*>(pb);
+  As[0][ak + 0][ar] = va.x;
+  As[0][ak + 1][ar] = va.y;
+  As[0][ak + 2][ar] = va.z;
+  As[0][ak + 3][ar] = va.w;
+  *reinterpret_cast<float4*>(&Bs[0][bk][bc]) = vb;
+  __syncthreads();
+  int cur = 0;
+  for (int k0 = 0; k0 < a.N; k0 += kK2) {
+    const bool more = k0 + kK2 < a.N;
+    if (more) {
+      va = *reinterpret_cast<const float4*>(pa + k0 + kK2);
+      vb = *reinterpret_cast<const float4*>(pb + (size_t)(k0 + kK2) * a.Ns);
+    }
+#pragma unroll
+    for (int k = 0; k < kK2; ++k) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[cur][k][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[cur][k][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[cur][k][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[cur][k][64 + tx * 4]);
+      const float x[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float y[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(x[i], y[j], acc[i][j]);
+    }
+    if (more) {
+      // the other buffer was last read before the previous barrier
+      As[cur ^ 1][ak + 0][ar] = va.x;
+      As[cur ^ 1][ak + 1][ar] = va.y;
+      As[cur ^ 1][ak + 2][ar] = va.z;
+      As[cur ^ 1][ak + 3][ar] = va.w;
+      *reinterpret_cast<float4*>(&Bs[cur ^ 1][bk][bc]) = vb;
+    }
+    __syncthreads();
+    cur ^= 1;
+  }
+  const size_t col = (size_t)a.col_block * a.Ns + j0 + tx * 4;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float* row = a.C + (size_t)(i0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4)) * a.N + col;
+    *reinterpret_cast<float4*>(row) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+    *reinterpret_cast<float4*>(row + 64) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+  }
+}
+
+// Output tile edge for a step of Ns x Ns: 128 when that gives at least 120 tiles.
+__host__ __device__ inline int ring_tile(int Ns) { return (Ns % kT2 == 0 && (Ns / kT2) * (Ns / kT2) >= 120) ? kT2 : kTile; }
+
 __device__ void push_stripe(const ops::RingMmStep& a) {
   const size_t nvec = (size_t)a.N * a.Ns / 4;
   const uint4* src = reinterpret_cast<const uint4*>(a.Bcur);
@@ -95,7 +168,8 @@ __device__ void push_stripe(const ops::RingMmStep& a) {
   for (; i < nvec; i += stride) dst[i] = src[i];
 }
 
-__global__ void __launch_bounds__(kThreads) k_ring_mm_step(ops::RingMmStep a, ErrorRecord* err) {
+template <int T>
+__global__ void __launch_bounds__(kThreads, 2) k_ring_mm_step(ops::RingMmStep a, ErrorRecord* err) {
   __shared__ int landed_s, free_s;
   if (threadIdx.x == 0) {
     landed_s = !a.arrivals || ring_wait(a.arrivals, a.arrivals_target, a, err, a.left);  // Bcur has landed
@@ -116,7 +190,8 @@ __global__ void __launch_bounds__(kThreads) k_ring_mm_step(ops::RingMmStep a, Er
       }
     }
   } else if (landed) {
-    sgemm_tile(a, (int)blockIdx.x - a.push_ctas);
+    if constexpr (T == kT2) sgemm_tile_128(a, (int)blockIdx.x - a.push_ctas);
+    else sgemm_tile(a, (int)blockIdx.x - a.push_ctas);
   }
   // Every thread of this CTA is done reading Bcur; the last CTA of the step tells the left
   // neighbour (the one that writes into this rank's landing buffers).
@@ -135,7 +210,10 @@ __global__ void __launch_bounds__(kThreads) k_ring_mm_step(ops::RingMmStep a, Er
 
 namespace ops {
 
-int ring_mm_grid(int Ns, int push_ctas) { return push_ctas + (Ns / kTile) * (Ns / kTile); }
+int ring_mm_grid(int Ns, int push_ctas) {
+  const int T = ring_tile(Ns);
+  return push_ctas + (Ns / T) * (Ns / T);
+}
 
 void ring_mm_step(const RingMmStep& a, cudaStream_t s) {
   NvtxRange nvtx("gicc::ops::ring_mm_step");
@@ -146,7 +224,10 @@ void ring_mm_step(const RingMmStep& a, cudaStream_t s) {
     throw std::runtime_error("gicc::ring_mm_step: a push needs arrivals_remote and push_ctas > 0");
   if (a.consumed_left && !a.ticket) throw std::runtime_error("gicc::ring_mm_step: consumed_left needs ticket");
   if (a.push_ctas < 0) throw std::runtime_error("gicc::ring_mm_step: push_ctas < 0");
-  k_ring_mm_step<<<ring_mm_grid(a.Ns, a.push_ctas), kThreads, 0, s>>>(a, device_error_record());
+  if (ring_tile(a.Ns) == kT2)
+    k_ring_mm_step<kT2><<<ring_mm_grid(a.Ns, a.push_ctas), kThreads, 0, s>>>(a, device_error_record());
+  else
+    k_ring_mm_step<kTile><<<ring_mm_grid(a.Ns, a.push_ctas), kThreads, 0, s>>>(a, device_error_record());
   GICC_CUDA(cudaGetLastError());
 }
 

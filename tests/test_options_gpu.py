@@ -13,11 +13,14 @@ pytestmark = [pytest.mark.gpu]
 WORKER = os.path.join(os.path.dirname(__file__), "workers", "options_worker.py")
 
 
-def test_ring_mm_single_gpu_matches_fp64():
+@pytest.mark.parametrize("N", [512, 1536])
+def test_ring_mm_single_gpu_matches_fp64(N):
+    """512: 64 x 64 SGEMM tiles; 1536: 128 x 128 tiles (144 tiles per step)."""
     import torch
+    from opengda_b200 import native
     from opengda_b200.models.ring_mm import RingMatmul, make_stripes
     from opengda_b200.ops.gemm import check_errors
-    N = 512
+    assert native().ring_mm_grid(N, 0) == ((N // 64) ** 2 if N == 512 else (N // 128) ** 2)
     mm = RingMatmul(N)
     for call in range(2):
         A_s, B_s, A, B = make_stripes(N, 1, 0, seed=call)
