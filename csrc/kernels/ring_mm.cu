@@ -82,8 +82,11 @@ __device__ void sgemm_tile(const ops::RingMmStep& a, int tile) {
 }
 
 // 128 x 128 tile: C[i0:i0+128, col0 + j0 : ... + 128] = A[i0:i0+128, :] . B[:, j0:j0+128].
-// Thread (ty, tx) of a 16 x 16 grid owns rows ty*4 + {0..3, 64..67} and columns tx*4 +
-// {0..3, 64..67}; a k-step is 8 deep.  A is stored k-major (transposed) with rows padded to
+// The 8 warps form a 4 x 2 grid of 32 x 64 warp tiles; lane (ty, tx) of a 4 x 8 lane grid
+// owns rows ty*4 + {0..3, 16..19} and columns tx*4 + {0..3, 32..35} of its warp tile, 8 x 8
+// in all.  So a warp's four 16-byte shared-memory reads per k touch 4 or 8 distinct vectors
+// (one wavefront each): 4 wavefronts per 2048 FMAs, which the shared-memory pipe sustains
+// at full FMA rate.  A k-step is 8 deep; A is stored k-major (transposed) with rows padded to
 // 132 floats, so the transposing stores of a warp fall in distinct banks; the next k-step's
 // operands are loaded into registers while the current one is multiplied.
 constexpr int kT2 = 128;
@@ -95,7 +98,9 @@ __device__ void sgemm_tile_128(const ops::RingMmStep& a, int tile) {
   __shared__ __align__(16) float Bs[2][kK2][kT2];
   const int tiles_n = a.Ns / kT2;
   const int i0 = (tile / tiles_n) * kT2, j0 = (tile % tiles_n) * kT2;
-  const int t = threadIdx.x, ty = t / 16, tx = t % 16;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int wr = (warp >> 1) * 32 + (lane >> 3) * 4;  // first row of this thread (and +16)
+  const int wc = (warp & 1) * 64 + (lane & 7) * 4;    // first column (and +32)
   const int ar = t >> 1, ak = (t & 1) * 4;    // A: row, first k of this thread's float4
   const int bk = t >> 5, bc = (t & 31) * 4;   // B: k row, first column
   const float* pa = a.A + (size_t)(i0 + ar) * a.N + ak;
@@ -118,10 +123,10 @@ __device__ void sgemm_tile_128(const ops::RingMmStep& a, int tile) {
     }
 #pragma unroll
     for (int k = 0; k < kK2; ++k) {
-      const float4 a0 = *reinterpret_cast<const float4*>(&As[cur][k][ty * 4]);
-      const float4 a1 = *reinterpret_cast<const float4*>(&As[cur][k][64 + ty * 4]);
-      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[cur][k][tx * 4]);
-      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[cur][k][64 + tx * 4]);
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[cur][k][wr]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[cur][k][wr + 16]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[cur][k][wc]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[cur][k][wc + 32]);
       const float x[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
       const float y[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
@@ -140,12 +145,12 @@ __device__ void sgemm_tile_128(const ops::RingMmStep& a, int tile) {
     __syncthreads();
     cur ^= 1;
   }
-  const size_t col = (size_t)a.col_block * a.Ns + j0 + tx * 4;
+  const size_t col = (size_t)a.col_block * a.Ns + j0 + wc;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    float* row = a.C + (size_t)(i0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4)) * a.N + col;
+    float* row = a.C + (size_t)(i0 + wr + (i < 4 ? i : 16 + i - 4)) * a.N + col;
     *reinterpret_cast<float4*>(row) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-    *reinterpret_cast<float4*>(row + 64) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+    *reinterpret_cast<float4*>(row + 32) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
   }
 }
 
