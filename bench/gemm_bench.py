@@ -13,7 +13,9 @@ which separates how well a kernel keeps the tensor cores busy from how fast the 
 cap lets it clock.  Tiles: 128 / 256 = one CTA per 128 x bn tile; 512 = CTA pairs,
 256 x 256; 1024 = CTA pairs, 256 x 512.  `--pair-opts` adds 256 x 512 variants with the
 pair kernel's options: `h<l2 hint>p<prefetch distance>[s<tma store>]` (`ops.gemm.set_tuning`'s
-pair_l2_hint, pair_prefetch and pair_tma_store).  Prints one JSON object.
+pair_l2_hint, pair_prefetch and pair_tma_store).  `--fp32` times the fp32 GEMM instead:
+cuBLAS SGEMM (tf32 off) against `ops.gemm.gemm_fp32` (three tf32 products on the tensor
+cores).  Prints one JSON object.
 """
 from __future__ import annotations
 
@@ -38,6 +40,8 @@ def main():
     ap.add_argument("--tiles", default="256,512,1024")
     ap.add_argument("--pair-group", type=int, default=0, help="raster group of the pair kernels (0 = default)")
     ap.add_argument("--pair-opts", default="", help="extra 256x512 variants: comma list of h<l2 hint>p<prefetch>")
+    ap.add_argument("--fp32", action="store_true",
+                    help="fp32 GEMM instead: cuBLAS SGEMM (tf32 off) against gemm_fp32 (three tf32 products)")
     ap.add_argument("--out", default=None)
     args = ap.parse_args()
     from opengda_b200 import native
@@ -49,17 +53,22 @@ def main():
         set_tuning(**dict(t, pair_group_m=args.pair_group))
     S = args.size
     g = torch.Generator(device="cuda").manual_seed(0)
-    A = torch.randn(S, S, device="cuda", generator=g).to(torch.bfloat16)
-    B = torch.randn(S, S, device="cuda", generator=g).to(torch.bfloat16)
-    C = torch.empty(S, S, device="cuda", dtype=torch.bfloat16)
+    dt = torch.float32 if args.fp32 else torch.bfloat16
+    A = torch.randn(S, S, device="cuda", generator=g).to(dt)
+    B = torch.randn(S, S, device="cuda", generator=g).to(dt)
+    C = torch.empty(S, S, device="cuda", dtype=dt)
+    torch.backends.cuda.matmul.allow_tf32 = False  # the cuBLAS arm is a true fp32 SGEMM
     ref = torch.matmul(A, B.t()).float()
     flop = 2.0 * S ** 3
     base = tuning()
     variants = {"cublas": lambda: torch.matmul(A, B.t(), out=C)}
     setups = {}
-    for bn in (int(x) for x in args.tiles.split(",")):
+    if args.fp32:
+        from opengda_b200.ops.gemm import gemm_fp32
+        variants["tc_fp32x3"] = lambda: gemm_fp32(A, B, out=C)
+    for bn in ([] if args.fp32 else (int(x) for x in args.tiles.split(","))):
         variants[f"tile{bn}"] = (lambda bn=bn: native().gemm(A, B, out=C, bn=bn))
-    for spec in (x for x in args.pair_opts.split(",") if x):
+    for spec in (x for x in args.pair_opts.split(",") if x and not args.fp32):
         m = re.fullmatch(r"h(\d)p(\d+)(?:s(\d))?", spec)
         if not m:
             raise SystemExit(f"--pair-opts: {spec!r} is not h<hint>p<prefetch>[s<tma store>]")

@@ -1,10 +1,11 @@
 """Ring-stripe fp32 matmul benchmark (the reference's distributed-matmul example,
 examples/gicc/mm.cu: N x N fp32, row stripes of A, column stripes of B moving around the
-ring; default N = 4096 as there): this framework's one-kernel-per-step ring (NVLink pushes
-inside the SGEMM kernel) against NCCL send/recv + cuBLAS fp32, both timed on the device as
-the max over ranks, with an fp64 CPU check of sampled elements of C.
+ring; default N = 4096 as there): this framework's ring (the step kernel pushes the stripe
+over NVLink while its other CTAs split it into tf32 parts for a tcgen05 GEMM, or run the
+fp32 SIMT SGEMM with --simt) against NCCL send/recv + cuBLAS fp32 SGEMM (tf32 off), both timed
+on the device as the max over ranks, with an fp64 CPU check of sampled elements of C.
 
-    python bench/ring_mm_bench.py [--size 4096]
+    python bench/ring_mm_bench.py [--size 4096] [--simt]
     torchrun --nproc-per-node N bench/ring_mm_bench.py
 """
 from __future__ import annotations
@@ -29,6 +30,7 @@ def main():
     ap.add_argument("--push-ctas", type=int, default=8)
     ap.add_argument("--samples", type=int, default=1000)
     ap.add_argument("--no-baseline", action="store_true")
+    ap.add_argument("--simt", action="store_true", help="the fp32 SIMT SGEMM step instead of the tf32 tensor-core one")
     ap.add_argument("--out", default=None)
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -45,7 +47,7 @@ def main():
     from opengda_b200.utils.timing import max_over_ranks
 
     N = args.n
-    mm = RingMatmul(N, rt=rt, push_ctas=args.push_ctas)
+    mm = RingMatmul(N, rt=rt, push_ctas=args.push_ctas, tensor_cores=False if args.simt else None)
     A_s, B_s, A, B = make_stripes(N, world, rank, seed=0)
 
     def timeit(fn):
@@ -83,7 +85,8 @@ def main():
         rt.check_device_errors()
     res = {"metric": "ring_mm_ms", "impl": "ours", "n_gpus": world, "N": N, "dtype": "fp32",
            "ms": ms, "tflops_total": mm.flops() / (ms * 1e-3) / 1e12, "max_rel_err_sampled": err,
-           "verified": bad == 0, "push_ctas": mm.push_ctas}
+           "verified": bad == 0, "push_ctas": mm.push_ctas,
+           "mode": "tensor cores (3 x tf32)" if mm.tensor_cores else "fp32 SIMT"}
     if not args.no_baseline and world > 1:
         from opengda_b200.baselines.ring_mm_nccl import NcclRingMatmul
         base = NcclRingMatmul(N)

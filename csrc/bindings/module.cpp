@@ -39,6 +39,27 @@ at::Tensor gemm(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tens
   return C;
 }
 
+at::Tensor gemm_fp32(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tensor> out, double alpha) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && A.scalar_type() == at::kFloat && B.scalar_type() == at::kFloat &&
+                  A.dim() == 2 && B.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1,
+              "A[M,K], B[N,K]: fp32 CUDA matrices with unit column stride");
+  TORCH_CHECK(A.size(1) == B.size(1), "A[M,K] and B[N,K] must share K");
+  const c10::cuda::CUDAGuard g(A.device());
+  const int64_t M = A.size(0), N = B.size(0), K = A.size(1);
+  at::Tensor C;
+  if (out.has_value()) {
+    C = *out;
+    TORCH_CHECK(C.is_cuda() && C.dim() == 2 && C.size(0) == M && C.size(1) == N && C.stride(1) == 1 &&
+                    C.scalar_type() == at::kFloat, "bad out");
+  } else {
+    C = at::empty({M, N}, A.options());
+  }
+  at::Tensor work = at::empty({(M + N) * 3 * K}, A.options());
+  gicc::ops::gemm_fp32(A.data_ptr<float>(), B.data_ptr<float>(), C.data_ptr<float>(), (int)M, (int)N, (int)K,
+                       A.stride(0), B.stride(0), C.stride(0), (float)alpha, work.data_ptr<float>(), cur_stream());
+  return C;
+}
+
 void gemm_tile_done_selftest(const at::Tensor& A, const at::Tensor& B, const at::Tensor& counters, int64_t skew_ns) {
   check_cuda_bf16(A, "A");
   check_cuda_bf16(B, "B");
@@ -113,6 +134,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   });
   m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("out") = py::none(), py::arg("alpha") = 1.0,
         py::arg("out_f32") = false, py::arg("bn") = 0, "C = alpha * A @ B^T with the tcgen05 GEMM");
+  m.def("gemm_fp32", &gemm_fp32, py::arg("A"), py::arg("B"), py::arg("out") = py::none(), py::arg("alpha") = 1.0,
+        "fp32 C = alpha * A @ B^T on the tensor cores (three tf32 products)");
   m.def("gemm_tile_done_selftest", &gemm_tile_done_selftest, py::arg("A"), py::arg("B"), py::arg("counters"),
         py::arg("skew_ns") = 20000, "run the GEMM core with an epilogue that checks the tile-done ordering");
   m.def("config", [] {

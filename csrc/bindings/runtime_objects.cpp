@@ -404,6 +404,10 @@ void bind_runtime_objects(py::module_& m) {
     ops::wait_count(P<const uint64_t>(counter), target, timeout_ns, rank, cur_stream());
   });
   m.def("ring_mm_grid", &ops::ring_mm_grid, py::arg("Ns"), py::arg("push_ctas"));
+  m.def("ring_mm_grid_tc", &ops::ring_mm_grid_tc, py::arg("push_ctas"));
+  m.def("tf32_split", [](uint64_t src, long long ld, int rows, int K, uint64_t dst, int order) {
+    ops::tf32_split(P<const float>(src), ld, rows, K, P<float>(dst), order, cur_stream());
+  }, py::arg("src"), py::arg("ld"), py::arg("rows"), py::arg("K"), py::arg("dst"), py::arg("order"));
   m.def("k_ring_mm_step", [](py::dict d) {
     ops::RingMmStep a;
     auto u64 = [&](const char* k) { return d.contains(k) ? d[k].cast<uint64_t>() : (uint64_t)0; };
@@ -427,6 +431,8 @@ void bind_runtime_objects(py::module_& m) {
     a.rank = d.contains("rank") ? d["rank"].cast<int>() : 0;
     a.left = d.contains("left") ? d["left"].cast<int>() : -1;
     a.right = d.contains("right") ? d["right"].cast<int>() : -1;
+    a.Asplit = P<const float>(u64("Asplit"));
+    a.Bsplit = P<float>(u64("Bsplit"));
     ops::ring_mm_step(a, cur_stream());
   });
   m.def("k_put_tile", [](uint64_t dst, int tiles, uint32_t tile_bytes, uint32_t seed, uint64_t sig) {

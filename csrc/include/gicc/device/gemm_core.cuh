@@ -129,6 +129,13 @@ struct PlainSched {
   __device__ void comm(int, int, volatile int*, ErrorRecord*, uint64_t) const {}
 };
 
+// Schedules with `static constexpr bool kTf32 = true` feed fp32 operands (128-byte swizzle
+// rows of 32 elements; their issue_loads use x = kb * 32) to kind::tf32 MMAs.
+template <class S, class = void>
+struct sched_tf32 : std::false_type {};
+template <class S>
+struct sched_tf32<S, std::void_t<decltype(S::kTf32)>> : std::integral_constant<bool, S::kTf32> {};
+
 template <int BN, class Sched, class Epi>
 __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensorMap* tmB, const Sched& sched,
                                           Epi& epi, ErrorRecord* err, uint64_t timeout_ns, int rank) {
@@ -248,7 +255,8 @@ __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensor
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = ptx::idesc_bf16_f32(BM, BN);
+      constexpr bool kTf32 = sched_tf32<Sched>::value;
+      constexpr uint32_t idesc = kTf32 ? ptx::idesc_tf32_f32(BM, BN) : ptx::idesc_bf16_f32(BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -293,7 +301,8 @@ __device__ __forceinline__ void gemm_core(const CUtensorMap* tmA, const CUtensor
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = ptx::sdesc_kmajor_sw128(a0 + k * 32);
             const uint64_t bd = ptx::sdesc_kmajor_sw128(b0 + k * 32);
-            ptx::mma_f16_ss(d, ad, bd, idesc, (kb > ti.kb0 || k > 0) ? 1u : 0u);
+            if constexpr (kTf32) ptx::mma_tf32_ss(d, ad, bd, idesc, (kb > ti.kb0 || k > 0) ? 1u : 0u);
+            else ptx::mma_f16_ss(d, ad, bd, idesc, (kb > ti.kb0 || k > 0) ? 1u : 0u);
           }
           issued = true;
           ptx::mma_commit(&empty[stage]);

@@ -17,6 +17,16 @@ namespace ops {
 // evenly as 128 x 256 tiles fill its SMs, else 256.
 GICC_EXPORT void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
                            long long ldc, bool out_f32, float alpha, int bn, cudaStream_t stream);
+// C[M,N] = alpha * A[M,K] * B[N,K]^T on kind::tf32 tensor cores (fp32 words, their tf32 part used).
+GICC_EXPORT void gemm_tf32(const float* A, const float* B, float* C, int M, int N, int K, long long lda, long long ldb,
+                           long long ldc, float alpha, cudaStream_t stream);
+// dst[rows][3K]: each src row split into its tf32 part hi and the rest lo = x - hi, laid out
+// (hi, hi, lo) for order 0 or (hi, lo, hi) for order 1.
+GICC_EXPORT void tf32_split(const float* src, long long ld, int rows, int K, float* dst, int order, cudaStream_t stream);
+// fp32 C = alpha * A * B^T on the tensor cores with three tf32 products (Ahi.Bhi + Ahi.Blo +
+// Alo.Bhi, one GEMM over 3K); work holds (M + N) * 3K floats.
+GICC_EXPORT void gemm_fp32(const float* A, const float* B, float* C, int M, int N, int K, long long lda, long long ldb,
+                           long long ldc, float alpha, float* work, cudaStream_t stream);
 // Process-wide tuning of gemm_bf16's 1-CTA kernel (A/B experiments; the defaults are the
 // measured configuration): m-blocks per raster group and the L2 eviction hints of the
 // operand loads (0 none, 1 keep A / stream B, 2 keep B / stream A).
@@ -113,10 +123,17 @@ struct RingMmStep {
   unsigned long long* ticket = nullptr;  // local count of finished CTAs (monotonic)
   unsigned long long ticket_target = 0;
   int push_ctas = 0;                     // CTAs that forward the stripe (kept for every step)
+  // Tensor-core mode (Bsplit non-null): the step kernel's other CTAs write Bcur^T as
+  // (hi, lo, hi) tf32 parts into Bsplit [Ns][3N], then a kind::tf32 GEMM with Asplit
+  // [Ns][3N] = (hi, hi, lo) of A_s (tf32_split order 0) writes the column block.
+  const float* Asplit = nullptr;
+  float* Bsplit = nullptr;
   uint64_t timeout_ns = 0;
   int rank = 0, left = -1, right = -1;
 };
 GICC_EXPORT int ring_mm_grid(int Ns, int push_ctas);
+// Grid of a tensor-core-mode step (push CTAs + splitting CTAs).
+GICC_EXPORT int ring_mm_grid_tc(int push_ctas);
 GICC_EXPORT void ring_mm_step(const RingMmStep& a, cudaStream_t s);
 
 // ---- Jacobi (jacobi.cu) ---------------------------------------------------------------------

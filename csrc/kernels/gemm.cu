@@ -3,6 +3,7 @@
 //   C[M,N] = alpha * A[M,K] * B[N,K]^T,  bf16 inputs, f32 accumulation, bf16 or f32 output.
 //
 // Host entry points: gicc::ops::gemm_bf16 (C++, throws) and gicc_gemm_bf16 (C ABI).
+#include <algorithm>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -266,9 +267,124 @@ __global__ void __launch_bounds__(kThreads, 1)
   gemm_core<256>(&tmA, &tmB, sched, epi, err, timeout_ns, -1);
 }
 
+// ---- fp32 GEMM on the tensor cores (3 x tf32) ----
+// x = hi + lo with hi = x rounded to tf32 (cvt.rna) and lo = x - hi (exact, |lo| <= 2^-11 |x|);
+// A.B^T = Ahi.Bhi^T + Ahi.Blo^T + Alo.Bhi^T + Alo.Blo^T, and the last term (below 2^-22 of
+// |A||B|) is dropped.  The three remaining products are one tf32 GEMM over K' = 3K of the
+// operands [Ahi | Ahi | Alo] and [Bhi | Blo | Bhi], accumulated in f32 in TMEM: the error is
+// about 2^-21 of |A||B| per product term (lo's own tf32 rounding in the MMA), against 2^-24
+// for fp32 FMA.
+
+// dst [rows][3K] = three K-long segments of src's rows: (hi, hi, lo) with order 0 or
+// (hi, lo, hi) with order 1.  src rows are 16-byte aligned (ld % 4 == 0), K % 4 == 0.
+__global__ void __launch_bounds__(256) k_tf32_split(const float* __restrict__ src, long long ld, int rows, int K,
+                                                    float* __restrict__ dst, int order) {
+  const int k4 = K / 4;
+  const size_t total = (size_t)rows * k4;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / k4), c = (int)(i - (size_t)r * k4) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(src + (size_t)r * ld + c);
+    float4 hi, lo;
+    hi.x = ptx::to_tf32(v.x);
+    hi.y = ptx::to_tf32(v.y);
+    hi.z = ptx::to_tf32(v.z);
+    hi.w = ptx::to_tf32(v.w);
+    lo.x = v.x - hi.x;
+    lo.y = v.y - hi.y;
+    lo.z = v.z - hi.z;
+    lo.w = v.w - hi.w;
+    float* d = dst + (size_t)r * 3 * K + c;
+    *reinterpret_cast<float4*>(d) = hi;
+    *reinterpret_cast<float4*>(d + K) = order == 0 ? hi : lo;
+    *reinterpret_cast<float4*>(d + 2 * K) = order == 0 ? lo : hi;
+  }
+}
+
+// The plain schedule over fp32 operands (32 elements per 128-byte k-block) for kind::tf32.
+struct PlainSchedTf32 : PlainSched {
+  static constexpr bool kTf32 = true;
+  __device__ TileInfo tile(int t) const {
+    TileInfo ti = PlainSched::tile(t);
+    ti.kb1 = (K + 31) / 32;
+    return ti;
+  }
+  __device__ void issue_loads(const TileInfo& ti, int kb, void* sA, void* sB, uint64_t* bar, const CUtensorMap* tmA,
+                              const CUtensorMap* tmB) const {
+    ptx::tma_load_2d(sA, tmA, bar, kb * 32, ti.a_row);
+    ptx::tma_load_2d(sB, tmB, bar, kb * 32, ti.b_row);
+  }
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_tf32(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, PlainSchedTf32 sched,
+                StoreEpi epi, ErrorRecord* err, uint64_t timeout_ns) {
+  gemm_core<256>(&tmA, &tmB, sched, epi, err, timeout_ns, -1);
+}
+
 }  // namespace gemm
 
 namespace ops {
+
+void tf32_split(const float* src, long long ld, int rows, int K, float* dst, int order, cudaStream_t stream) {
+  if (rows <= 0 || K <= 0 || K % 4 || ld % 4 || (reinterpret_cast<uintptr_t>(src) & 15) ||
+      (reinterpret_cast<uintptr_t>(dst) & 15) || order < 0 || order > 1)
+    throw std::runtime_error("gicc::tf32_split: K % 4 == 0, ld % 4 == 0, 16-byte aligned src and dst, order 0 or 1");
+  const size_t vecs = (size_t)rows * (K / 4);
+  const int grid = (int)std::min<size_t>((vecs + 255) / 256, (size_t)num_sms() * 8);
+  gemm::k_tf32_split<<<grid, 256, 0, stream>>>(src, ld, rows, K, dst, order);
+  GICC_CUDA(cudaGetLastError());
+}
+
+void gemm_tf32(const float* A, const float* B, float* C, int M, int N, int K, long long lda, long long ldb,
+               long long ldc, float alpha, cudaStream_t stream) {
+  NvtxRange nvtx("gicc::ops::gemm_tf32");
+  using namespace gemm;
+  using Cf = Cfg<256>;
+  if (M <= 0 || N <= 0 || K <= 0) throw std::runtime_error("gicc::gemm_tf32: empty shape");
+  if (lda % 4 || ldb % 4 || ldc < N || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
+    throw std::runtime_error("gicc::gemm_tf32: 16-byte aligned A/B rows (lda, ldb % 4 == 0), ldc >= N");
+  const CUtensorMap tA = make_tmap_2d(A, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, M, K, lda, BM, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tB = make_tmap_2d(B, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, K, ldb, 256, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  PlainSchedTf32 s;
+  s.M = M;
+  s.N = N;
+  s.K = K;
+  s.bn = 256;
+  s.num_m = (M + BM - 1) / BM;
+  s.num_n = (N + 255) / 256;
+  s.group_m = gemm_tuning().group_m;
+  s.l2hint = 0;
+  StoreEpi e;
+  e.C = C;
+  e.ldc = ldc;
+  e.M = M;
+  e.N = N;
+  e.alpha = alpha;
+  e.out_f32 = 1;
+  e.vec = c_vector_ok(C, ldc, true) ? 1 : 0;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  GICC_CUDA(cudaGetDevice(&dev));
+  if (!attr_set[dev]) {
+    GICC_CUDA(cudaFuncSetAttribute(k_gemm_tf32, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmemBytes));
+    attr_set[dev] = true;
+  }
+  const int tiles = s.num_m * s.num_n;
+  const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
+  k_gemm_tf32<<<grid, kThreads, Cf::kSmemBytes, stream>>>(tA, tB, s, e, device_error_record(), default_timeout_ns());
+  GICC_CUDA(cudaGetLastError());
+}
+
+void gemm_fp32(const float* A, const float* B, float* C, int M, int N, int K, long long lda, long long ldb,
+               long long ldc, float alpha, float* work, cudaStream_t stream) {
+  NvtxRange nvtx("gicc::ops::gemm_fp32");
+  if (K % 4) throw std::runtime_error("gicc::gemm_fp32: K % 4 == 0");
+  float* Ap = work;                          // [M][3K] = (hi, hi, lo)
+  float* Bp = work + (size_t)M * 3 * K;      // [N][3K] = (hi, lo, hi)
+  tf32_split(A, lda, M, K, Ap, 0, stream);
+  tf32_split(B, ldb, N, K, Bp, 1, stream);
+  gemm_tf32(Ap, Bp, C, M, N, 3 * K, 3LL * K, 3LL * K, ldc, alpha, stream);
+}
 
 void gemm_tile_done_selftest(const void* A, const void* B, int M, int N, int K, uint32_t* counters, uint32_t skew_ns,
                              cudaStream_t stream) {

@@ -11,6 +11,10 @@
 //   register-tiled SIMT SGEMM, fp32 in and out: 128 x 128 per CTA (8 x 8 per thread,
 //   double-buffered shared memory, two CTAs per SM) when a step has at least 120 such
 //   tiles, else 64 x 64 (4 x 4 per thread) so that small stripes still fill the GPU;
+// * or, in tensor-core mode (RingMmStep::Bsplit), the other CTAs write the stripe transposed
+//   as its tf32 parts (hi, lo, hi) and the step's column block is then one kind::tf32 GEMM
+//   over 3N with A_s's parts (hi, hi, lo): fp32 accuracy to about 2^-21 of |A||B| per term
+//   at tensor-core speed (ops::gemm_tf32, launched after the step kernel on its stream);
 // * the last CTA to finish reports the step as consumed to the left neighbour.
 //
 // Every wait is bounded; a timeout records an error (where = W_RING_MM) and the CTA skips
@@ -154,6 +158,31 @@ __device__ void sgemm_tile_128(const ops::RingMmStep& a, int tile) {
   }
 }
 
+// Tensor-core mode: Bcur [N][Ns] -> Bsplit [Ns][3N], row j = (hi, lo, hi) of Bcur's column
+// j, in 32 x 32 tiles through shared memory (loads and stores 128 bytes per warp row).
+constexpr int kSplitCtas = 128;
+
+__device__ void split_transpose(const ops::RingMmStep& a, int cta, int nctas) {
+  __shared__ float tile[32][33];
+  const int tiles_j = a.Ns / 32, tiles = (a.N / 32) * tiles_j;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const size_t N3 = 3 * (size_t)a.N;
+  for (int t = cta; t < tiles; t += nctas) {
+    const int k0 = (t / tiles_j) * 32, j0 = (t % tiles_j) * 32;
+    for (int r = ty; r < 32; r += kThreads / 32) tile[r][tx] = a.Bcur[(size_t)(k0 + r) * a.Ns + j0 + tx];
+    __syncthreads();
+    for (int r = ty; r < 32; r += kThreads / 32) {
+      const float x = tile[tx][r];
+      const float hi = ptx::to_tf32(x), lo = x - hi;
+      float* d = a.Bsplit + (size_t)(j0 + r) * N3 + k0 + tx;
+      d[0] = hi;
+      d[a.N] = lo;
+      d[2 * (size_t)a.N] = hi;
+    }
+    __syncthreads();
+  }
+}
+
 // Output tile edge for a step of Ns x Ns: 128 when that gives at least 120 tiles.
 __host__ __device__ inline int ring_tile(int Ns) { return (Ns % kT2 == 0 && (Ns / kT2) * (Ns / kT2) >= 120) ? kT2 : kTile; }
 
@@ -195,7 +224,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_ring_mm_step(ops::RingMmStep a,
       }
     }
   } else if (landed) {
-    if constexpr (T == kT2) sgemm_tile_128(a, (int)blockIdx.x - a.push_ctas);
+    if constexpr (T == 0) split_transpose(a, (int)blockIdx.x - a.push_ctas, (int)gridDim.x - a.push_ctas);
+    else if constexpr (T == kT2) sgemm_tile_128(a, (int)blockIdx.x - a.push_ctas);
     else sgemm_tile(a, (int)blockIdx.x - a.push_ctas);
   }
   // Every thread of this CTA is done reading Bcur; the last CTA of the step tells the left
@@ -215,6 +245,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_ring_mm_step(ops::RingMmStep a,
 
 namespace ops {
 
+int ring_mm_grid_tc(int push_ctas) { return push_ctas + kSplitCtas; }
+
 int ring_mm_grid(int Ns, int push_ctas) {
   const int T = ring_tile(Ns);
   return push_ctas + (Ns / T) * (Ns / T);
@@ -229,6 +261,16 @@ void ring_mm_step(const RingMmStep& a, cudaStream_t s) {
     throw std::runtime_error("gicc::ring_mm_step: a push needs arrivals_remote and push_ctas > 0");
   if (a.consumed_left && !a.ticket) throw std::runtime_error("gicc::ring_mm_step: consumed_left needs ticket");
   if (a.push_ctas < 0) throw std::runtime_error("gicc::ring_mm_step: push_ctas < 0");
+  if (a.Bsplit) {
+    if (!a.Asplit || a.N % 32 || a.Ns % 32 || (reinterpret_cast<uintptr_t>(a.Asplit) & 15) ||
+        (reinterpret_cast<uintptr_t>(a.Bsplit) & 15))
+      throw std::runtime_error("gicc::ring_mm_step: tensor-core mode needs Asplit, N % 32 == 0 and aligned buffers");
+    k_ring_mm_step<0><<<ring_mm_grid_tc(a.push_ctas), kThreads, 0, s>>>(a, device_error_record());
+    GICC_CUDA(cudaGetLastError());
+    const long long k3 = 3LL * a.N;
+    gemm_tf32(a.Asplit, a.Bsplit, a.C + (size_t)a.col_block * a.Ns, a.Ns, a.Ns, (int)k3, k3, k3, a.N, 1.0f, s);
+    return;
+  }
   if (ring_tile(a.Ns) == kT2)
     k_ring_mm_step<kT2><<<ring_mm_grid(a.Ns, a.push_ctas), kThreads, 0, s>>>(a, device_error_record());
   else

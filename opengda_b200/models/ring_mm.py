@@ -10,9 +10,13 @@ SGEMM); the landing buffers alternate, and a neighbour overwrites one only after
 that reads it reported the step that last read it.  Counters are monotonic across calls, so
 nothing is reset between calls.
 
-The bf16 tensor-core version of this workload at scale is ``DistGemm`` (all-gather fused
-into the GEMM); this one keeps the reference's fp32 data and ring structure and is checked
-against a CPU oracle.  ``opengda_b200.baselines.ring_mm_nccl`` runs the same ring with NCCL
+With ``tensor_cores=True`` (the default when N % 32 == 0) the step kernel's other CTAs write
+the held stripe transposed as its tf32 parts (hi, lo, hi) instead, and the column block is
+one kind::tf32 tcgen05 GEMM over 3N with A_s's parts (hi, hi, lo) (``ops.gemm.gemm_fp32``'s
+method: fp32 data, error about 2^-21 of |A||B| per term); ``tensor_cores=False`` keeps the
+fp32 SIMT SGEMM.  The bf16 tensor-core version of this workload at scale is ``DistGemm``
+(all-gather fused into the GEMM); this one keeps the reference's fp32 data and ring structure
+and is checked against a CPU oracle.  ``opengda_b200.baselines.ring_mm_nccl`` runs the same ring with NCCL
 send/recv and cuBLAS.
 """
 from __future__ import annotations
@@ -26,7 +30,8 @@ from ..utils.graphs import refuse_capture
 
 
 class RingMatmul:
-    def __init__(self, N: int, rt=None, push_ctas: int = 8, device: Optional[torch.device] = None):
+    def __init__(self, N: int, rt=None, push_ctas: int = 8, device: Optional[torch.device] = None,
+                 tensor_cores: Optional[bool] = None):
         self.rt = rt
         self.n = rt.size if rt is not None else 1
         self.r = rt.rank if rt is not None else 0
@@ -37,7 +42,16 @@ class RingMatmul:
             raise ValueError("need N / ranks % 64 == 0 and N % 16 == 0")
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.push_ctas = push_ctas if self.n > 1 else 0
-        self.grid = native().ring_mm_grid(self.Ns, self.push_ctas)
+        self.tensor_cores = (N % 32 == 0) if tensor_cores is None else bool(tensor_cores)
+        if self.tensor_cores:
+            if N % 32:
+                raise ValueError("tensor_cores needs N % 32 == 0")
+            # A_s's tf32 parts (hi, hi, lo) and two buffers for the held stripe's (hi, lo, hi)
+            self.a_split = torch.empty(self.Ns, 3 * N, dtype=torch.float32, device=self.device)
+            self.b_split = [torch.empty(self.Ns, 3 * N, dtype=torch.float32, device=self.device) for _ in range(2)]
+            self.grid = native().ring_mm_grid_tc(self.push_ctas)
+        else:
+            self.grid = native().ring_mm_grid(self.Ns, self.push_ctas)
         self.steps_done = 0  # this rank's steps over all calls
         self.calls = 0
         if self.n > 1:
@@ -46,7 +60,7 @@ class RingMatmul:
             w = rt.signal_alloc(2)  # [0] stripes arrived here (x push_ctas), [1] steps the right rank finished
             self.w_arrivals, self.w_consumed = w, w + 1
             self.ticket = torch.zeros(1, dtype=torch.int64, device=self.device)
-        self.launches_per_call = self.n
+        self.launches_per_call = self.n * (2 if self.tensor_cores else 1) + (1 if self.tensor_cores else 0)
 
     def forward(self, A_s: torch.Tensor, B_s: torch.Tensor, C_s: Optional[torch.Tensor] = None) -> torch.Tensor:
         """A_s [Ns, N] and B_s [N, Ns] fp32 (this rank's stripes) -> C_s [Ns, N] = A_s . B."""
@@ -59,10 +73,15 @@ class RingMatmul:
             C_s = torch.empty(Ns, N, dtype=torch.float32, device=self.device)
         self.calls += 1
         left, right = (r - 1) % n, (r + 1) % n
+        if self.tensor_cores:
+            native().tf32_split(A_s.data_ptr(), N, Ns, N, self.a_split.data_ptr(), 0)
         for s in range(n):
             p = ring_step_plan(n, r, self.calls, s, self.push_ctas, self.steps_done, self.grid)
             d = {"N": N, "Ns": Ns, "A": A_s.data_ptr(), "C": C_s.data_ptr(), "col_block": p["col_block"],
                  "push_ctas": self.push_ctas, "rank": r, "left": left, "right": right}
+            if self.tensor_cores:
+                d["Asplit"] = self.a_split.data_ptr()
+                d["Bsplit"] = self.b_split[s & 1].data_ptr()
             if n == 1:
                 d["Bcur"] = B_s.data_ptr()
             else:

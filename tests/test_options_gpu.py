@@ -14,14 +14,16 @@ WORKER = os.path.join(os.path.dirname(__file__), "workers", "options_worker.py")
 
 
 @pytest.mark.parametrize("N", [512, 1536])
-def test_ring_mm_single_gpu_matches_fp64(N):
-    """512: 64 x 64 SGEMM tiles; 1536: 128 x 128 tiles (144 tiles per step)."""
+@pytest.mark.parametrize("tensor_cores", [False, True])
+def test_ring_mm_single_gpu_matches_fp64(N, tensor_cores):
+    """SIMT mode: 64 x 64 SGEMM tiles at 512, 128 x 128 at 1536 (144 tiles per step);
+    tensor-core mode: the stripe split into tf32 parts and one kind::tf32 GEMM per step."""
     import torch
     from opengda_b200 import native
     from opengda_b200.models.ring_mm import RingMatmul, make_stripes
     from opengda_b200.ops.gemm import check_errors
     assert native().ring_mm_grid(N, 0) == ((N // 64) ** 2 if N == 512 else (N // 128) ** 2)
-    mm = RingMatmul(N)
+    mm = RingMatmul(N, tensor_cores=tensor_cores)
     for call in range(2):
         A_s, B_s, A, B = make_stripes(N, 1, 0, seed=call)
         C = mm(A_s, B_s)
@@ -142,7 +144,7 @@ def test_pending_options_multigpu(tmp_path):
     errors = {k: v for r in res for k, v in r.items() if k.endswith("_error")}
     assert not errors, errors
     for r in res:
-        assert r["ring_mm_err"] < 2e-5, r
+        assert r["ring_mm_err"] < 2e-5 and r["ring_mm_simt_err"] < 2e-5, r
         for k in ("ag_ce", "rs_join", "rs_group2", "ag_unicast", "rs_unicast", "ag_pair1", "ag_pair2",
                   "ag_pair2_unicast", "rs_pair1", "rs_pair2", "ag_feeder"):
             assert r[f"gemm_{k}_relerr"] < 1e-2, (k, r)

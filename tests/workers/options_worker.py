@@ -28,21 +28,23 @@ def main():
     r, n = rt.rank, rt.size
     res = {"rank": r}
 
-    # 1. ring-stripe fp32 matmul, three calls (monotonic counters across calls)
+    # 1. ring-stripe fp32 matmul, three calls (monotonic counters across calls), in the
+    #    tensor-core mode (default) and the SIMT mode
     try:
         from opengda_b200.models.ring_mm import RingMatmul, make_stripes
         N = 1024
-        mm = RingMatmul(N, rt=rt, push_ctas=4)
-        worst = 0.0
-        for call in range(3):
-            A_s, B_s, A, B = make_stripes(N, n, r, seed=call)
-            C = mm(A_s, B_s).cpu().double()
-            Ns = N // n
-            ref = A[r * Ns:(r + 1) * Ns].double() @ B.double()
-            scale = A[r * Ns:(r + 1) * Ns].double().abs() @ B.double().abs()
-            worst = max(worst, float(((C - ref).abs() / scale).max()))
-        rt.check_device_errors()
-        res["ring_mm_err"] = worst
+        for key, tc in (("ring_mm_err", True), ("ring_mm_simt_err", False)):
+            mm = RingMatmul(N, rt=rt, push_ctas=4, tensor_cores=tc)
+            worst = 0.0
+            for call in range(3):
+                A_s, B_s, A, B = make_stripes(N, n, r, seed=call)
+                C = mm(A_s, B_s).cpu().double()
+                Ns = N // n
+                ref = A[r * Ns:(r + 1) * Ns].double() @ B.double()
+                scale = A[r * Ns:(r + 1) * Ns].double().abs() @ B.double().abs()
+                worst = max(worst, float(((C - ref).abs() / scale).max()))
+            rt.check_device_errors()
+            res[key] = worst
     except Exception as e:  # record it and go on: the other steps still report
         res["step1_error"] = f"{type(e).__name__}: {e}"
 
