@@ -5,6 +5,8 @@ a few launches, a few GB on the device at most.
     python bench/profile_kernels.py gemm_pair 8192     # k_gemm_bf16_pair<1> (CTA pairs, 256 x 256), 4 launches
     python bench/profile_kernels.py gemm_pair_wide 8192  # k_gemm_bf16_pair<2> (CTA pairs, 256 x 512), 4 launches
     python bench/profile_kernels.py cublas 8192        # torch.matmul (cuBLAS) on the same operands, 4 launches
+    python bench/profile_kernels.py gemm_fp32 8192     # k_tf32_split x 2 + k_gemm_tf32 (fp32 on the tensor cores), 4 calls
+    python bench/profile_kernels.py sgemm 8192         # torch.matmul fp32 (cuBLAS SGEMM, tf32 off), 4 launches
     python bench/profile_kernels.py jacobi 8192 8192   # k_jacobi, 4 launches
     python bench/profile_kernels.py moe 1024           # MoE layer (n=1), 2 forwards
     python bench/profile_kernels.py copy 268435456     # k_copy (local HBM copy)
@@ -41,6 +43,18 @@ def main():
                 torch.matmul(A, B.t(), out=C)
             else:
                 gemm(A, B, out=C, bn=bn)
+    elif case in ("gemm_fp32", "sgemm"):
+        from opengda_b200.ops.gemm import gemm_fp32
+        torch.backends.cuda.matmul.allow_tf32 = False
+        M = N = K = args[0] if args else 8192
+        A = torch.randn(M, K, device="cuda")
+        B = torch.randn(N, K, device="cuda")
+        C = torch.empty(M, N, device="cuda")
+        for _ in range(4):
+            if case == "sgemm":
+                torch.matmul(A, B.t(), out=C)
+            else:
+                gemm_fp32(A, B, out=C)
     elif case == "jacobi":
         from opengda_b200.models.jacobi import Jacobi
         nx = args[0] if args else 8192
