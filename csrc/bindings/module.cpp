@@ -39,7 +39,8 @@ at::Tensor gemm(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tens
   return C;
 }
 
-at::Tensor gemm_fp32(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tensor> out, double alpha) {
+at::Tensor gemm_fp32(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tensor> out, double alpha,
+                     int64_t bn) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && A.scalar_type() == at::kFloat && B.scalar_type() == at::kFloat &&
                   A.dim() == 2 && B.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1,
               "A[M,K], B[N,K]: fp32 CUDA matrices with unit column stride");
@@ -56,7 +57,8 @@ at::Tensor gemm_fp32(const at::Tensor& A, const at::Tensor& B, c10::optional<at:
   }
   at::Tensor work = at::empty({(M + N) * 3 * K}, A.options());
   gicc::ops::gemm_fp32(A.data_ptr<float>(), B.data_ptr<float>(), C.data_ptr<float>(), (int)M, (int)N, (int)K,
-                       A.stride(0), B.stride(0), C.stride(0), (float)alpha, work.data_ptr<float>(), cur_stream());
+                       A.stride(0), B.stride(0), C.stride(0), (float)alpha, work.data_ptr<float>(), cur_stream(),
+                       (int)bn);
   return C;
 }
 
@@ -135,6 +137,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("out") = py::none(), py::arg("alpha") = 1.0,
         py::arg("out_f32") = false, py::arg("bn") = 0, "C = alpha * A @ B^T with the tcgen05 GEMM");
   m.def("gemm_fp32", &gemm_fp32, py::arg("A"), py::arg("B"), py::arg("out") = py::none(), py::arg("alpha") = 1.0,
+        py::arg("bn") = 0,
         "fp32 C = alpha * A @ B^T on the tensor cores (three tf32 products)");
   m.def("gemm_tile_done_selftest", &gemm_tile_done_selftest, py::arg("A"), py::arg("B"), py::arg("counters"),
         py::arg("skew_ns") = 20000, "run the GEMM core with an epilogue that checks the tile-done ordering");

@@ -111,6 +111,15 @@ __device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t a_desc, uint6
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+__device__ __forceinline__ void mma_pair_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void commit_pair(uint32_t bar_cluster_addr) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster_addr)
                : "memory");
@@ -204,6 +213,9 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
   constexpr int S = Cf::kStages;
   constexpr int kAccs = Cf::kAccs;
   constexpr bool kDyn = sched_dynamic<Sched>::value;
+  // kind::tf32 schedules (Sched::kTf32): fp32 operands, 32 elements per 128-byte k-block
+  constexpr bool kTf32 = sched_tf32<Sched>::value;
+  constexpr int kKE = kTf32 ? 32 : BK;  // elements per k-block (the TMA x step)
   constexpr int kFirstComm = 2 + Cf::kEpiWarps;  // first communication warp
   extern __shared__ uint8_t gemm2_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gemm2_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -337,20 +349,20 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
           if (leader) ptx::mbar_arrive_expect_tx(&full[stage], 2 * Cf::kStageBytes);
           const int a_y = ti.a_row + (int)crank * BM;
           if (lopt.l2hint == 0) {
-            tma_load_2d_pair(sA + stage * kABytes, tmA, bar, kb * BK, a_y);
+            tma_load_2d_pair(sA + stage * kABytes, tmA, bar, kb * kKE, a_y);
 #pragma unroll
             for (int h = 0; h < NH; ++h)
-              tma_load_2d_pair(sB + (stage * NH + h) * kBBytes, tmB, bar, kb * BK,
+              tma_load_2d_pair(sB + (stage * NH + h) * kBBytes, tmB, bar, kb * kKE,
                                ti.b_row + h * BN2 + (int)crank * (BN2 / 2));
           } else {
-            tma_load_2d_pair_hint(sA + stage * kABytes, tmA, bar, kb * BK, a_y, pol_a);
+            tma_load_2d_pair_hint(sA + stage * kABytes, tmA, bar, kb * kKE, a_y, pol_a);
 #pragma unroll
             for (int h = 0; h < NH; ++h)
-              tma_load_2d_pair_hint(sB + (stage * NH + h) * kBBytes, tmB, bar, kb * BK,
+              tma_load_2d_pair_hint(sB + (stage * NH + h) * kBBytes, tmB, bar, kb * kKE,
                                     ti.b_row + h * BN2 + (int)crank * (BN2 / 2), pol_b);
           }
           if (lopt.prefetch > 0 && kb + lopt.prefetch < ti.kb1) {
-            const int px = (kb + lopt.prefetch) * BK;
+            const int px = (kb + lopt.prefetch) * kKE;
             tma_prefetch_2d(tmA, px, a_y);
 #pragma unroll
             for (int h = 0; h < NH; ++h) tma_prefetch_2d(tmB, px, ti.b_row + h * BN2 + (int)crank * (BN2 / 2));
@@ -375,7 +387,7 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ---------------- MMA issuer (leader CTA) ----------------
-      constexpr uint32_t idesc = ptx::idesc_bf16_f32(2 * BM, BN2);
+      constexpr uint32_t idesc = kTf32 ? ptx::idesc_tf32_f32(2 * BM, BN2) : ptx::idesc_bf16_f32(2 * BM, BN2);
       const uint32_t peer = 1;
       int stage = 0;
       uint32_t phase = 0;
@@ -414,7 +426,8 @@ __device__ __forceinline__ void gemm_core_pair(const CUtensorMap* tmA, const CUt
             for (int h = 0; h < NH; ++h) {
               if (h < h0 || h >= h1) continue;
               const uint64_t bd = ptx::sdesc_kmajor_sw128(b0 + h * kBBytes + k * 32);
-              mma_pair(d + h * BN2, ad, bd, idesc, (kb > ti.kb0 || k > 0) ? 1u : 0u);
+              if constexpr (kTf32) mma_pair_tf32(d + h * BN2, ad, bd, idesc, (kb > ti.kb0 || k > 0) ? 1u : 0u);
+              else mma_pair(d + h * BN2, ad, bd, idesc, (kb > ti.kb0 || k > 0) ? 1u : 0u);
             }
           }
         };

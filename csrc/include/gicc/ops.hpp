@@ -17,16 +17,17 @@ namespace ops {
 // evenly as 128 x 256 tiles fill its SMs, else 256.
 GICC_EXPORT void gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
                            long long ldc, bool out_f32, float alpha, int bn, cudaStream_t stream);
-// C[M,N] = alpha * A[M,K] * B[N,K]^T on kind::tf32 tensor cores (fp32 words, their tf32 part used).
+// C[M,N] = alpha * A[M,K] * B[N,K]^T on kind::tf32 tensor cores (fp32 words, their tf32 part used);
+// bn as gemm_bf16's (256 one CTA, 512 / 1024 CTA pairs, 0 by shape).
 GICC_EXPORT void gemm_tf32(const float* A, const float* B, float* C, int M, int N, int K, long long lda, long long ldb,
-                           long long ldc, float alpha, cudaStream_t stream);
+                           long long ldc, float alpha, cudaStream_t stream, int bn = 0);
 // dst[rows][3K]: each src row split into its tf32 part hi and the rest lo = x - hi, laid out
 // (hi, hi, lo) for order 0 or (hi, lo, hi) for order 1.
 GICC_EXPORT void tf32_split(const float* src, long long ld, int rows, int K, float* dst, int order, cudaStream_t stream);
 // fp32 C = alpha * A * B^T on the tensor cores with three tf32 products (Ahi.Bhi + Ahi.Blo +
 // Alo.Bhi, one GEMM over 3K); work holds (M + N) * 3K floats.
 GICC_EXPORT void gemm_fp32(const float* A, const float* B, float* C, int M, int N, int K, long long lda, long long ldb,
-                           long long ldc, float alpha, float* work, cudaStream_t stream);
+                           long long ldc, float alpha, float* work, cudaStream_t stream, int bn = 0);
 // Process-wide tuning of gemm_bf16's 1-CTA kernel (A/B experiments; the defaults are the
 // measured configuration): m-blocks per raster group and the L2 eviction hints of the
 // operand loads (0 none, 1 keep A / stream B, 2 keep B / stream A).

@@ -315,6 +315,23 @@ struct PlainSchedTf32 : PlainSched {
   }
 };
 
+// The CTA-pair schedule over fp32 operands for kind::tf32.
+struct PairPlainSchedTf32 : PairPlainSched {
+  static constexpr bool kTf32 = true;
+  __device__ TileInfo tile(int t) const {
+    TileInfo ti = PairPlainSched::tile(t);
+    ti.kb1 = (K + 31) / 32;
+    return ti;
+  }
+};
+
+template <int NH>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::PairCfg<NH>::kThreads, 1)
+    k_gemm_tf32_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     PairPlainSchedTf32 sched, StoreEpi epi, ErrorRecord* err, uint64_t timeout_ns) {
+  pair::gemm_core_pair<NH>(&tmA, &tmB, sched, epi, err, timeout_ns, -1);
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tf32(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, PlainSchedTf32 sched,
                 StoreEpi epi, ErrorRecord* err, uint64_t timeout_ns) {
@@ -335,14 +352,64 @@ void tf32_split(const float* src, long long ld, int rows, int K, float* dst, int
   GICC_CUDA(cudaGetLastError());
 }
 
+static int default_tile(int M, int N);  // tile by shape (defined with gemm_bf16)
+
+namespace {
+template <int NH>
+void launch_tf32_pair(const float* A, const float* B, float* C, int M, int N, int K, long long lda, long long ldb,
+                      long long ldc, float alpha, cudaStream_t stream) {
+  using namespace gemm;
+  using Cf = pair::PairCfg<NH>;
+  const CUtensorMap tA = make_tmap_2d(A, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, M, K, lda, BM, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tB = make_tmap_2d(B, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, K, ldb, pair::BN2 / 2, 32,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  PairPlainSchedTf32 s;
+  s.M = M;
+  s.N = N;
+  s.K = K;
+  s.cols = Cf::kCols;
+  s.num_m = (M + 2 * BM - 1) / (2 * BM);
+  s.num_n = (N + Cf::kCols - 1) / Cf::kCols;
+  s.group_m = gemm_tuning().pair_group_m;
+  StoreEpi e;
+  e.C = C;
+  e.ldc = ldc;
+  e.M = M;
+  e.N = N;
+  e.alpha = alpha;
+  e.out_f32 = 1;
+  e.vec = c_vector_ok(C, ldc, true) ? 1 : 0;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  GICC_CUDA(cudaGetDevice(&dev));
+  if (!attr_set[dev]) {
+    GICC_CUDA(cudaFuncSetAttribute(k_gemm_tf32_pair<NH>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmemBytes));
+    attr_set[dev] = true;
+  }
+  const int pairs_max = num_sms(dev) / 2;
+  const int tiles = s.num_m * s.num_n;
+  const int grid = 2 * (tiles < pairs_max ? tiles : pairs_max);
+  k_gemm_tf32_pair<NH><<<grid, Cf::kThreads, Cf::kSmemBytes, stream>>>(tA, tB, s, e, device_error_record(),
+                                                                        default_timeout_ns());
+  GICC_CUDA(cudaGetLastError());
+}
+}  // namespace
+
 void gemm_tf32(const float* A, const float* B, float* C, int M, int N, int K, long long lda, long long ldb,
-               long long ldc, float alpha, cudaStream_t stream) {
+               long long ldc, float alpha, cudaStream_t stream, int bn) {
   NvtxRange nvtx("gicc::ops::gemm_tf32");
   using namespace gemm;
   using Cf = Cfg<256>;
   if (M <= 0 || N <= 0 || K <= 0) throw std::runtime_error("gicc::gemm_tf32: empty shape");
   if (lda % 4 || ldb % 4 || ldc < N || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
     throw std::runtime_error("gicc::gemm_tf32: 16-byte aligned A/B rows (lda, ldb % 4 == 0), ldc >= N");
+  if (bn == 0) bn = default_tile(M, N);
+  if (bn == 1024 || bn == 512) {
+    if (bn == 1024) launch_tf32_pair<2>(A, B, C, M, N, K, lda, ldb, ldc, alpha, stream);
+    else launch_tf32_pair<1>(A, B, C, M, N, K, lda, ldb, ldc, alpha, stream);
+    return;
+  }
+  if (bn != 256) throw std::runtime_error("gicc::gemm_tf32: bn must be 0, 256, 512 or 1024");
   const CUtensorMap tA = make_tmap_2d(A, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, M, K, lda, BM, 32, CU_TENSOR_MAP_SWIZZLE_128B);
   const CUtensorMap tB = make_tmap_2d(B, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, K, ldb, 256, 32, CU_TENSOR_MAP_SWIZZLE_128B);
   PlainSchedTf32 s;
@@ -376,14 +443,14 @@ void gemm_tf32(const float* A, const float* B, float* C, int M, int N, int K, lo
 }
 
 void gemm_fp32(const float* A, const float* B, float* C, int M, int N, int K, long long lda, long long ldb,
-               long long ldc, float alpha, float* work, cudaStream_t stream) {
+               long long ldc, float alpha, float* work, cudaStream_t stream, int bn) {
   NvtxRange nvtx("gicc::ops::gemm_fp32");
   if (K % 4) throw std::runtime_error("gicc::gemm_fp32: K % 4 == 0");
   float* Ap = work;                          // [M][3K] = (hi, hi, lo)
   float* Bp = work + (size_t)M * 3 * K;      // [N][3K] = (hi, lo, hi)
   tf32_split(A, lda, M, K, Ap, 0, stream);
   tf32_split(B, ldb, N, K, Bp, 1, stream);
-  gemm_tf32(Ap, Bp, C, M, N, 3 * K, 3LL * K, 3LL * K, ldc, alpha, stream);
+  gemm_tf32(Ap, Bp, C, M, N, 3 * K, 3LL * K, 3LL * K, ldc, alpha, stream, bn);
 }
 
 void gemm_tile_done_selftest(const void* A, const void* B, int M, int N, int K, uint32_t* counters, uint32_t skew_ns,

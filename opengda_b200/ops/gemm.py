@@ -20,15 +20,17 @@ def gemm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = None, alph
     return native().gemm(A, B, out, float(alpha), out_dtype == torch.float32, int(bn))
 
 
-def gemm_fp32(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = None, alpha: float = 1.0) -> torch.Tensor:
+def gemm_fp32(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = None, alpha: float = 1.0,
+              bn: int = 0) -> torch.Tensor:
     """fp32 C = alpha * A @ B^T on the tcgen05 tensor cores (csrc/kernels/gemm.cu, gemm_fp32).
 
     A [M, K] and B [N, K] fp32 (K % 4 == 0, rows 16-byte aligned).  Each operand is split
     into its tf32 part and the remainder, and the three products hi.hi + hi.lo + lo.hi run
     as one kind::tf32 GEMM over 3K with f32 accumulation: the error stays within a few
     2^-21 of |A||B| per term (fp32 FMA: 2^-24), at tensor-core rather than CUDA-core speed.
-    Uses (M + N) * 3K floats of workspace."""
-    return native().gemm_fp32(A, B, out, float(alpha))
+    Uses (M + N) * 3K floats of workspace.  ``bn`` picks the tile as in ``gemm`` (256 one CTA,
+    512 / 1024 CTA pairs with 256 x 256 / 256 x 512 tiles, 0 by shape)."""
+    return native().gemm_fp32(A, B, out, float(alpha), int(bn))
 
 
 def set_tuning(group_m: int = 16, l2_hint: int = 0, pair_group_m: int = 16, pair_l2_hint: int = 0,

@@ -95,15 +95,17 @@ def test_gemm_cta_pair_load_options(l2_hint, prefetch):
 
 
 @pytest.mark.parametrize("M,N,K", [(256, 256, 128), (300, 520, 200), (1000, 264, 516), (2048, 2048, 4096)])
-def test_gemm_fp32_on_tensor_cores_matches_fp64(M, N, K):
-    """fp32 GEMM from three tf32 products on the tensor cores, against an fp64 product:
-    the error per element stays below 1e-5 of sum |A||B| (fp32 FMA itself is near 6e-8 per
-    term); ragged M, N and K' = 3K not a multiple of the 32-element k-block included."""
+@pytest.mark.parametrize("bn", [256, 512, 1024])
+def test_gemm_fp32_on_tensor_cores_matches_fp64(M, N, K, bn):
+    """fp32 GEMM from three tf32 products on the tensor cores (one CTA, or CTA pairs with
+    256 x 256 / 256 x 512 tiles), against an fp64 product: the error per element stays below
+    1e-5 of sum |A||B| (fp32 FMA itself is near 6e-8 per term); ragged M, N and K' = 3K not a
+    multiple of the 32-element k-block included."""
     from opengda_b200.ops.gemm import gemm_fp32, check_errors
     g = torch.Generator(device="cuda").manual_seed(M + N + K)
     A = torch.randn(M, K, device="cuda", generator=g)
     B = torch.randn(N, K, device="cuda", generator=g)
-    C = gemm_fp32(A, B, alpha=0.5)
+    C = gemm_fp32(A, B, alpha=0.5, bn=bn)
     torch.cuda.synchronize()
     check_errors()
     ref = 0.5 * (A.double() @ B.double().t())
