@@ -5,7 +5,8 @@
 //     own 128 rows of B (no multicast: every load reads this GPU's memory); both CTAs'
 //     loads complete on the leader CTA's "full" mbarrier (cta_group::2 form of
 //     cp.async.bulk.tensor);
-//   * one thread of the leader issues tcgen05.mma.cta_group::2 (M=256, N=256, K=16) NH
+//   * one thread of the leader issues tcgen05.mma.cta_group::2 (M=256, N=256, K=16 of
+//     bf16, or K=8 of tf32 for schedules with kTf32: the same 32 bytes of a 128-byte row) NH
 //     times per k-step (the A tile is shared by the NH halves), which reads both CTAs'
 //     shared memory and accumulates into both CTAs' TMEM (each CTA holds its 128 rows x
 //     NH*256 columns);
@@ -17,6 +18,9 @@
 //     kStages - 1 k-steps, and issues the lagging half-1 MMAs of those k-steps once the
 //     epilogue has drained half 1 (the stages are released only then), so most of the
 //     drain overlaps tensor work;
+//   * the epilogue reads TMEM in batches of up to 128 columns per tcgen05.wait::ld (as the
+//     launch's registers allow) and, for epilogues with kStagedStore, writes bf16 C through
+//     two 2 KB shared-memory boxes per warp to TMA stores (whole lines to L2);
 //   * the leader's tcgen05.commit arrives on the barrier of each CTA (two commits, no
 //     multicast form), and the peer CTA's epilogue warps arrive on the leader's
 //     "accumulator free" barrier remotely.
